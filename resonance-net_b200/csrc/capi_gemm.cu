@@ -1,0 +1,25 @@
+// C-ABI entry of the GEMM engine (used by parity tests and by callers that
+// want the engine directly).
+#include "gemm.cuh"
+#include "status.h"
+
+extern "C" int rnet_gemm_f32(int M, int N, int K, const float* A, int lda, int a_mn_major,
+                             const float* B, int ldb, int b_mn_major, float* C, int ldc,
+                             const float* R, int ldr, int op, float alpha, void* stream) {
+  using namespace rnet_gemm;
+  if (op < 0 || op > 2) return rnet_status::fail(RNET_ERR_ARG, "rnet_gemm_f32: bad op");
+  if (op == 2 && R == nullptr) return rnet_status::fail(RNET_ERR_ARG, "rnet_gemm_f32: null R");
+  Operand a{A, lda, a_mn_major != 0};
+  Operand b{B, ldb, b_mn_major != 0};
+  Epilogue e;
+  e.kind = op == 0 ? EPI_STORE : (op == 1 ? EPI_ACCUM : EPI_RESID);
+  e.alpha = alpha;
+  e.C = C;
+  e.ldc = ldc;
+  e.R = R;
+  e.ldr = ldr;
+  cudaError_t err = gemm_tf32x3((cudaStream_t)stream, M, N, K, a, b, e, 0, 0,
+                                rnet_status::device_error_word());
+  if (err != cudaSuccess) return rnet_status::fail_cuda(err, "rnet_gemm_f32");
+  return RNET_OK;
+}

@@ -1,0 +1,59 @@
+// Host-side interface of the tcgen05 GEMM engine (3xTF32 split, fp32 in/out).
+//
+//   C[M,N] (epilogue)= A[M,K] * B[N,K]^T
+//
+// Each operand is either K-major (element (i,k) at p[i*ld + k]) or MN-major
+// (element (i,k) at p[k*ld + i]); both are consumed natively by TMA + UMMA
+// (kind::tf32 supports MN-major operands on sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace rnet_gemm {
+
+struct Operand {
+  const float* p = nullptr;
+  int ld = 0;            // elements between consecutive stored rows
+  bool mn_major = false; // see header comment
+};
+
+enum EpiKind : int {
+  EPI_STORE = 0,       // C = alpha*acc
+  EPI_ACCUM = 1,       // C += alpha*acc        (vector red.add; split-K safe)
+  EPI_RESID = 2,       // C = R + alpha*acc
+  EPI_SWIGLU_FWD = 3,  // paired B: G = acc[gate], U = acc[up], H = silu(G)*U
+  EPI_SWIGLU_BWD = 4,  // acc = dH; DGU[:, f] = dG, DGU[:, F+f] = dU
+  EPI_TOP2 = 5,        // row-owner: running top-2 over N, softmax, idx/w (+optional C)
+};
+
+struct Epilogue {
+  int kind = EPI_STORE;
+  float alpha = 1.0f;
+  float* C = nullptr;
+  int ldc = 0;
+  const float* R = nullptr;  // residual (EPI_RESID)
+  int ldr = 0;
+  // SwiGLU: gate/up caches and hidden output, all [M, ldf]
+  float* G = nullptr;
+  float* U = nullptr;
+  float* H = nullptr;
+  const float* Gc = nullptr;
+  const float* Uc = nullptr;
+  int ldf = 0;
+  // top-2
+  int* topk_idx = nullptr;
+  float* topk_w = nullptr;
+};
+
+// Launch. `b_pair_off` > 0 makes every B tile two halves of BN/2 rows taken at
+// logical rows n0 and n0 + b_pair_off (used to pair gate/up weights so one
+// accumulator tile holds both). `k_splits` = 0 picks automatically (only
+// EPI_ACCUM may split K). Returns cudaSuccess or the launch error.
+cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand& A,
+                        const Operand& B, const Epilogue& epi, int b_pair_off = 0,
+                        int k_splits = 0, unsigned* err_word = nullptr);
+
+// Number of SMs of the current device (cached).
+int num_sms();
+
+}  // namespace rnet_gemm

@@ -1,0 +1,556 @@
+// Persistent warp-specialised tcgen05 GEMM for sm_100a with 3xTF32 error
+// compensation, so fp32 operands give fp32-class results on the tensor cores.
+//
+// Every fp32 operand x is split into hi = rna_tf32(x) and lo = x - hi inside
+// shared memory; each 8-deep K slice issues three kind::tf32 UMMAs
+// (hi*lo, lo*hi, hi*hi) into one fp32 TMEM accumulator. The hi*hi product is
+// exact in fp32 terms; the dropped lo*lo term is ~2^-22 relative.
+//
+// Roles (448 threads = 14 warps):
+//   warps 0-3  epilogue (warp w owns TMEM lanes 32w..32w+31 = tile rows)
+//   warp  4    TMA producer (raw fp32 tiles, SWIZZLE_128B)
+//   warp  5    TMEM allocator + single-thread UMMA issuer
+//   warps 6-13 split warps (raw -> hi in place, lo into the twin buffer)
+// Pipelines: full[s] (TMA tx) -> split[s] (8 warp arrivals) -> empty[s]
+// (tcgen05.commit); accumulators double-buffered in TMEM with accf/acce.
+//
+// Reference parity: replaces every cublasSgemm call of the reference
+// (src/min_gru.cu:64-178, src/causal_conv.cu:76-165, src/slot_memory.cu:91-235,
+// src/swiglu_ffn.cu:32-143, src/embedding.cu:61, src/resonance_net.cpp:428-437).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace rnet_gemm {
+using namespace rnet_dev;
+
+constexpr int BM = 128;
+constexpr int BK = 32;  // fp32 elements = 128 B = one SWIZZLE_128B row
+constexpr int NUM_EPI_WARPS = 4;
+constexpr int PRODUCER_WARP = 4;
+constexpr int MMA_WARP = 5;
+constexpr int FIRST_SPLIT_WARP = 6;
+constexpr int NUM_SPLIT_WARPS = 8;
+constexpr int NUM_THREADS = 32 * (FIRST_SPLIT_WARP + NUM_SPLIT_WARPS);
+
+struct KParams {
+  int M, N, K;
+  int m_tiles, n_tiles, k_splits, kb_total, kb_per_split;
+  int num_units;
+  int row_owner;   // 1: a unit is one m-tile swept over all n-tiles
+  int b_pair_off;  // rows
+  int a_mn, b_mn;
+  Epilogue epi;
+  unsigned* err;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int RAW_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = 2 * RAW_BYTES;  // raw(hi) + lo
+  static constexpr int STAGES = (BN == 256) ? 2 : 3;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+__device__ __forceinline__ void unit_range(const KParams& p, int unit, int& mt, int& nt0,
+                                           int& nt1, int& kb0, int& kb1) {
+  if (p.row_owner) {
+    mt = unit;
+    nt0 = 0;
+    nt1 = p.n_tiles;
+    kb0 = 0;
+    kb1 = p.kb_total;
+  } else {
+    const int nt = unit % p.n_tiles;
+    const int rest = unit / p.n_tiles;
+    const int ks = rest % p.k_splits;
+    mt = rest / p.k_splits;
+    nt0 = nt;
+    nt1 = nt + 1;
+    kb0 = ks * p.kb_per_split;
+    kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+  }
+}
+
+__device__ __forceinline__ float silu_fast(float g) { return g / (1.0f + __expf(-g)); }
+
+// ------------------------------------------------------------------ epilogue
+template <int BN>
+__device__ __forceinline__ void store_row_chunk(const KParams& p, int row, int col0,
+                                                const float (&v)[32]) {
+  const Epilogue& e = p.epi;
+  if (row >= p.M) return;
+  const float a = e.alpha;
+  if (col0 + 32 <= p.N) {
+    if (e.kind == EPI_STORE) {
+      float4* dst = reinterpret_cast<float4*>(e.C + (size_t)row * e.ldc + col0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        dst[j] = make_float4(a * v[4 * j], a * v[4 * j + 1], a * v[4 * j + 2], a * v[4 * j + 3]);
+    } else if (e.kind == EPI_ACCUM) {
+      float* dst = e.C + (size_t)row * e.ldc + col0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        red_add_v4(dst + 4 * j, a * v[4 * j], a * v[4 * j + 1], a * v[4 * j + 2],
+                   a * v[4 * j + 3]);
+    } else {  // EPI_RESID
+      const float4* r = reinterpret_cast<const float4*>(e.R + (size_t)row * e.ldr + col0);
+      float4* dst = reinterpret_cast<float4*>(e.C + (size_t)row * e.ldc + col0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 q = r[j];
+        dst[j] = make_float4(q.x + a * v[4 * j], q.y + a * v[4 * j + 1], q.z + a * v[4 * j + 2],
+                             q.w + a * v[4 * j + 3]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int col = col0 + i;
+      if (col < p.N) {
+        float* dst = e.C + (size_t)row * e.ldc + col;
+        if (e.kind == EPI_STORE) *dst = a * v[i];
+        else if (e.kind == EPI_ACCUM) atomicAdd(dst, a * v[i]);
+        else *dst = e.R[(size_t)row * e.ldr + col] + a * v[i];
+      }
+    }
+  }
+}
+
+struct Top2State {
+  float h0, h1;
+  int i0, i1;
+};
+
+template <int BN>
+__device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc, int row,
+                                                 int nt, bool last_sub, Top2State& st) {
+  const Epilogue& e = p.epi;
+  float v[32];
+  if (e.kind == EPI_SWIGLU_FWD) {
+    constexpr int HALF_CHUNKS = BN / 64;
+#pragma unroll 1
+    for (int c = 0; c < HALF_CHUNKS; ++c) {
+      float g[32];
+      tmem_ld_32cols(tacc + c * 32, g);
+      tmem_ld_32cols(tacc + (c + HALF_CHUNKS) * 32, v);
+      const int f0 = nt * (BN / 2) + c * 32;
+      if (row < p.M) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int f = f0 + i;
+          if (f < p.N) {
+            const size_t o = (size_t)row * e.ldf + f;
+            e.G[o] = g[i];
+            e.U[o] = v[i];
+            e.H[o] = silu_fast(g[i]) * v[i];
+          }
+        }
+      }
+    }
+    return;
+  }
+  if (e.kind == EPI_SWIGLU_BWD) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      tmem_ld_32cols(tacc + c * 32, v);
+      const int f0 = nt * BN + c * 32;
+      if (row < p.M) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int f = f0 + i;
+          if (f < p.N) {
+            const size_t o = (size_t)row * e.ldf + f;
+            const float g = e.Gc[o], u = e.Uc[o];
+            const float sig = 1.0f / (1.0f + __expf(-g));
+            const float dsilu = sig + g * sig * (1.0f - sig);
+            const float dh = v[i];
+            float* dgu = e.C + (size_t)row * e.ldc;
+            dgu[f] = dh * u * dsilu;
+            dgu[p.N + f] = dh * (g * sig);
+          }
+        }
+      }
+    }
+    return;
+  }
+  if (e.kind == EPI_TOP2) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      tmem_ld_32cols(tacc + c * 32, v);
+      const int s0 = nt * BN + c * 32;
+      if (e.C != nullptr && row < p.M) store_row_chunk<BN>(p, row, s0, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int s = s0 + i;
+        const float x = v[i] * e.alpha;
+        // Reference order (src/slot_memory.cu:40-51): replace the first
+        // minimum of the held pair when strictly greater.
+        const bool m1 = st.h1 < st.h0;
+        const float hm = m1 ? st.h1 : st.h0;
+        if (s < p.N && x > hm) {
+          if (m1) { st.h1 = x; st.i1 = s; } else { st.h0 = x; st.i0 = s; }
+        }
+      }
+    }
+    if (last_sub && row < p.M) {
+      const float mx = fmaxf(st.h0, st.h1);
+      const float e0 = __expf(st.h0 - mx), e1 = __expf(st.h1 - mx);
+      const float sum = e0 + e1;
+      e.topk_idx[2 * (size_t)row] = st.i0;
+      e.topk_idx[2 * (size_t)row + 1] = st.i1;
+      e.topk_w[2 * (size_t)row] = e0 / sum;
+      e.topk_w[2 * (size_t)row + 1] = e1 / sum;
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    tmem_ld_32cols(tacc + c * 32, v);
+    store_row_chunk<BN>(p, row, nt * BN + c * 32, v);
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+template <int BN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
+                       const __grid_constant__ CUtensorMap tmB, const KParams p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* split = bars + C::STAGES;
+  uint64_t* empty = bars + 2 * C::STAGES;
+  uint64_t* accf = bars + 3 * C::STAGES;
+  uint64_t* acce = accf + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&split[s], NUM_SPLIT_WARPS);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], NUM_EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == PRODUCER_WARP && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == PRODUCER_WARP) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+        int mt, nt0, nt1, kb0, kb1;
+        unit_range(p, unit, mt, nt0, nt1, kb0, kb1);
+        for (int nt = nt0; nt < nt1 && ok; ++nt) {
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int s = it % C::STAGES;
+            const uint32_t ph = (it / C::STAGES) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1, p.err, abort_flag)) { ok = false; break; }
+            uint8_t* sa = smem + s * C::STAGE_BYTES;
+            uint8_t* sb = sa + C::A_BYTES;
+            mbar_arrive_expect_tx(&full[s], C::RAW_BYTES);
+            const int k0 = kb * BK;
+            const int m0 = mt * BM;
+            if (!p.a_mn) {
+              tma_load_2d(sa, &tmA, &full[s], k0, m0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BM / 32; ++j) tma_load_2d(sa + j * 4096, &tmA, &full[s], m0 + 32 * j, k0);
+            }
+            if (p.b_pair_off == 0) {
+              const int n0 = nt * BN;
+              if (!p.b_mn) {
+                tma_load_2d(sb, &tmB, &full[s], k0, n0);
+              } else {
+#pragma unroll
+                for (int j = 0; j < BN / 32; ++j) tma_load_2d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, k0);
+              }
+            } else {
+              const int n0 = nt * (BN / 2);
+              if (!p.b_mn) {
+                tma_load_2d(sb, &tmB, &full[s], k0, n0);
+                tma_load_2d(sb + (BN / 2) * 128, &tmB, &full[s], k0, n0 + p.b_pair_off);
+              } else {
+#pragma unroll
+                for (int j = 0; j < BN / 64; ++j) {
+                  tma_load_2d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, k0);
+                  tma_load_2d(sb + (j + BN / 64) * 4096, &tmB, &full[s], n0 + p.b_pair_off + 32 * j, k0);
+                }
+              }
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == MMA_WARP) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(BM, BN, 2, p.a_mn, p.b_mn);
+      // Byte advance of one 8-deep K slice and the LBO/SBO of each operand.
+      const uint32_t a_kstep = p.a_mn ? 1024u : 32u;
+      const uint32_t b_kstep = p.b_mn ? 1024u : 32u;
+      const uint32_t a_lbo = p.a_mn ? 4096u : 16u;
+      const uint32_t b_lbo = p.b_mn ? 4096u : 16u;
+      const uint32_t a_sbo = p.a_mn ? 512u : 1024u;
+      const uint32_t b_sbo = p.b_mn ? 512u : 1024u;
+      const uint32_t a_lay = p.a_mn ? 1u : 2u;
+      const uint32_t b_lay = p.b_mn ? 1u : 2u;
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+        int mt, nt0, nt1, kb0, kb1;
+        unit_range(p, unit, mt, nt0, nt1, kb0, kb1);
+        for (int nt = nt0; nt < nt1 && ok; ++nt, ++tc) {
+          const int ab = tc & 1;
+          const uint32_t tph = (tc >> 1) & 1;
+          if (!mbar_wait(&acce[ab], tph ^ 1, p.err, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t tacc = tmem_base + ab * BN;
+          uint32_t accumulate = 0;
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int s = it % C::STAGES;
+            const uint32_t ph = (it / C::STAGES) & 1;
+            if (!mbar_wait(&split[s], ph, p.err, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t a_hi = smem_u32(smem + s * C::STAGE_BYTES);
+            const uint32_t b_hi = a_hi + C::A_BYTES;
+            const uint32_t a_lo = a_hi + C::RAW_BYTES;
+            const uint32_t b_lo = b_hi + C::RAW_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < BK / 8; ++kk) {
+              const uint64_t dah = make_sdesc(a_hi + kk * a_kstep, a_lbo, a_sbo, a_lay);
+              const uint64_t dal = make_sdesc(a_lo + kk * a_kstep, a_lbo, a_sbo, a_lay);
+              const uint64_t dbh = make_sdesc(b_hi + kk * b_kstep, b_lbo, b_sbo, b_lay);
+              const uint64_t dbl = make_sdesc(b_lo + kk * b_kstep, b_lbo, b_sbo, b_lay);
+              umma_tf32(tacc, dah, dbl, idesc, accumulate);
+              umma_tf32(tacc, dal, dbh, idesc, 1);
+              umma_tf32(tacc, dah, dbh, idesc, 1);
+              accumulate = 1;
+            }
+            umma_commit(&empty[s]);
+          }
+          if (!ok) break;
+          umma_commit(&accf[ab]);
+        }
+      }
+    }
+  } else if (warp >= FIRST_SPLIT_WARP) {
+    const int t = threadIdx.x - FIRST_SPLIT_WARP * 32;
+    constexpr int NT = NUM_SPLIT_WARPS * 32;
+    constexpr int N4 = C::RAW_BYTES / 16;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+      int mt, nt0, nt1, kb0, kb1;
+      unit_range(p, unit, mt, nt0, nt1, kb0, kb1);
+      for (int nt = nt0; nt < nt1 && ok; ++nt) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, p.err, abort_flag)) { ok = false; break; }
+          float4* raw = reinterpret_cast<float4*>(smem + s * C::STAGE_BYTES);
+          float4* lo = reinterpret_cast<float4*>(smem + s * C::STAGE_BYTES + C::RAW_BYTES);
+#pragma unroll 4
+          for (int i = t; i < N4; i += NT) {
+            float4 x = raw[i];
+            float4 h, l;
+            uint32_t u;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x.x)); h.x = __uint_as_float(u);
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x.y)); h.y = __uint_as_float(u);
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x.z)); h.z = __uint_as_float(u);
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x.w)); h.w = __uint_as_float(u);
+            l.x = x.x - h.x; l.y = x.y - h.y; l.z = x.z - h.z; l.w = x.w - h.w;
+            raw[i] = h;
+            lo[i] = l;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&split[s]);
+        }
+      }
+    }
+  } else {  // epilogue warps 0..3
+    const int q = warp;  // TMEM lane quadrant
+    uint32_t tc = 0;
+    bool ok = true;
+    for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+      int mt, nt0, nt1, kb0, kb1;
+      unit_range(p, unit, mt, nt0, nt1, kb0, kb1);
+      const int row = mt * BM + q * 32 + lane;
+      Top2State st{-1e30f, -1e30f, 0, 0};
+      for (int nt = nt0; nt < nt1; ++nt, ++tc) {
+        const int ab = tc & 1;
+        const uint32_t tph = (tc >> 1) & 1;
+        if (!mbar_wait(&accf[ab], tph, p.err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN;
+        epilogue_subtile<BN>(p, tacc, row, nt, nt == nt1 - 1, st);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[ab]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == MMA_WARP) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ host
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 2-D fp32 tensor map with a 128-byte inner box. K-major tiles use
+// SWIZZLE_128B; MN-major tiles use SWIZZLE_128B_ATOM_32B (the layout UMMA
+// requires for MN-major tf32 operands).
+static bool make_map(CUtensorMap* m, const float* base, uint64_t inner, uint64_t outer,
+                     uint64_t ld_elems, uint32_t box_outer, bool mn_major) {
+  auto enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * sizeof(float)};
+  cuuint32_t box[2] = {32, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN>
+static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
+                          const KParams& kp) {
+  using C = Cfg<BN>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const int grid = kp.num_units < num_sms() ? kp.num_units : num_sms();
+  gemm_tf32x3_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ta, tb, kp);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand& A,
+                        const Operand& B, const Epilogue& epi, int b_pair_off, int k_splits,
+                        unsigned* err_word) {
+  if (M <= 0 || N <= 0) return cudaSuccess;
+  if (K <= 0 || A.p == nullptr || B.p == nullptr) return cudaErrorInvalidValue;
+  if ((A.ld % 4) || (B.ld % 4) || (reinterpret_cast<uintptr_t>(A.p) & 15) ||
+      (reinterpret_cast<uintptr_t>(B.p) & 15))
+    return cudaErrorInvalidValue;
+  // Paired-B epilogues need BN/2 = 64 aligned feature halves -> BN = 128.
+  const bool paired = b_pair_off > 0;
+  const bool row_owner = epi.kind == EPI_TOP2;
+  const int BN = (paired || row_owner || N <= 128) ? 128 : 256;
+  const int n_logical_tile = paired ? BN / 2 : BN;
+
+  KParams kp{};
+  kp.M = M;
+  kp.N = N;
+  kp.K = K;
+  kp.m_tiles = (M + BM - 1) / BM;
+  kp.n_tiles = (N + n_logical_tile - 1) / n_logical_tile;
+  kp.kb_total = (K + BK - 1) / BK;
+  kp.row_owner = row_owner ? 1 : 0;
+  kp.b_pair_off = b_pair_off;
+  kp.a_mn = A.mn_major ? 1 : 0;
+  kp.b_mn = B.mn_major ? 1 : 0;
+  kp.epi = epi;
+  kp.err = err_word;
+
+  int splits = 1;
+  if (epi.kind == EPI_ACCUM) {
+    if (k_splits > 0) {
+      splits = k_splits;
+    } else {
+      const int tiles = kp.m_tiles * kp.n_tiles;
+      if (tiles < num_sms()) {
+        splits = num_sms() / tiles;
+        const int max_splits = kp.kb_total / 4 > 0 ? kp.kb_total / 4 : 1;  // >= 4 k-blocks each
+        if (splits > max_splits) splits = max_splits;
+      }
+    }
+  }
+  if (splits < 1) splits = 1;
+  kp.kb_per_split = (kp.kb_total + splits - 1) / splits;
+  kp.k_splits = (kp.kb_total + kp.kb_per_split - 1) / kp.kb_per_split;
+  kp.num_units = row_owner ? kp.m_tiles : kp.m_tiles * kp.n_tiles * kp.k_splits;
+
+  CUtensorMap ta, tb;
+  bool ok;
+  if (!A.mn_major)
+    ok = make_map(&ta, A.p, (uint64_t)K, (uint64_t)M, A.ld, BM, false);
+  else
+    ok = make_map(&ta, A.p, (uint64_t)M, (uint64_t)K, A.ld, 32, true);
+  if (!ok) return cudaErrorInvalidValue;
+  const uint64_t b_rows = paired ? (uint64_t)b_pair_off + N : (uint64_t)N;
+  if (!B.mn_major)
+    ok = make_map(&tb, B.p, (uint64_t)K, b_rows, B.ld, paired ? BN / 2 : BN, false);
+  else
+    ok = make_map(&tb, B.p, b_rows, (uint64_t)K, B.ld, 32, true);
+  if (!ok) return cudaErrorInvalidValue;
+
+  if (BN == 128) return launch<128>(stream, ta, tb, kp);
+  return launch<256>(stream, ta, tb, kp);
+}
+
+}  // namespace rnet_gemm
