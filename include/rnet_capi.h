@@ -50,6 +50,139 @@ int rnet_gemm_f32(int M, int N, int K, const float* A, int lda, int a_mn_major, 
                   int ldb, int b_mn_major, float* C, int ldc, const float* R, int ldr, int op,
                   float alpha, void* stream);
 
+/* ------------------------------------------------------------------ layer ops
+ * One entry per function of the reference's include/layers.h:28-153, same
+ * argument meaning, same accumulate/overwrite contract:
+ *   overwrite: every *_forward output and cache, rms_norm_backward dx,
+ *              cross_entropy loss (sum over tokens) and dlogits;
+ *   accumulate (+=): every parameter gradient, and dx of causal_conv /
+ *              min_gru / slot_memory / swiglu backward.
+ * All pointers are device pointers; temporaries are stream-ordered. The
+ * cuBLAS handle of the reference signatures has no counterpart here. */
+int rnet_rms_norm_forward(const float* x, const float* w, float* y, float* rms_cache,
+                          int batch_seq, int dim, float eps, void* stream);
+int rnet_rms_norm_backward(const float* dy, const float* x, const float* w,
+                           const float* rms_cache, float* dx, float* dw, int batch_seq, int dim,
+                           void* stream);
+int rnet_embed_forward(const int* tokens, const float* table, float* output, int batch_seq,
+                       int vocab, int dim, void* stream);
+int rnet_embed_backward(const float* dout, const int* tokens, float* dtable, int batch_seq,
+                        int vocab, int dim, void* stream);
+/* output[M,N] = input[M,K] * weight[N,K]^T */
+int rnet_linear_forward(const float* input, const float* weight, float* output, int M, int N,
+                        int K, void* stream);
+/* conv_buf [3, B*T, D] receives {S = c3+c7+c15, c7, c15} like the reference. */
+int rnet_causal_conv_forward(const float* x, float* y, const float* conv3_w,
+                             const float* conv7_w, const float* conv15_w, const float* mix_w,
+                             float* conv_buf, int batch, int seq_len, int dim, void* stream);
+/* dmix_quirk = 1 reproduces the reference's mix-weight gradient, which uses
+ * S + c7 + c15 (src/causal_conv.cu:155-168); 0 uses S (the exact gradient). */
+int rnet_causal_conv_backward(const float* dy, const float* x, const float* conv3_w,
+                              const float* conv7_w, const float* conv15_w, const float* mix_w,
+                              const float* conv_buf, float* dx, float* d_conv3_w,
+                              float* d_conv7_w, float* d_conv15_w, float* d_mix_w, int batch,
+                              int seq_len, int dim, int dmix_quirk, void* stream);
+int rnet_min_gru_forward(const float* x, float* y, const float* Wz, const float* Wh,
+                         const float* bz, const float* bh, float* z_cache, float* h_cache,
+                         int batch, int seq_len, int dim, void* stream);
+int rnet_min_gru_backward(const float* dy, const float* x, const float* Wz, const float* Wh,
+                          const float* bz, const float* bh, const float* z_cache,
+                          const float* h_cache, float* dx, float* dWz, float* dWh, float* dbz,
+                          float* dbh, int batch, int seq_len, int dim, void* stream);
+/* scores_cache may be NULL (scores are then not materialised; top_k == 2). */
+int rnet_slot_memory_forward(const float* x, float* y, const float* slot_keys,
+                             const float* slot_values, const float* proj_q,
+                             const float* proj_out, float* q_cache, float* scores_cache,
+                             int* topk_idx_cache, float* topk_w_cache, int batch, int seq_len,
+                             int dim, int n_slots, int top_k, void* stream);
+int rnet_slot_memory_backward(const float* dy, const float* x, const float* slot_keys,
+                              const float* slot_values, const float* proj_q,
+                              const float* proj_out, const float* q_cache,
+                              const float* scores_cache, const int* topk_idx_cache,
+                              const float* topk_w_cache, float* dx, float* d_slot_keys,
+                              float* d_slot_values, float* d_proj_q, float* d_proj_out,
+                              int batch, int seq_len, int dim, int n_slots, int top_k,
+                              void* stream);
+int rnet_swiglu_forward(const float* x, float* y, const float* gate_w, const float* up_w,
+                        const float* down_w, float* gate_cache, float* up_cache, int batch_seq,
+                        int dim, int d_ff, void* stream);
+int rnet_swiglu_backward(const float* dy, const float* x, const float* gate_w,
+                         const float* up_w, const float* down_w, const float* gate_cache,
+                         const float* up_cache, float* dx, float* d_gate_w, float* d_up_w,
+                         float* d_down_w, int batch_seq, int dim, int d_ff, void* stream);
+int rnet_cross_entropy_forward(const float* logits, const int* targets, float* loss,
+                               float* dlogits, int batch_seq, int vocab, void* stream);
+int rnet_residual_add(float* x, const float* y, size_t n, void* stream);
+int rnet_scale_grads(float* grads, float scale, size_t n, void* stream);
+
+/* ------------------------------------------------------------------ model
+ * The reference's ResonanceNet class (include/resonance_net.h:56-130).
+ * Parameters and gradients are single flat fp32 device buffers in checkpoint
+ * tensor order (embed, output, final_norm, then per layer norm1..4, conv3,
+ * conv7, conv15, mix, Wz, Wh, bz, bh, slot_keys, slot_values, proj_q,
+ * proj_out, gate, up, down). */
+typedef struct rnet_model_config {
+  int d_model, n_layers, d_ff, n_heads, gru_dim, n_slots, slot_top_k, vocab_size, seq_len;
+  float rms_eps;
+} rnet_model_config; /* byte-identical to the 40-byte checkpoint header */
+
+typedef struct rnet_model rnet_model;
+typedef struct rnet_dist rnet_dist;
+
+/* reference_init = 1: the reference's own initialisation (seeded uniform
+ * Xavier, norm gains 1, biases 0); 0: all parameters zero. */
+int rnet_model_create(const rnet_model_config* cfg, int device, int reference_init,
+                      rnet_model** out);
+/* Create a model from a checkpoint file (config read from its header). */
+int rnet_model_create_from_checkpoint(const char* path, int device, rnet_model** out);
+int rnet_model_destroy(rnet_model* m);
+int rnet_model_get_config(const rnet_model* m, rnet_model_config* out);
+int rnet_model_param_count(const rnet_model* m, size_t* n);
+int rnet_model_device_buffers(rnet_model* m, float** d_params, float** d_grads);
+int rnet_model_stream(rnet_model* m, void** stream);
+int rnet_model_set_params(rnet_model* m, const float* host, size_t n);
+int rnet_model_get_params(rnet_model* m, float* host, size_t n);
+int rnet_model_get_grads(rnet_model* m, float* host, size_t n);
+/* Re-derive internal layouts after the caller wrote d_params directly. */
+int rnet_model_params_updated(rnet_model* m);
+int rnet_model_set_conv_quirk(rnet_model* m, int on);
+int rnet_model_forward(rnet_model* m, const int* d_tokens, float* d_logits, int batch,
+                       int seq_len);
+int rnet_model_backward(rnet_model* m, const float* d_dlogits, const int* d_tokens, int batch,
+                        int seq_len);
+int rnet_model_zero_grad(rnet_model* m);
+int rnet_model_step(rnet_model* m, float lr, float grad_clip);
+/* zero_grad + forward + cross-entropy (dlogits scaled by 1/(batch*seq_len))
+ * + backward + (all-reduce) + clipped SGD, all on the model stream.
+ * d_loss_sum (device, may be NULL) receives the summed token loss. */
+int rnet_model_train_step(rnet_model* m, const int* d_inputs, const int* d_targets, int batch,
+                          int seq_len, float lr, float grad_clip, float* d_loss_sum);
+/* Same with host token buffers; copies in, steps, copies the loss sum out and
+ * waits for it. */
+int rnet_model_train_step_host(rnet_model* m, const int* h_inputs, const int* h_targets,
+                               int batch, int seq_len, float lr, float grad_clip,
+                               float* h_loss_sum);
+/* Device pointers to the last cached forward's top-k indices / weights of a
+ * layer ([batch*seq_len, top_k], reference slot order). */
+int rnet_model_topk(rnet_model* m, int layer, const int** d_idx, const float** d_w);
+/* Host copies of the same ([batch*seq_len*top_k] each; waits for the stream). */
+int rnet_model_topk_host(rnet_model* m, int layer, int* h_idx, float* h_w, size_t n);
+int rnet_model_save(rnet_model* m, const char* path);
+int rnet_model_load_weights(rnet_model* m, const char* path);
+/* Wait for the model stream and report any device error word bits. */
+int rnet_model_synchronize(rnet_model* m);
+
+/* ------------------------------------------------------------------ data parallel
+ * The reference's include/dist.h:12-36 over NCCL (loaded at run time). */
+int rnet_dist_unique_id(unsigned char uid[128]);
+int rnet_dist_create(int rank, int world, int local_rank, const unsigned char uid[128],
+                     int timeout_ms, rnet_dist** out);
+int rnet_dist_destroy(rnet_dist* d);
+int rnet_dist_allreduce_sum(rnet_dist* d, float* d_buf, size_t count, void* stream);
+/* Attach (or detach with NULL): backward then all-reduces gradient buckets
+ * as they complete and step() uses the reference's world-size scaling. */
+int rnet_model_set_dist(rnet_model* m, rnet_dist* d);
+
 #ifdef __cplusplus
 }
 #endif

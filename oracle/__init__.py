@@ -1,0 +1,159 @@
+"""ORACLE — test infrastructure only.
+
+ctypes bindings of
+  * liboracle.so  — scalar C++/OpenMP restatement of the reference math
+                    (oracle/oracle.cpp, every function cites the reference
+                    file:line it follows);
+  * _ref/libref.so — the reference's own CUDA sources compiled unmodified
+                    plus a small C-ABI harness (oracle/ref_capi.cpp).
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+legs may import this package, and only as the checker or the timed baseline —
+never as the product path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_ORACLE = os.path.join(HERE, "liboracle.so")
+LIB_REF = os.path.join(HERE, "_ref", "libref.so")
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_F = ctypes.c_float
+
+
+class OrcConfig(ctypes.Structure):
+    """Byte-identical to the reference ModelConfig (include/config.h:7-18)."""
+    _fields_ = [("d_model", _I), ("n_layers", _I), ("d_ff", _I), ("n_heads", _I),
+                ("gru_dim", _I), ("n_slots", _I), ("slot_top_k", _I), ("vocab_size", _I),
+                ("seq_len", _I), ("rms_eps", _F)]
+
+
+def make_config(d_model=512, n_layers=8, d_ff=1024, n_slots=1024, top_k=2, vocab=256,
+                seq_len=256, eps=1e-6) -> OrcConfig:
+    return OrcConfig(d_model, n_layers, d_ff, 8, d_model, n_slots, top_k, vocab, seq_len, eps)
+
+
+def build() -> None:
+    """Compile liboracle.so (and the reference harness when the reference
+    sources are present in this container)."""
+    subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
+    if os.path.isdir("/root/reference/src"):
+        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True,
+                       stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_ORACLE):
+            build()
+        _lib = ctypes.CDLL(LIB_ORACLE)
+        _lib.orc_param_count.restype = ctypes.c_size_t
+        _lib.orc_param_count.argtypes = [ctypes.POINTER(OrcConfig)]
+    return _lib
+
+
+def ptr(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(_P)
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_num_threads(int(n))
+
+
+def num_threads() -> int:
+    return int(lib().orc_num_threads())
+
+
+def param_count(cfg: OrcConfig) -> int:
+    return int(lib().orc_param_count(ctypes.byref(cfg)))
+
+
+def train_step(cfg, params, tokens, targets, B, T, lr=3e-4, clip=1.0, quirk=1):
+    """One reference training step. Returns dict(loss_sum, grads, params (updated),
+    topk_idx [L,N,k], topk_w [L,N,k], logits [N,V])."""
+    params = np.array(params, dtype=np.float32, copy=True)
+    n = param_count(cfg)
+    grads = np.zeros(n, np.float32)
+    N = B * T
+    k = cfg.slot_top_k
+    idx = np.zeros((cfg.n_layers, N, k), np.int32)
+    w = np.zeros((cfg.n_layers, N, k), np.float32)
+    logits = np.zeros((N, cfg.vocab_size), np.float32)
+    loss = _F(0)
+    tok = np.ascontiguousarray(tokens, np.int32)
+    tgt = np.ascontiguousarray(targets, np.int32)
+    lib().orc_train_step(ctypes.byref(cfg), ptr(params), ptr(grads), ptr(tok), ptr(tgt), B, T,
+                         _F(lr), _F(clip), quirk, ctypes.byref(loss), ptr(idx), ptr(w),
+                         ptr(logits))
+    return dict(loss_sum=loss.value, grads=grads, params=params, topk_idx=idx, topk_w=w,
+                logits=logits)
+
+
+def forward(cfg, params, tokens, B, T):
+    N = B * T
+    logits = np.zeros((N, cfg.vocab_size), np.float32)
+    idx = np.zeros((cfg.n_layers, N, cfg.slot_top_k), np.int32)
+    w = np.zeros((cfg.n_layers, N, cfg.slot_top_k), np.float32)
+    tok = np.ascontiguousarray(tokens, np.int32)
+    lib().orc_model_forward(ctypes.byref(cfg), ptr(np.ascontiguousarray(params, np.float32)),
+                            ptr(tok), B, T, ptr(logits), ptr(idx), ptr(w))
+    return logits, idx, w
+
+
+def topk_margins(cfg, params, tokens, B, T):
+    """Per-layer top-k selection margins [L, B*T] (see oracle.cpp topk_row)."""
+    m = np.zeros((cfg.n_layers, B * T), np.float32)
+    tok = np.ascontiguousarray(tokens, np.int32)
+    lib().orc_topk_margins(ctypes.byref(cfg), ptr(np.ascontiguousarray(params, np.float32)),
+                           ptr(tok), B, T, ptr(m))
+    return m
+
+
+def sgd_step(cfg, params, grads, lr, clip, world=1):
+    p = np.array(params, np.float32, copy=True)
+    lib().orc_sgd_step(ctypes.byref(cfg), ptr(p), ptr(np.ascontiguousarray(grads, np.float32)),
+                       _F(lr), _F(clip), int(world))
+    return p
+
+
+# ------------------------------------------------------------------ reference harness
+_ref = None
+
+
+def ref_available() -> bool:
+    return os.path.exists(LIB_REF)
+
+
+def ref_lib() -> ctypes.CDLL:
+    global _ref
+    if _ref is None:
+        _ref = ctypes.CDLL(LIB_REF)
+        _ref.ref_model_load.restype = _P
+        _ref.ref_model_load.argtypes = [ctypes.c_char_p]
+        _ref.ref_model_param_count.restype = ctypes.c_size_t
+        _ref.ref_model_param_count.argtypes = [_P]
+        _ref.ref_train_step.restype = _F
+        _ref.ref_train_step.argtypes = [_P, _P, _P, _I, _I, _F, _F]
+        _ref.ref_train_step_device.argtypes = [_P, _P, _P, _I, _I, _F, _F]
+        _ref.ref_forward.argtypes = [_P, _P, _I, _I, _P]
+        _ref.ref_forward_device.argtypes = [_P, _P, _I, _I]
+        for f in ("ref_model_get_params", "ref_model_get_grads"):
+            getattr(_ref, f).argtypes = [_P, _P]
+        _ref.ref_get_logits.argtypes = [_P, _P, _I]
+        _ref.ref_get_topk.argtypes = [_P, _P, _P, _I]
+        _ref.ref_model_destroy.argtypes = [_P]
+    return _ref

@@ -289,9 +289,12 @@ void orc_gru_bwd(const float* dy, const float* x, const float* Wz, const float* 
 // src/slot_memory.cu:14-77 top-k selection + softmax + gather, exactly the
 // reference's sequential scan: held = (-1e30, idx 0) x k; for each slot i in
 // order, m = first index of the smallest held value; replace if v > held[m].
-static void topk_row(const float* sr, int S, int k, int* idx, float* w) {
-  float val[8];
-  int id[8];
+// `margin` (optional) receives the selection margin: the smaller of the gap
+// between the k-th and (k+1)-th largest score and the smallest gap among the
+// selected k (ties there decide the positional order).
+static void topk_row(const float* sr, int S, int k, int* idx, float* w, float* margin = nullptr) {
+  float val[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  int id[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   for (int j = 0; j < k; ++j) { val[j] = -1e30f; id[j] = 0; }
   for (int i = 0; i < S; ++i) {
     const float v = sr[i];
@@ -299,6 +302,20 @@ static void topk_row(const float* sr, int S, int k, int* idx, float* w) {
     for (int j = 1; j < k; ++j)
       if (val[j] < val[mk]) mk = j;
     if (v > val[mk]) { val[mk] = v; id[mk] = i; }
+  }
+  if (margin) {
+    float kth = val[0];
+    for (int j = 1; j < k; ++j) kth = std::fmin(kth, val[j]);
+    float next = -INFINITY;
+    for (int i = 0; i < S; ++i) {
+      bool sel = false;
+      for (int j = 0; j < k; ++j) sel = sel || id[j] == i;
+      if (!sel) next = std::fmax(next, sr[i]);
+    }
+    float m = kth - next;
+    for (int a = 0; a < k; ++a)
+      for (int b = a + 1; b < k; ++b) m = std::fmin(m, std::fabs(val[a] - val[b]));
+    *margin = m;
   }
   float mx = val[0];
   for (int j = 1; j < k; ++j) mx = std::fmax(mx, val[j]);
@@ -639,6 +656,32 @@ void copy_topk(const OrcConfig* c, const std::vector<LayerCache>& caches, int N,
 }  // namespace
 
 extern "C" {
+
+// Row-wise top-k + softmax on a given score matrix (the reference's selection
+// rule, src/slot_memory.cu:32-62), for known-answer tests of tie handling.
+void orc_topk_rows(const float* scores, int N, int S, int k, int* idx, float* w) {
+  for (int n = 0; n < N; ++n)
+    topk_row(scores + (size_t)n * S, S, k, idx + (size_t)n * k, w + (size_t)n * k);
+}
+
+// Per-layer top-k selection margins [L, B*T] of a forward pass (see topk_row).
+void orc_topk_margins(const OrcConfig* c, const float* params, const int* tokens, int B, int T,
+                      float* margins) {
+  ModelP P = bind(c, const_cast<float*>(params));
+  const int N = B * T;
+  std::vector<float> logits((size_t)N * c->vocab_size);
+  std::vector<LayerCache> caches;
+  // forward with caches, then re-run the selection on each layer's scores
+  model_fwd_impl(c, P, tokens, B, T, logits.data(), &caches, nullptr, nullptr, nullptr);
+  for (int l = 0; l < c->n_layers; ++l) {
+    std::vector<int> idx((size_t)N * c->slot_top_k);
+    std::vector<float> w((size_t)N * c->slot_top_k);
+    for (int n = 0; n < N; ++n)
+      topk_row(caches[l].scores.data() + (size_t)n * c->n_slots, c->n_slots, c->slot_top_k,
+               idx.data() + (size_t)n * c->slot_top_k, w.data() + (size_t)n * c->slot_top_k,
+               margins + (size_t)l * N + n);
+  }
+}
 
 void orc_model_forward(const OrcConfig* c, const float* params, const int* tokens, int B, int T,
                        float* logits, int* topk_out, float* topw_out) {

@@ -1,0 +1,516 @@
+// ResonanceNet model engine (see engine.h).
+//
+// Reference orchestration: src/resonance_net.cpp:44-216 (allocation, init),
+// :218-343 (forward with caches), :346-408 (inference forward), :411-548
+// (backward), :551-697 (step, zero_grad), :743-824 (checkpoint).
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "dist.h"
+#include "engine.h"
+#include "gemm.cuh"
+#include "kernels.cuh"
+#include "status.h"
+
+namespace rnet_engine {
+using rnet_gemm::Epilogue;
+using rnet_gemm::Operand;
+using namespace rnet_gemm;
+
+namespace {
+
+Operand kmaj(const float* p, int ld) { return Operand{p, ld, false}; }
+Operand mnmaj(const float* p, int ld) { return Operand{p, ld, true}; }
+
+Epilogue epi_store(float* C, int ldc) {
+  Epilogue e;
+  e.kind = EPI_STORE;
+  e.C = C;
+  e.ldc = ldc;
+  return e;
+}
+Epilogue epi_accum(float* C, int ldc) {
+  Epilogue e;
+  e.kind = EPI_ACCUM;
+  e.C = C;
+  e.ldc = ldc;
+  return e;
+}
+Epilogue epi_resid(float* C, const float* R, int ld) {
+  Epilogue e;
+  e.kind = EPI_RESID;
+  e.C = C;
+  e.ldc = ld;
+  e.R = R;
+  e.ldr = ld;
+  return e;
+}
+
+size_t layer_count(const rnet_model_config& c) {
+  const size_t D = c.d_model, F = c.d_ff, S = c.n_slots;
+  return 4 * D + 25 * D + 3 * D * D + 2 * D + 2 * D * S + 2 * D * D + 3 * D * F;
+}
+
+}  // namespace
+
+#define CK(expr)                                                     \
+  do {                                                               \
+    cudaError_t _e = (expr);                                         \
+    if (_e != cudaSuccess) return rnet_status::fail_cuda(_e, #expr); \
+  } while (0)
+
+Engine::Engine(const rnet_model_config& c) : cfg_(c) {}
+
+Engine::~Engine() {
+  if (device_ >= 0) cudaSetDevice(device_);
+  if (stream_) cudaStreamSynchronize(stream_);
+  cudaFree(params_);
+  cudaFree(grads_);
+  cudaFree(KT_);
+  cudaFree(VT_);
+  cudaFree(dKT_);
+  cudaFree(dVT_);
+  cudaFree(scratch_);
+  cudaFree(arena_);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+int Engine::gemm_err(cudaError_t e, const char* what) {
+  return rnet_status::fail_cuda(e, what);
+}
+
+int Engine::init(int device, bool reference_init) {
+  const rnet_model_config& c = cfg_;
+  if (c.d_model <= 0 || c.n_layers <= 0 || c.d_ff <= 0 || c.n_slots <= 0 || c.vocab_size <= 0)
+    return rnet_status::fail(RNET_ERR_ARG, "model config: non-positive dimension");
+  if (c.d_model % 32 || c.d_ff % 32 || c.n_slots % 4 || c.vocab_size % 4)
+    return rnet_status::fail(RNET_ERR_ARG,
+                             "model config: d_model and d_ff must be multiples of 32, "
+                             "n_slots and vocab_size multiples of 4");
+  if (c.d_model > 2048) return rnet_status::fail(RNET_ERR_UNSUPPORTED, "d_model > 2048");
+  if (c.vocab_size > 1024) return rnet_status::fail(RNET_ERR_UNSUPPORTED, "vocab_size > 1024");
+  if (c.slot_top_k < 1 || c.slot_top_k > 8 || c.slot_top_k > c.n_slots)
+    return rnet_status::fail(RNET_ERR_ARG, "slot_top_k must be in [1, min(8, n_slots)]");
+  device_ = device;
+  CK(cudaSetDevice(device));
+  CK(cudaStreamCreate(&stream_));  // blocking w.r.t. the legacy stream, like the reference
+
+  const size_t D = c.d_model, V = c.vocab_size, F = c.d_ff, S = c.n_slots, L = c.n_layers;
+  P_ = 2 * V * D + D + L * layer_count(c);
+  CK(cudaMalloc(&params_, P_ * sizeof(float)));
+  CK(cudaMalloc(&grads_, P_ * sizeof(float)));
+  CK(cudaMemset(grads_, 0, P_ * sizeof(float)));
+  auto bind = [&](float* base, std::vector<LayerParams>& out, float** e, float** o, float** f) {
+    float* p = base;
+    auto take = [&](size_t n) { float* r = p; p += n; return r; };
+    *e = take(V * D);
+    *o = take(V * D);
+    *f = take(D);
+    out.resize(L);
+    for (size_t l = 0; l < L; ++l) {
+      LayerParams& q = out[l];
+      q.offset = (size_t)(p - base);
+      q.n1 = take(D); q.n2 = take(D); q.n3 = take(D); q.n4 = take(D);
+      q.c3 = take(3 * D); q.c7 = take(7 * D); q.c15 = take(15 * D); q.mix = take(D * D);
+      q.Wz = take(D * D); q.Wh = take(D * D); q.bz = take(D); q.bh = take(D);
+      q.keys = take(D * S); q.vals = take(D * S); q.pq = take(D * D); q.pout = take(D * D);
+      q.gate = take(F * D); q.up = take(F * D); q.down = take(D * F);
+      q.count = (size_t)(p - base) - q.offset;
+    }
+  };
+  bind(params_, W_, &embed_, &outw_, &fnorm_);
+  bind(grads_, G_, &g_embed_, &g_outw_, &g_fnorm_);
+  CK(cudaMalloc(&KT_, L * S * D * sizeof(float)));
+  CK(cudaMalloc(&VT_, L * S * D * sizeof(float)));
+  CK(cudaMalloc(&dKT_, L * S * D * sizeof(float)));
+  CK(cudaMalloc(&dVT_, L * S * D * sizeof(float)));
+  const size_t scr = rnet_k::sgd_scratch_floats() + 64;
+  CK(cudaMalloc(&scratch_, scr * sizeof(float)));
+  loss_dev_ = scratch_ + rnet_k::sgd_scratch_floats();
+  norm_dev_ = loss_dev_ + 1;
+
+  if (reference_init) {
+    // Same distributions, seeds and tensor order as the reference
+    // (src/resonance_net.cpp:27-42 and :180-216): U(-1/sqrt(fan_in), +1/sqrt(fan_in))
+    // from std::mt19937(seed), seed = 42, 43, ... in tensor order; norm gains 1,
+    // biases 0.
+    std::vector<float> h(P_, 0.0f);
+    unsigned seed = 42;
+    auto xavier = [&](float* dptr, size_t n, int fan_in) {
+      std::mt19937 rng(seed++);
+      const float sc = 1.0f / sqrtf((float)fan_in);
+      std::uniform_real_distribution<float> dist(-sc, sc);
+      float* hp = h.data() + (dptr - params_);
+      for (size_t i = 0; i < n; ++i) hp[i] = dist(rng);
+    };
+    auto ones = [&](float* dptr, size_t n) {
+      float* hp = h.data() + (dptr - params_);
+      for (size_t i = 0; i < n; ++i) hp[i] = 1.0f;
+    };
+    xavier(embed_, V * D, (int)D);
+    xavier(outw_, V * D, (int)D);
+    ones(fnorm_, D);
+    for (size_t l = 0; l < L; ++l) {
+      LayerParams& w = W_[l];
+      ones(w.n1, D); ones(w.n2, D); ones(w.n3, D); ones(w.n4, D);
+      xavier(w.c3, 3 * D, (int)D);
+      xavier(w.c7, 7 * D, (int)D);
+      xavier(w.c15, 15 * D, (int)D);
+      xavier(w.mix, D * D, (int)D);
+      xavier(w.Wz, D * D, (int)D);
+      xavier(w.Wh, D * D, (int)D);
+      xavier(w.keys, D * S, (int)D);
+      xavier(w.vals, D * S, (int)D);
+      xavier(w.pq, D * D, (int)D);
+      xavier(w.pout, D * D, (int)D);
+      xavier(w.gate, D * F, (int)D);
+      xavier(w.up, D * F, (int)D);
+      xavier(w.down, F * D, (int)F);
+    }
+    CK(cudaMemcpy(params_, h.data(), P_ * sizeof(float), cudaMemcpyHostToDevice));
+  } else {
+    CK(cudaMemset(params_, 0, P_ * sizeof(float)));
+  }
+  return refresh_shadows();
+}
+
+int Engine::refresh_shadows() {
+  const int D = cfg_.d_model, S = cfg_.n_slots;
+  for (int l = 0; l < cfg_.n_layers; ++l) {
+    CK(rnet_k::transpose(W_[l].keys, KT_ + (size_t)l * S * D, D, S, 0, stream_));
+    CK(rnet_k::transpose(W_[l].vals, VT_ + (size_t)l * S * D, D, S, 0, stream_));
+  }
+  return RNET_OK;
+}
+
+int Engine::set_params_host(const float* h, size_t n) {
+  if (n != P_) return rnet_status::fail(RNET_ERR_ARG, "set_params: wrong parameter count");
+  CK(cudaMemcpyAsync(params_, h, P_ * sizeof(float), cudaMemcpyHostToDevice, stream_));
+  int rc = refresh_shadows();
+  if (rc) return rc;
+  CK(cudaStreamSynchronize(stream_));
+  return RNET_OK;
+}
+
+int Engine::get_params_host(float* h, size_t n) {
+  if (n != P_) return rnet_status::fail(RNET_ERR_ARG, "get_params: wrong parameter count");
+  CK(cudaMemcpyAsync(h, params_, P_ * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  return RNET_OK;
+}
+
+int Engine::get_grads_host(float* h, size_t n) {
+  if (n != P_) return rnet_status::fail(RNET_ERR_ARG, "get_grads: wrong parameter count");
+  CK(cudaMemcpyAsync(h, grads_, P_ * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  return RNET_OK;
+}
+
+int Engine::ensure_capacity(int N, bool with_caches) {
+  if (N <= cap_N_ && (cap_caches_ || !with_caches)) return RNET_OK;
+  const size_t D = cfg_.d_model, F = cfg_.d_ff, S = cfg_.n_slots, V = cfg_.vocab_size;
+  const size_t L = cfg_.n_layers, k = cfg_.slot_top_k;
+  const size_t n = (size_t)N;
+  const size_t nact = with_caches ? L : 1;
+  std::vector<std::pair<void**, size_t>> plan;  // (slot, bytes)
+  act_.assign(nact, LayerAct{});
+  auto f = [&](float** p, size_t cnt) { plan.push_back({(void**)p, cnt * sizeof(float)}); };
+  for (size_t l = 0; l < nact; ++l) {
+    LayerAct& a = act_[l];
+    f(&a.n1, n * D); f(&a.n2, n * D); f(&a.n3, n * D); f(&a.n4, n * D);
+    f(&a.rinv1, n); f(&a.rinv2, n); f(&a.rinv3, n); f(&a.rinv4, n);
+    f(&a.S, n * D); f(&a.Sq, n * D); f(&a.P, 2 * n * D); f(&a.z, n * D); f(&a.h, n * D);
+    f(&a.q, n * D); f(&a.r, n * D);
+    plan.push_back({(void**)&a.idx, n * k * sizeof(int)});
+    f(&a.w, n * k);
+    f(&a.r1, n * D); f(&a.r2, n * D); f(&a.r3, n * D);
+    f(&a.G, n * F); f(&a.U, n * F); f(&a.H, n * F);
+  }
+  f(&X_, (with_caches ? (L + 1) : 2) * n * D);
+  f(&nf_, n * D);
+  f(&rinvf_, n);
+  f(&logits_, n * V);
+  f(&dlogits_, n * V);
+  if (k != 2) f(&scores_, n * S);
+  else scores_ = nullptr;
+  if (with_caches) {
+    f(&dX_, n * D); f(&dsub_, n * D); f(&dS_, n * D); f(&dq_, n * D); f(&dr_, n * D);
+    f(&dPZH_, 2 * n * D); f(&dGU_, 2 * n * F); f(&dnf_, n * D);
+    // conv weight-grad partials (<= 192 x 25 x D) and CE loss partials share it
+    const size_t cp = 192 * 25 * D, cep = rnet_k::ce_partials_floats(N) + 8;
+    f(&conv_parts_, cp > cep ? cp : cep);
+  } else {
+    dX_ = dsub_ = dS_ = dq_ = dr_ = dPZH_ = dGU_ = dnf_ = conv_parts_ = nullptr;
+  }
+  size_t total = 0;
+  for (auto& e : plan) total += (e.second + 255) & ~size_t(255);
+  if (arena_) {
+    cudaStreamSynchronize(stream_);
+    cudaFree(arena_);
+    arena_ = nullptr;
+  }
+  CK(cudaMalloc(&arena_, total));
+  arena_bytes_ = total;
+  char* p = (char*)arena_;
+  for (auto& e : plan) {
+    *e.first = p;
+    p += (e.second + 255) & ~size_t(255);
+  }
+  cap_N_ = N;
+  cap_caches_ = with_caches;
+  have_cache_ = false;
+  return RNET_OK;
+}
+
+// ------------------------------------------------------------------ forward
+int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B, int T) {
+  const int N = B * T, D = cfg_.d_model, F = cfg_.d_ff, S = cfg_.n_slots, k = cfg_.slot_top_k;
+  const float eps = cfg_.rms_eps;
+  const LayerParams& w = W_[l];
+  unsigned* err = rnet_status::device_error_word();
+  cudaStream_t s = stream_;
+  const float* KT = KT_ + (size_t)l * S * D;
+  const float* VT = VT_ + (size_t)l * S * D;
+  // 1. multi-scale causal conv (reference layer_forward :287-299)
+  CK(rnet_k::rms_norm_fwd(Xl, w.n1, a.n1, a.rinv1, N, D, eps, s));
+  CK(rnet_k::conv_fwd(a.n1, w.c3, w.c7, w.c15, a.S, conv_quirk ? a.Sq : nullptr, nullptr,
+                      nullptr, B, T, D, s));
+  CK(gemm_tf32x3(s, N, D, D, kmaj(a.S, D), kmaj(w.mix, D), epi_resid(a.r1, Xl, D), 0, 0, err));
+  // 2. MinGRU (:301-313): P = n2 [Wz;Wh]^T, fused gate + scan + residual
+  CK(rnet_k::rms_norm_fwd(a.r1, w.n2, a.n2, a.rinv2, N, D, eps, s));
+  CK(gemm_tf32x3(s, N, 2 * D, D, kmaj(a.n2, D), kmaj(w.Wz, D), epi_store(a.P, 2 * D), 0, 0, err));
+  CK(rnet_k::gru_scan_fwd(a.P, a.P + D, 2 * D, w.bz, w.bh, a.z, a.h, nullptr, a.r1, a.r2, B, T,
+                          D, s));
+  // 3. slot memory (:315-330)
+  CK(rnet_k::rms_norm_fwd(a.r2, w.n3, a.n3, a.rinv3, N, D, eps, s));
+  CK(gemm_tf32x3(s, N, D, D, kmaj(a.n3, D), kmaj(w.pq, D), epi_store(a.q, D), 0, 0, err));
+  if (k == 2) {
+    Epilogue e;
+    e.kind = EPI_TOP2;
+    e.topk_idx = a.idx;
+    e.topk_w = a.w;
+    CK(gemm_tf32x3(s, N, S, D, kmaj(a.q, D), kmaj(KT, D), e, 0, 0, err));
+  } else {
+    CK(gemm_tf32x3(s, N, S, D, kmaj(a.q, D), kmaj(KT, D), epi_store(scores_, S), 0, 0, err));
+    CK(rnet_k::topk_rows(scores_, a.idx, a.w, N, S, k, s));
+  }
+  CK(rnet_k::slot_gather(a.idx, a.w, VT, a.r, N, D, S, k, err, s));
+  CK(gemm_tf32x3(s, N, D, D, kmaj(a.r, D), kmaj(w.pout, D), epi_resid(a.r3, a.r2, D), 0, 0, err));
+  // 4. SwiGLU FFN (:332-342): paired gate|up tiles, SiLU*up in the epilogue
+  CK(rnet_k::rms_norm_fwd(a.r3, w.n4, a.n4, a.rinv4, N, D, eps, s));
+  {
+    Epilogue e;
+    e.kind = EPI_SWIGLU_FWD;
+    e.G = a.G;
+    e.U = a.U;
+    e.H = a.H;
+    e.ldf = F;
+    CK(gemm_tf32x3(s, N, F, D, kmaj(a.n4, D), kmaj(w.gate, D), e, F, 0, err));
+  }
+  CK(gemm_tf32x3(s, N, D, F, kmaj(a.H, F), kmaj(w.down, F), epi_resid(Xn, a.r3, D), 0, 0, err));
+  return RNET_OK;
+}
+
+int Engine::forward(const int* d_tokens, float* d_logits, int B, int T) {
+  if (B <= 0 || T <= 0) return rnet_status::fail(RNET_ERR_ARG, "forward: empty batch");
+  const int N = B * T, D = cfg_.d_model, V = cfg_.vocab_size;
+  // Same cache rule as the reference (src/resonance_net.cpp:245).
+  const bool caches = N <= 64 * (cfg_.seq_len > 0 ? cfg_.seq_len : 256);
+  int rc = ensure_capacity(N, caches);
+  if (rc) return rc;
+  cudaStream_t s = stream_;
+  unsigned* err = rnet_status::device_error_word();
+  const size_t ND = (size_t)N * D;
+  CK(rnet_k::embed_fwd(d_tokens, embed_, X_, N, V, D, err, s));
+  for (int l = 0; l < cfg_.n_layers; ++l) {
+    const float* Xl = caches ? X_ + (size_t)l * ND : X_ + (size_t)(l & 1) * ND;
+    float* Xn = caches ? X_ + (size_t)(l + 1) * ND : X_ + (size_t)((l + 1) & 1) * ND;
+    rc = layer_forward(l, Xl, Xn, caches ? act_[l] : act_[0], B, T);
+    if (rc) return rc;
+  }
+  const float* XL = caches ? X_ + (size_t)cfg_.n_layers * ND : X_ + (size_t)(cfg_.n_layers & 1) * ND;
+  CK(rnet_k::rms_norm_fwd(XL, fnorm_, nf_, rinvf_, N, D, cfg_.rms_eps, s));
+  CK(gemm_tf32x3(s, N, V, D, kmaj(nf_, D), kmaj(outw_, D), epi_store(d_logits, V), 0, 0, err));
+  have_cache_ = caches;
+  last_B_ = B;
+  last_T_ = T;
+  return RNET_OK;
+}
+
+// ------------------------------------------------------------------ backward
+int Engine::head_backward(const float* d_dlogits, int N) {
+  const int D = cfg_.d_model, V = cfg_.vocab_size;
+  unsigned* err = rnet_status::device_error_word();
+  cudaStream_t s = stream_;
+  // src/resonance_net.cpp:428-442
+  CK(gemm_tf32x3(s, N, D, V, kmaj(d_dlogits, V), mnmaj(outw_, D), epi_store(dnf_, D), 0, 0, err));
+  CK(gemm_tf32x3(s, V, D, N, mnmaj(d_dlogits, V), mnmaj(nf_, D), epi_accum(g_outw_, D), 0, 0, err));
+  const float* XL = X_ + (size_t)cfg_.n_layers * N * D;
+  CK(rnet_k::rms_norm_bwd(dnf_, XL, fnorm_, rinvf_, dX_, g_fnorm_, N, D, 0, s));
+  return RNET_OK;
+}
+
+int Engine::layer_backward(int l, int B, int T) {
+  const int N = B * T, D = cfg_.d_model, F = cfg_.d_ff, S = cfg_.n_slots, k = cfg_.slot_top_k;
+  const LayerParams& w = W_[l];
+  const LayerParams& g = G_[l];
+  LayerAct& a = act_[l];
+  unsigned* err = rnet_status::device_error_word();
+  cudaStream_t s = stream_;
+  const float* Xl = X_ + (size_t)l * N * D;
+  float* dKT = dKT_ + (size_t)l * S * D;
+  float* dVT = dVT_ + (size_t)l * S * D;
+  // 4. SwiGLU (src/resonance_net.cpp:468-490, src/swiglu_ffn.cu:88-152)
+  {
+    Epilogue e;
+    e.kind = EPI_SWIGLU_BWD;
+    e.C = dGU_;
+    e.ldc = 2 * F;
+    e.Gc = a.G;
+    e.Uc = a.U;
+    e.ldf = F;
+    CK(gemm_tf32x3(s, N, F, D, kmaj(dX_, D), mnmaj(w.down, F), e, 0, 0, err));
+  }
+  CK(gemm_tf32x3(s, D, F, N, mnmaj(dX_, D), mnmaj(a.H, F), epi_accum(g.down, F), 0, 0, err));
+  CK(gemm_tf32x3(s, N, D, 2 * F, kmaj(dGU_, 2 * F), mnmaj(w.gate, D), epi_store(dsub_, D), 0, 0, err));
+  CK(gemm_tf32x3(s, 2 * F, D, N, mnmaj(dGU_, 2 * F), mnmaj(a.n4, D), epi_accum(g.gate, D), 0, 0, err));
+  CK(rnet_k::rms_norm_bwd(dsub_, a.r3, w.n4, a.rinv4, dX_, g.n4, N, D, 1, s));
+  // 3. slot memory (:492-510, src/slot_memory.cu:171-244) — sparse top-k path
+  CK(gemm_tf32x3(s, N, D, D, kmaj(dX_, D), mnmaj(w.pout, D), epi_store(dr_, D), 0, 0, err));
+  CK(gemm_tf32x3(s, D, D, N, mnmaj(dX_, D), mnmaj(a.r, D), epi_accum(g.pout, D), 0, 0, err));
+  CK(cudaMemsetAsync(dKT, 0, (size_t)S * D * sizeof(float), s));
+  CK(cudaMemsetAsync(dVT, 0, (size_t)S * D * sizeof(float), s));
+  CK(rnet_k::slot_sparse_bwd(dr_, a.idx, a.w, VT_ + (size_t)l * S * D, KT_ + (size_t)l * S * D,
+                             a.q, dq_, dVT, dKT, N, D, S, k, err, s));
+  CK(rnet_k::transpose(dKT, g.keys, S, D, 1, s));
+  CK(rnet_k::transpose(dVT, g.vals, S, D, 1, s));
+  CK(gemm_tf32x3(s, N, D, D, kmaj(dq_, D), mnmaj(w.pq, D), epi_store(dsub_, D), 0, 0, err));
+  CK(gemm_tf32x3(s, D, D, N, mnmaj(dq_, D), mnmaj(a.n3, D), epi_accum(g.pq, D), 0, 0, err));
+  CK(rnet_k::rms_norm_bwd(dsub_, a.r2, w.n3, a.rinv3, dX_, g.n3, N, D, 1, s));
+  // 2. MinGRU (:512-528, src/min_gru.cu:128-191)
+  CK(rnet_k::gru_scan_bwd(dX_, a.z, a.h, a.P + D, 2 * D, w.bh, dPZH_, dPZH_ + D, 2 * D, g.bz,
+                          g.bh, B, T, D, s));
+  CK(gemm_tf32x3(s, N, D, 2 * D, kmaj(dPZH_, 2 * D), mnmaj(w.Wz, D), epi_store(dsub_, D), 0, 0, err));
+  CK(gemm_tf32x3(s, 2 * D, D, N, mnmaj(dPZH_, 2 * D), mnmaj(a.n2, D), epi_accum(g.Wz, D), 0, 0, err));
+  CK(rnet_k::rms_norm_bwd(dsub_, a.r1, w.n2, a.rinv2, dX_, g.n2, N, D, 1, s));
+  // 1. causal conv (:530-545, src/causal_conv.cu:132-190)
+  CK(gemm_tf32x3(s, N, D, D, kmaj(dX_, D), mnmaj(w.mix, D), epi_store(dS_, D), 0, 0, err));
+  CK(gemm_tf32x3(s, D, D, N, mnmaj(dX_, D), mnmaj(conv_quirk ? a.Sq : a.S, D),
+                 epi_accum(g.mix, D), 0, 0, err));
+  CK(rnet_k::conv_bwd(dS_, a.n1, w.c3, w.c7, w.c15, dsub_, g.c3, g.c7, g.c15, conv_parts_, B, T,
+                      D, 0, s));
+  CK(rnet_k::rms_norm_bwd(dsub_, Xl, w.n1, a.rinv1, dX_, g.n1, N, D, 1, s));
+  return RNET_OK;
+}
+
+int Engine::backward(const float* d_dlogits, const int* d_tokens, int B, int T) {
+  if (!have_cache_ || B != last_B_ || T != last_T_)
+    return rnet_status::fail(RNET_ERR_ARG,
+                             "backward: needs a preceding cached forward with the same B, T");
+  const int N = B * T;
+  int rc = head_backward(d_dlogits, N);
+  if (rc) return rc;
+  for (int l = cfg_.n_layers - 1; l >= 0; --l) {
+    rc = layer_backward(l, B, T);
+    if (rc) return rc;
+    if (dist) {
+      rc = dist_reduce_range(dist, grads_ + G_[l].offset, G_[l].count, stream_);
+      if (rc) return rc;
+    }
+  }
+  CK(rnet_k::embed_bwd(dX_, d_tokens, g_embed_, N, cfg_.vocab_size, cfg_.d_model, stream_));
+  if (dist) {
+    rc = dist_reduce_range(dist, grads_, 2 * (size_t)cfg_.vocab_size * cfg_.d_model + cfg_.d_model,
+                           stream_);
+    if (rc) return rc;
+  }
+  return RNET_OK;
+}
+
+int Engine::zero_grad() {
+  CK(cudaMemsetAsync(grads_, 0, P_ * sizeof(float), stream_));
+  return RNET_OK;
+}
+
+int Engine::step(float lr, float clip) {
+  int world = 1;
+  if (dist) {
+    int rc = dist_wait(dist, stream_);
+    if (rc) return rc;
+    world = dist_world(dist);
+  }
+  CK(rnet_k::sgd_clip_step(params_, grads_, P_, lr, clip, world, scratch_, norm_dev_, stream_));
+  return refresh_shadows();
+}
+
+int Engine::train_step(const int* d_in, const int* d_tgt, int B, int T, float lr, float clip,
+                       float* d_loss_sum) {
+  const int N = B * T, V = cfg_.vocab_size;
+  if (N > 64 * (cfg_.seq_len > 0 ? cfg_.seq_len : 256))
+    return rnet_status::fail(RNET_ERR_ARG, "train_step: batch*seq_len exceeds 64*seq_len");
+  int rc = zero_grad();
+  if (rc) return rc;
+  rc = ensure_capacity(N, true);
+  if (rc) return rc;
+  rc = forward(d_in, logits_, B, T);
+  if (rc) return rc;
+  CK(rnet_k::cross_entropy(logits_, d_tgt, d_loss_sum ? d_loss_sum : loss_dev_, dlogits_,
+                           1.0f / (float)N, conv_parts_, N, V, rnet_status::device_error_word(),
+                           stream_));
+  rc = backward(dlogits_, d_in, B, T);
+  if (rc) return rc;
+  return step(lr, clip);
+}
+
+int Engine::topk(int layer, int** idx, float** w) {
+  if (!have_cache_ || layer < 0 || layer >= cfg_.n_layers)
+    return rnet_status::fail(RNET_ERR_ARG, "topk: no cached forward or bad layer");
+  *idx = act_[layer].idx;
+  *w = act_[layer].w;
+  return RNET_OK;
+}
+
+// ------------------------------------------------------------------ checkpoint
+// Byte layout of the reference (src/resonance_net.cpp:743-782): the 40-byte
+// ModelConfig, then every tensor in order as raw fp32 — here one contiguous
+// write because the parameters already live in that order.
+int Engine::save(const char* path) {
+  std::vector<float> h(P_);
+  CK(cudaMemcpyAsync(h.data(), params_, P_ * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  FILE* f = fopen(path, "wb");
+  if (!f) return rnet_status::fail(RNET_ERR_IO, std::string("cannot open for write: ") + path);
+  bool ok = fwrite(&cfg_, sizeof(cfg_), 1, f) == 1;
+  ok = ok && fwrite(h.data(), sizeof(float), P_, f) == P_;
+  ok = (fclose(f) == 0) && ok;
+  if (!ok) return rnet_status::fail(RNET_ERR_IO, std::string("short write: ") + path);
+  return RNET_OK;
+}
+
+int Engine::load_weights(const char* path) {
+  FILE* f = fopen(path, "rb");
+  if (!f) return rnet_status::fail(RNET_ERR_IO, std::string("cannot open: ") + path);
+  rnet_model_config c;
+  if (fread(&c, sizeof(c), 1, f) != 1) {
+    fclose(f);
+    return rnet_status::fail(RNET_ERR_IO, "checkpoint: truncated header");
+  }
+  if (c.d_model != cfg_.d_model || c.n_layers != cfg_.n_layers || c.d_ff != cfg_.d_ff ||
+      c.n_slots != cfg_.n_slots || c.vocab_size != cfg_.vocab_size) {
+    fclose(f);
+    return rnet_status::fail(RNET_ERR_IO, "checkpoint: config does not match this model");
+  }
+  std::vector<float> h(P_);
+  const size_t got = fread(h.data(), sizeof(float), P_, f);
+  const bool extra = fgetc(f) != EOF;
+  fclose(f);
+  if (got != P_) return rnet_status::fail(RNET_ERR_IO, "checkpoint: truncated tensor data");
+  if (extra) return rnet_status::fail(RNET_ERR_IO, "checkpoint: trailing bytes after tensors");
+  return set_params_host(h.data(), P_);
+}
+
+}  // namespace rnet_engine

@@ -83,18 +83,18 @@ __device__ __forceinline__ float silu_fast(float g) { return g / (1.0f + __expf(
 
 // ------------------------------------------------------------------ epilogue
 template <int BN>
-__device__ __forceinline__ void store_row_chunk(const KParams& p, int row, int col0,
+__device__ __forceinline__ void store_row_chunk(const KParams& p, int kind, int row, int col0,
                                                 const float (&v)[32]) {
   const Epilogue& e = p.epi;
   if (row >= p.M) return;
   const float a = e.alpha;
   if (col0 + 32 <= p.N) {
-    if (e.kind == EPI_STORE) {
+    if (kind == EPI_STORE) {
       float4* dst = reinterpret_cast<float4*>(e.C + (size_t)row * e.ldc + col0);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         dst[j] = make_float4(a * v[4 * j], a * v[4 * j + 1], a * v[4 * j + 2], a * v[4 * j + 3]);
-    } else if (e.kind == EPI_ACCUM) {
+    } else if (kind == EPI_ACCUM) {
       float* dst = e.C + (size_t)row * e.ldc + col0;
 #pragma unroll
       for (int j = 0; j < 8; ++j)
@@ -116,8 +116,8 @@ __device__ __forceinline__ void store_row_chunk(const KParams& p, int row, int c
       const int col = col0 + i;
       if (col < p.N) {
         float* dst = e.C + (size_t)row * e.ldc + col;
-        if (e.kind == EPI_STORE) *dst = a * v[i];
-        else if (e.kind == EPI_ACCUM) atomicAdd(dst, a * v[i]);
+        if (kind == EPI_STORE) *dst = a * v[i];
+        else if (kind == EPI_ACCUM) atomicAdd(dst, a * v[i]);
         else *dst = e.R[(size_t)row * e.ldr + col] + a * v[i];
       }
     }
@@ -186,7 +186,7 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
     for (int c = 0; c < BN / 32; ++c) {
       tmem_ld_32cols(tacc + c * 32, v);
       const int s0 = nt * BN + c * 32;
-      if (e.C != nullptr && row < p.M) store_row_chunk<BN>(p, row, s0, v);
+      if (e.C != nullptr && row < p.M) store_row_chunk<BN>(p, EPI_STORE, row, s0, v);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int s = s0 + i;
@@ -214,7 +214,7 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
     tmem_ld_32cols(tacc + c * 32, v);
-    store_row_chunk<BN>(p, row, nt * BN + c * 32, v);
+    store_row_chunk<BN>(p, e.kind, row, nt * BN + c * 32, v);
   }
 }
 

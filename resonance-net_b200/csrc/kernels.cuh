@@ -1,0 +1,91 @@
+// Launchers of the non-GEMM ResonanceNet kernels (all sm_100a, fp32).
+// Every launcher is asynchronous on `s` and returns the launch status.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace rnet_k {
+
+// ---- RMSNorm (rms_norm.cu) ------------------------------------------------
+// y = x * rinv * w, rinv = rsqrt(mean(x^2) + eps)        (y may be null)
+cudaError_t rms_norm_fwd(const float* x, const float* w, float* y, float* rinv, int rows,
+                         int D, float eps, cudaStream_t s);
+// dx_norm = rinv*(dy*w - xhat*mean(dy*w*xhat)); dw += sum_rows dy*xhat.
+// mode 0: dx = dx_norm (overwrite); mode 1: dx += dx_norm (residual stream).
+cudaError_t rms_norm_bwd(const float* dy, const float* x, const float* w, const float* rinv,
+                         float* dx, float* dw, int rows, int D, int mode, cudaStream_t s);
+
+// ---- depthwise causal convolution (causal_conv.cu) -------------------------
+// c3/c7/c15 of x over each length-T sequence, S = c3 + c7 + c15.
+// Writes S; optionally Sq = S + c7 + c15 (reference dmix operand) and/or c7,
+// c15 individually (reference conv_buf layout).
+cudaError_t conv_fwd(const float* x, const float* w3, const float* w7, const float* w15,
+                     float* S, float* Sq, float* c7, float* c15, int B, int T, int D,
+                     cudaStream_t s);
+// dx (+)= sum_K conv_K^T(dS); dw_K[k] += sum x[t-(K-1)+k] dS[t].
+// accumulate: 0 -> dx = ..., 1 -> dx += ...
+// `partials` is scratch of conv_bwd_partials_floats(B, T, D) floats.
+size_t conv_bwd_partials_floats(int B, int T, int D);
+cudaError_t conv_bwd(const float* dS, const float* x, const float* w3, const float* w7,
+                     const float* w15, float* dx, float* dw3, float* dw7, float* dw15,
+                     float* partials, int B, int T, int D, int accumulate, cudaStream_t s);
+
+// ---- MinGRU scan (min_gru_scan.cu) ----------------------------------------
+// z = sigmoid(pz + bz), h~ = ph + bh, h_t = (1-z) h_{t-1} + z h~ (h_{-1} = 0).
+// pz/ph rows have stride ldp. Writes z, h; optional y = h (copy) and optional
+// residual out = res + h.
+cudaError_t gru_scan_fwd(const float* pz, const float* ph, int ldp, const float* bz,
+                         const float* bh, float* z, float* h, float* y, const float* res,
+                         float* out, int B, int T, int D, cudaStream_t s);
+// Reverse scan: dh_t = dy_t + (1 - z_{t+1}) dh_{t+1};
+// dz = dh (h~ - h_{t-1}) z (1-z), dh~ = dh z. h~ = ph + bh (ph stride ldp).
+// Writes dz/dh~ with row stride ldd (dh~ at column offset `dht_off`),
+// dbz += sum dz, dbh += sum dh~.
+cudaError_t gru_scan_bwd(const float* dy, const float* z, const float* h, const float* ph,
+                         int ldp, const float* bh, float* dz, float* dht, int ldd, float* dbz,
+                         float* dbh, int B, int T, int D, cudaStream_t s);
+
+// ---- slot memory (slot_memory.cu) -----------------------------------------
+// out[j*R + i] = in[i*C + j] (+ accumulate into out if acc)
+cudaError_t transpose(const float* in, float* out, int R, int C, int acc, cudaStream_t s);
+// r[n,:] = sum_j w[n,j] VT[idx[n,j], :]
+cudaError_t slot_gather(const int* idx, const float* w, const float* VT, float* r, int N,
+                        int D, int S, int k, unsigned* err, cudaStream_t s);
+// Sparse backward through top-k + softmax + gather (one warp per token):
+//   dwj = <dr, VT[idx_j]>, dsc_j = w_j (dwj - sum w dw), dq = sum dsc_j KT[idx_j]
+//   dVT[idx_j] += w_j dr, dKT[idx_j] += dsc_j q
+cudaError_t slot_sparse_bwd(const float* dr, const int* idx, const float* w, const float* VT,
+                            const float* KT, const float* q, float* dq, float* dVT, float* dKT,
+                            int N, int D, int S, int k, unsigned* err, cudaStream_t s);
+// Top-k (k <= 8) over a materialised score matrix, reference order semantics,
+// + softmax (used by the per-op API for k != 2).
+cudaError_t topk_rows(const float* scores, int* idx, float* w, int N, int S, int k,
+                      cudaStream_t s);
+
+// ---- embedding / loss / utilities (embed_loss.cu) -------------------------
+cudaError_t embed_fwd(const int* tok, const float* table, float* out, int N, int V, int D,
+                      unsigned* err, cudaStream_t s);
+cudaError_t embed_bwd(const float* dout, const int* tok, float* dtable, int N, int V, int D,
+                      cudaStream_t s);
+// loss_sum (overwritten) = sum_n -(log softmax(l_n)[t_n]); dl = (softmax - onehot)*scale.
+// `partials` scratch: ce_partials_floats(N) floats.
+size_t ce_partials_floats(int N);
+cudaError_t cross_entropy(const float* logits, const int* tgt, float* loss_sum, float* dl,
+                          float scale, float* partials, int N, int V, unsigned* err,
+                          cudaStream_t s);
+cudaError_t residual_add(float* x, const float* y, size_t n, cudaStream_t s);
+cudaError_t scale(float* x, float a, size_t n, cudaStream_t s);
+cudaError_t add3(const float* a, const float* b, const float* c, float* out, size_t n,
+                 cudaStream_t s);
+// h = g * sigmoid(g) * u   (reference silu_mul_kernel, src/swiglu_ffn.cu:11-21)
+cudaError_t silu_mul(const float* g, const float* u, float* h, size_t n, cudaStream_t s);
+
+// ---- optimizer (optimizer.cu) ---------------------------------------------
+// Global-norm clip + SGD over one flat buffer, no host synchronisation:
+//   lr_eff = lr/world * min(1, clip / (||g|| / world))   (if clip > 0)
+//   p -= lr_eff * g
+// `scratch` = sgd_scratch_floats() floats. norm_out (optional) gets ||g||.
+size_t sgd_scratch_floats();
+cudaError_t sgd_clip_step(float* params, const float* grads, size_t n, float lr, float clip,
+                          int world, float* scratch, float* norm_out, cudaStream_t s);
+
+}  // namespace rnet_k

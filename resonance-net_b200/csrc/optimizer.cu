@@ -1,0 +1,96 @@
+// Global-norm gradient clipping + SGD over the flat parameter buffer, entirely
+// on the device (no host round trip).
+//
+// Reference: src/resonance_net.cpp:551-663 — lr /= world_size under DDP,
+// ||g|| from one cublasSdot per tensor (each a host sync), clip against
+// ||g|| / world_size, then one cublasSaxpy(-lr) per tensor. Here: a fixed-grid
+// double-precision sum of squares, a single-block finalisation that computes
+// the effective learning rate on the device, and one vectorised update pass.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace rnet_k {
+
+namespace {
+
+constexpr int NORM_BLOCKS = 592;  // 4 x 148, fixed so the reduction order is fixed
+
+__global__ void sumsq_kernel(const float* __restrict__ g, size_t n, double* __restrict__ part) {
+  __shared__ double sh[256];
+  double a = 0.0;
+  const size_t n4 = n / 4;
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const float4 v = g4[i];
+    a += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+  }
+  if (blockIdx.x == 0)
+    for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) a += (double)g[i] * g[i];
+  sh[threadIdx.x] = a;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part[blockIdx.x] = sh[0];
+}
+
+__global__ void finalize_kernel(const double* __restrict__ part, int nparts, float lr,
+                                float clip, int world, float* __restrict__ lr_out,
+                                float* __restrict__ norm_out) {
+  __shared__ double sh[256];
+  double a = 0.0;
+  for (int i = threadIdx.x; i < nparts; i += 256) a += part[i];
+  sh[threadIdx.x] = a;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const double norm = sqrt(sh[0]);
+    float l = lr;
+    if (world > 1) l /= (float)world;
+    const double avg = norm / (world > 1 ? world : 1);
+    if (clip > 0.f && avg > clip) l = (float)(l * (clip / avg));
+    *lr_out = l;
+    if (norm_out) *norm_out = (float)norm;
+  }
+}
+
+__global__ void update_kernel(float* __restrict__ p, const float* __restrict__ g, size_t n,
+                              const float* __restrict__ lr_ptr) {
+  const float neg = -*lr_ptr;
+  const size_t n4 = n / 4;
+  float4* p4 = reinterpret_cast<float4*>(p);
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float4 a = p4[i];
+    const float4 b = g4[i];
+    a.x += neg * b.x; a.y += neg * b.y; a.z += neg * b.z; a.w += neg * b.w;
+    p4[i] = a;
+  }
+  if (blockIdx.x == 0)
+    for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) p[i] += neg * g[i];
+}
+
+}  // namespace
+
+size_t sgd_scratch_floats() { return 2 * NORM_BLOCKS + 8; }
+
+cudaError_t sgd_clip_step(float* params, const float* grads, size_t n, float lr, float clip,
+                          int world, float* scratch, float* norm_out, cudaStream_t s) {
+  if (!n) return cudaSuccess;
+  if ((reinterpret_cast<uintptr_t>(params) | reinterpret_cast<uintptr_t>(grads)) & 15)
+    return cudaErrorInvalidValue;
+  double* part = reinterpret_cast<double*>(scratch);
+  float* lr_dev = scratch + 2 * NORM_BLOCKS;
+  sumsq_kernel<<<NORM_BLOCKS, 256, 0, s>>>(grads, n, part);
+  finalize_kernel<<<1, 256, 0, s>>>(part, NORM_BLOCKS, lr, clip, world, lr_dev, norm_out);
+  update_kernel<<<148 * 8, 256, 0, s>>>(params, grads, n, lr_dev);
+  return cudaGetLastError();
+}
+
+}  // namespace rnet_k

@@ -1,0 +1,92 @@
+"""Whole-model parity on the GPU: one full training step of the CUDA engine
+(through the C ABI) against the CPU oracle and against the golden fixtures
+recorded from the reference's own CUDA build.
+
+Tolerance: fp32, 1e-4 relative (per tensor, see tests/helpers.py); top-2
+indices bit-exact as sets except tokens whose selection margin is < 1e-6.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from helpers import FP32_TOL, assert_close, assert_grads_close, rel_err, topk_sets_match
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+CASES = {
+    "cfg_tiny": dict(d_model=64, n_layers=1, d_ff=128, n_slots=64, top_k=2, vocab=256, B=2, T=32,
+                     pseed=1234, tseed=1),
+    "cfg_small": dict(d_model=64, n_layers=2, d_ff=128, n_slots=160, top_k=2, vocab=256, B=3,
+                      T=100, pseed=99, tseed=5),
+}
+
+
+def _run_engine(rnet, cuda, cfg, params, tok, tgt, B, T, lr=3e-4, clip=1.0):
+    torch = cuda
+    m = rnet.Model(cfg, device=0, reference_init=False)
+    m.set_params(params)
+    d_in = torch.from_numpy(tok.reshape(-1)).cuda()
+    d_tgt = torch.from_numpy(tgt.reshape(-1)).cuda()
+    loss = torch.zeros(1, device="cuda")
+    m.train_step(d_in, d_tgt, B, T, lr, clip, loss)
+    m.synchronize()
+    N = B * T
+    tk = [m.topk_host(l, N) for l in range(cfg.n_layers)]
+    out = dict(loss_sum=float(loss.item()), grads=m.get_grads(), params_after=m.get_params(),
+               topk_idx=np.stack([t[0] for t in tk]), topk_w=np.stack([t[1] for t in tk]))
+    m.close()
+    return out
+
+
+def _make(orc, rdata, c):
+    cfg = orc.make_config(c["d_model"], c["n_layers"], c["d_ff"], c["n_slots"], c["top_k"],
+                          c["vocab"], seq_len=c["T"])
+    params = rdata.init_params_normal(cfg, seed=c["pseed"])
+    tok, tgt = rdata.uniform_tokens(c["B"], c["T"], seed=c["tseed"])
+    return cfg, params, tok, tgt
+
+
+def _rcfg(rnet, cfg):
+    return rnet.ModelConfig(cfg.d_model, cfg.n_layers, cfg.d_ff, cfg.n_heads, cfg.gru_dim,
+                            cfg.n_slots, cfg.slot_top_k, cfg.vocab_size, cfg.seq_len, cfg.rms_eps)
+
+
+def _compare(cfg, rdata, ours, ref, params, margins, what):
+    assert abs(ours["loss_sum"] - ref["loss_sum"]) <= FP32_TOL * abs(ref["loss_sum"]), \
+        f"{what}: loss {ours['loss_sum']} vs {ref['loss_sum']}"
+    ok = topk_sets_match(ours["topk_idx"], ref["topk_idx"], margins)
+    assert ok.all(), f"{what}: top-k index sets differ on {(~ok).sum()} tokens"
+    assert_grads_close(cfg, ours["grads"], ref["grads"], rdata.tensor_layout, what=what + " grads")
+    d_ours = ours["params_after"].astype(np.float64) - params
+    d_ref = ref["params_after"].astype(np.float64) - params
+    assert rel_err(d_ours, d_ref) <= FP32_TOL, f"{what}: SGD update rel {rel_err(d_ours, d_ref):.3e}"
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_train_step_vs_oracle(case, rnet, rdata, orc, cuda):
+    c = CASES[case]
+    cfg, params, tok, tgt = _make(orc, rdata, c)
+    ours = _run_engine(rnet, cuda, _rcfg(rnet, cfg), params, tok, tgt, c["B"], c["T"])
+    ref = orc.train_step(cfg, params, tok, tgt, c["B"], c["T"], 3e-4, 1.0, quirk=1)
+    margins = orc.topk_margins(cfg, params, tok, c["B"], c["T"])
+    _compare(cfg, rdata, ours, ref, params.astype(np.float64), margins, f"{case} vs oracle")
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_train_step_vs_reference_golden(case, rnet, rdata, orc, cuda):
+    path = os.path.join(GOLDEN, f"{case}.npz")
+    if not os.path.exists(path):
+        pytest.skip("golden fixture not generated")
+    g = np.load(path)
+    c = CASES[case]
+    cfg, params, tok, tgt = _make(orc, rdata, c)
+    np.testing.assert_array_equal(params, g["params"])
+    np.testing.assert_array_equal(tok, g["tokens"])
+    ours = _run_engine(rnet, cuda, _rcfg(rnet, cfg), params, tok, tgt, c["B"], c["T"])
+    ref = {k: g[k] for k in ("grads", "params_after", "topk_idx", "topk_w")}
+    ref["loss_sum"] = float(g["loss_sum"])
+    margins = orc.topk_margins(cfg, params, tok, c["B"], c["T"])
+    _compare(cfg, rdata, ours, ref, params.astype(np.float64), margins, f"{case} vs reference")
