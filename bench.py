@@ -1,0 +1,372 @@
+#!/usr/bin/env python
+"""ResonanceNet training-step benchmark on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 is launched by torchrun (RANK / LOCAL_RANK / WORLD_SIZE / MASTER_* from
+the environment); the library's own NCCL communicator all-reduces gradient
+buckets during backward, torch.distributed is only used for the barrier, the
+max-over-ranks timing reduction and the NCCL id broadcast.
+
+Workload: d_model 512, 8 layers, d_ff 1024, 1024 slots,
+top-2, vocab 256, fp32; per GPU batch 64 x seq 256 of synthetic Zipf(1.1)
+byte tokens (a pool of 8 batches per rank, seed 7 + rank), weights N(0, 0.02)
+(seed 1234). One step = zero_grad + forward + cross-entropy + backward
+(+ bucketed all-reduce) + clipped SGD. Prints ONE JSON line on rank 0.
+
+--impl reference times the reference's own CUDA implementation
+(oracle/_ref/libref.so: its sources compiled unmodified for sm_100a) through
+its ResonanceNet class on the same config and data, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "train tok/s (d512 L8 B64 T256)"
+UNIT = "tok/s"
+CFG = dict(d_model=512, n_layers=8, d_ff=1024, n_slots=1024, top_k=2, vocab=256, seq_len=256)
+LR, CLIP = 3e-4, 1.0
+POOL = 8
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--seq", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", os.environ.get("RANK", 0))))
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return dict(hbm=p["hbm_gbs"], bf16=p["bf16_tflops"],
+                    bf16_sust=p.get("bf16_tflops_sustained", p["bf16_tflops"]), src="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sust=1400.0, src="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return float("nan")
+        sm = [num(r[1]) for r in rows]
+        mx = max(num(r[2]) for r in rows)
+        loaded = [s for s in sm if s > 0.5 * mx] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return dict(sm_mhz=statistics.median(loaded), sm_max_mhz=mx, reasons=reasons,
+                    samples=len(rows), power_w_max=max(num(r[3]) for r in rows))
+
+
+def zipf_pool(rdata, B, T, seed):
+    toks, tgts = [], []
+    for i in range(POOL):
+        a, b = rdata.zipf_tokens(B, T, seed=seed * 1000 + i)
+        toks.append(a.reshape(-1))
+        tgts.append(b.reshape(-1))
+    return toks, tgts
+
+
+def cpu_baseline(rdata):
+    """The CPU oracle (scalar C++/OpenMP restatement of the reference math),
+    one full training step of the config-2 model on a bounded sample."""
+    import numpy as np
+    import oracle
+    cfg = oracle.make_config(**CFG)
+    params = rdata.init_params_normal(cfg, seed=1234)
+    B, T = 1, 256
+    tok, tgt = rdata.zipf_tokens(B, T, seed=7)
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    oracle.train_step(cfg, params, tok[:, :32], tgt[:, :32], 1, 32)  # warm the pool
+    t0 = time.perf_counter()
+    oracle.train_step(cfg, params, tok, tgt, B, T, LR, CLIP)
+    dt = time.perf_counter() - t0
+    return dict(value=B * T / dt, unit=UNIT, cores=threads, kind="port",
+                sample=f"one full train step (fwd+bwd+SGD) of the d512/L8 model on B=1 x T=256 "
+                       f"Zipf tokens ({dt:.1f} s, {threads} OpenMP threads)")
+
+
+def run_ours(args, rank, world, local):
+    import numpy as np
+    import torch
+    rnet = importlib.import_module("resonance-net_b200")
+    rdata = importlib.import_module("resonance-net_b200.data")
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        pg = dist
+    B, T = args.batch, args.seq
+    cfg = rnet.ModelConfig.make(d_model=CFG["d_model"], n_layers=CFG["n_layers"],
+                                d_ff=CFG["d_ff"], n_slots=CFG["n_slots"], top_k=CFG["top_k"],
+                                vocab=CFG["vocab"], seq_len=CFG["seq_len"])
+    model = rnet.Model(cfg, device=local, reference_init=False)
+    model.set_params(rdata.init_params_normal(cfg, seed=1234))
+    dist_h = None
+    if world > 1:
+        uid = [rnet.Dist.unique_id() if rank == 0 else None]
+        pg.broadcast_object_list(uid, src=0)
+        dist_h = rnet.Dist(rank, world, local, uid[0])
+        model.set_dist(dist_h)
+    toks, tgts = zipf_pool(rdata, B, T, seed=7 + rank)
+    d_in = [torch.from_numpy(t).cuda() for t in toks]
+    d_tg = [torch.from_numpy(t).cuda() for t in tgts]
+    h_in = [torch.from_numpy(t).pin_memory() for t in toks]
+    h_tg = [torch.from_numpy(t).pin_memory() for t in tgts]
+    d_loss = torch.zeros(1, device="cuda")
+    stream = torch.cuda.ExternalStream(model.stream())
+
+    def barrier():
+        torch.cuda.synchronize()
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if not pg:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(args.warmup):
+        model.train_step(d_in[i % POOL], d_tg[i % POOL], B, T, LR, CLIP, d_loss)
+    model.synchronize()
+
+    # ---- device-resident timed region (value) ------------------------------
+    clocks = ClockSampler(local)
+    barrier()
+    clocks.start()
+    n0 = rnet.kernel_launches()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        model.train_step(d_in[i % POOL], d_tg[i % POOL], B, T, LR, CLIP, d_loss)
+    ev1.record(stream)
+    ev1.synchronize()
+    launches = rnet.kernel_launches() - n0
+    barrier()
+    ck = clocks.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    model.synchronize()
+    loss = float(d_loss.item()) / (B * T)
+
+    # ---- the same steps again with per-kernel-class CUDA events (roofline) -
+    barrier()
+    model.profile_enable(True)
+    model.profile_read(reset=True)
+    for i in range(args.steps):
+        model.train_step(d_in[i % POOL], d_tg[i % POOL], B, T, LR, CLIP, d_loss)
+    prof = model.profile_read(reset=True)
+    model.profile_enable(False)
+    barrier()
+
+    # ---- end-to-end through the public API with host buffers (e2e) --------
+    barrier()
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev2.record(stream)
+    for i in range(args.steps):
+        model.train_step_host(h_in[i % POOL].numpy(), h_tg[i % POOL].numpy(), B, T, LR, CLIP)
+    ev3.record(stream)
+    ev3.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(ev2.elapsed_time(ev3))
+
+    if rank != 0:
+        _finish(pg, model, dist_h)
+        return
+    tokens = world * B * T * args.steps
+    peaks = measured_peaks()
+    g = prof["gemm"]
+    gemm_tflops = g["flops"] / (g["ms"] * 1e-3) / 1e12 if g["ms"] > 0 else 0.0
+    per_launch_ms = g["ms"] / max(1, g["launches"])
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "gemm_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    kernels = {}
+    for k, v in prof.items():
+        if v["launches"]:
+            kernels[k] = dict(ms_per_step=round(v["ms"] / args.steps, 4),
+                              share=round(v["ms"] / max(1e-9, sum(x["ms"] for x in prof.values())), 4))
+            if v["ms"] > 0 and v["bytes"] > 0 and k != "gemm":
+                kernels[k]["GBps"] = round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1)
+                kernels[k]["hbm_frac"] = round(kernels[k]["GBps"] / peaks["hbm"], 3)
+    out = {
+        "metric": METRIC, "value": round(tokens / (ms * 1e-3), 1), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (3xTF32 tcgen05)",
+        "data": "synthetic Zipf(1.1) byte tokens, N(0,0.02) weights",
+        "config": {"workload": "train step, d512 L8 F1024 S1024 top2 V256", "model": "ResonanceNet",
+                   "global_batch": world * B, "seq_len": T, "parallelism": f"dp{world}",
+                   "per_gpu_batch": B, "l2": "working set per step ~6.5 GB >> 126 MB L2 (no flush)"},
+        "e2e": {"value": round(tokens / (ms_e2e * 1e-3), 1), "unit": UNIT,
+                "h2d_bytes_per_step": 2 * B * T * 4, "d2h_bytes_per_step": 4},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "kernel": "gemm_tf32x3 (all GEMMs of the step)",
+                     "achieved": round(gemm_tflops, 2), "peak": peaks["bf16_sust"],
+                     "unit": "TFLOP/s", "frac": round(gemm_tflops / peaks["bf16_sust"], 4),
+                     "peak_src": f"{peaks['src']} bf16 dense, sustained",
+                     "ceiling_3xtf32": round(peaks["bf16_sust"] / 6, 1),
+                     "frac_of_3xtf32_ceiling": round(gemm_tflops / (peaks["bf16_sust"] / 6), 4),
+                     "ms_per_launch": round(per_launch_ms, 4), "traffic": traffic},
+        "kernels": kernels, "loss": round(loss, 4),
+        "clocks": ck,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(importlib.import_module("resonance-net_b200.data"))
+    print(json.dumps(out), flush=True)
+    _finish(pg, model, dist_h)
+
+
+def _finish(pg, model, dist_h):
+    model.synchronize()
+    model.close()
+    if dist_h:
+        dist_h.close()
+    if pg:
+        pg.destroy_process_group()
+
+
+def run_reference(args, rank, world, local):
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    import oracle
+    rdata = importlib.import_module("resonance-net_b200.data")
+    base = {"impl": "reference", "metric": METRIC, "unit": UNIT}
+    if not oracle.ref_available():
+        print(json.dumps({**base, "unavailable": "oracle/_ref/libref.so (reference CUDA build) "
+                                                 "not built"}), flush=True)
+        return
+    torch.cuda.set_device(local)
+    B, T = args.batch, args.seq
+    cfg = oracle.make_config(**CFG)
+    R = oracle.ref_lib()
+    fd, path = tempfile.mkstemp(suffix=".bin")
+    os.close(fd)
+    rdata.write_checkpoint(path, cfg, rdata.init_params_normal(cfg, seed=1234))
+    saved = os.dup(1)
+    os.dup2(2, 1)  # the reference prints to stdout; keep ours to one JSON line
+    try:
+        h = R.ref_model_load(path.encode())
+        toks, tgts = zipf_pool(rdata, B, T, seed=7)
+        d_in = [torch.from_numpy(t).cuda() for t in toks]
+        d_tg = [torch.from_numpy(t).cuda() for t in tgts]
+        for i in range(args.warmup):
+            R.ref_train_step_device(h, d_in[i % POOL].data_ptr(), d_tg[i % POOL].data_ptr(), B, T,
+                                    ctypes.c_float(LR), ctypes.c_float(CLIP))
+        torch.cuda.synchronize()
+        clocks = ClockSampler(local)
+        clocks.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            R.ref_train_step_device(h, d_in[i % POOL].data_ptr(), d_tg[i % POOL].data_ptr(), B, T,
+                                    ctypes.c_float(LR), ctypes.c_float(CLIP))
+        e1.record()
+        torch.cuda.synchronize()
+        ck = clocks.stop()
+        ms = e0.elapsed_time(e1)
+        R.ref_model_destroy(h)
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+        os.unlink(path)
+    v = round(B * T * args.steps / (ms * 1e-3), 1)
+    out = {**base, "value": v, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "fp32 (cuBLAS SGEMM)",
+           "data": "synthetic Zipf(1.1) byte tokens, N(0,0.02) weights",
+           "config": {"workload": "train step, d512 L8 F1024 S1024 top2 V256",
+                      "model": "ResonanceNet", "global_batch": B, "seq_len": T,
+                      "parallelism": "dp1"},
+           "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "cpu_baseline": {"value": v, "unit": UNIT, "cores": None, "kind": "reference",
+                            "sample": "the reference has no CPU implementation; this is its own "
+                                      "CUDA build (unmodified sources, sm_100a) timed on the "
+                                      "same B200, full config"},
+           "clocks": ck}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = env_rank()
+    if args.impl == "reference":
+        run_reference(args, rank, world, local)
+    else:
+        run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -36,6 +36,9 @@ const char* rnet_last_error(void);
 /* Library ABI version (major*100 + minor). */
 int rnet_abi_version(void);
 
+/* Number of CUDA kernels this library has launched in this process. */
+int rnet_kernel_launches(unsigned long long* n);
+
 /* Read (and optionally clear) the device error word of the current device:
  * bit 0 = a bounded wait timed out, bit 1 = out-of-range index seen,
  * bit 2 = TMEM allocation failed. Synchronises the device. */
@@ -172,6 +175,39 @@ int rnet_model_load_weights(rnet_model* m, const char* path);
 /* Wait for the model stream and report any device error word bits. */
 int rnet_model_synchronize(rnet_model* m);
 
+/* Per-kernel-class timing with CUDA events on the model stream. Classes
+ * (index order): gemm, scan_fwd, scan_bwd, conv_fwd, conv_bwd, rms_fwd,
+ * rms_bwd, slot_gather, slot_sparse_bwd, embed, cross_entropy, sgd, other.
+ * read() fills arrays of n_kinds entries: total ms, algorithmic FLOPs and
+ * bytes, number of timed launch groups; reset clears the record. */
+#define RNET_PROFILE_KINDS 13
+int rnet_model_profile_enable(rnet_model* m, int on);
+int rnet_model_profile_read(rnet_model* m, double* ms, double* flops, double* bytes,
+                            long long* launches, int n_kinds, int reset);
+
+/* ------------------------------------------------------------------ decode
+ * Recurrent inference with the O(1) per-stream state (per layer: the last 14
+ * causal-conv inputs and the MinGRU h; 15 * d_model floats per layer per
+ * stream). n_streams advance in lock step. The reference has no counterpart
+ * (its `generate()` is declared, never defined; `infer` recomputes the whole
+ * prefix per token). */
+typedef struct rnet_decoder rnet_decoder;
+int rnet_decoder_create(rnet_model* m, int n_streams, rnet_decoder** out);
+int rnet_decoder_destroy(rnet_decoder* d);
+/* d_tokens [n_streams, seq_len] (device). Runs the chunked-scan forward and
+ * keeps the state; the last-position logits / argmax become available. */
+int rnet_decoder_prefill(rnet_decoder* d, const int* d_tokens, int seq_len);
+/* One token per stream: d_tokens [n_streams] (device) or NULL to feed back
+ * the previous argmax. */
+int rnet_decoder_step(rnet_decoder* d, const int* d_tokens);
+/* n_steps greedy steps (fed back on the device); d_out [n_steps, n_streams]
+ * (device, may be NULL). use_graph = 1 replays one captured CUDA graph per step. */
+int rnet_decoder_generate(rnet_decoder* d, int n_steps, int* d_out, int use_graph);
+/* Device pointers to the current logits [n_streams, vocab] and next tokens
+ * [n_streams], and the state buffer with its size per stream in floats. */
+int rnet_decoder_outputs(rnet_decoder* d, const float** d_logits, const int** d_next);
+int rnet_decoder_state(rnet_decoder* d, float** d_state, size_t* floats_per_stream);
+
 /* ------------------------------------------------------------------ data parallel
  * The reference's include/dist.h:12-36 over NCCL (loaded at run time). */
 int rnet_dist_unique_id(unsigned char uid[128]);
@@ -179,6 +215,14 @@ int rnet_dist_create(int rank, int world, int local_rank, const unsigned char ui
                      int timeout_ms, rnet_dist** out);
 int rnet_dist_destroy(rnet_dist* d);
 int rnet_dist_allreduce_sum(rnet_dist* d, float* d_buf, size_t count, void* stream);
+int rnet_dist_group_start(rnet_dist* d);
+int rnet_dist_group_end(rnet_dist* d);
+/* File rendezvous of the 128-byte unique id (reference src/dist.cpp:53-93):
+ * write = write "<path>.tmp" then rename (readers never see a partial file);
+ * read = poll until a complete file appears, RNET_ERR_TIMEOUT after
+ * timeout_ms, RNET_ERR_IO on a short/unreadable file. Host only. */
+int rnet_dist_uid_file_write(const char* path, const unsigned char uid[128]);
+int rnet_dist_uid_file_read(const char* path, int timeout_ms, unsigned char uid[128]);
 /* Attach (or detach with NULL): backward then all-reduces gradient buckets
  * as they complete and step() uses the reference's world-size scaling. */
 int rnet_model_set_dist(rnet_model* m, rnet_dist* d);

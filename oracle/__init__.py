@@ -99,8 +99,8 @@ def train_step(cfg, params, tokens, targets, B, T, lr=3e-4, clip=1.0, quirk=1):
     lib().orc_train_step(ctypes.byref(cfg), ptr(params), ptr(grads), ptr(tok), ptr(tgt), B, T,
                          _F(lr), _F(clip), quirk, ctypes.byref(loss), ptr(idx), ptr(w),
                          ptr(logits))
-    return dict(loss_sum=loss.value, grads=grads, params=params, topk_idx=idx, topk_w=w,
-                logits=logits)
+    return dict(loss_sum=loss.value, grads=grads, params=params, params_after=params,
+                topk_idx=idx, topk_w=w, logits=logits)
 
 
 def forward(cfg, params, tokens, B, T):

@@ -85,10 +85,24 @@ _SIGS = {
     "rnet_model_save": [_P, ctypes.c_char_p],
     "rnet_model_load_weights": [_P, ctypes.c_char_p],
     "rnet_model_synchronize": [_P],
+    "rnet_model_profile_enable": [_P, _I],
+    "rnet_model_profile_read": [_P, _P, _P, _P, _P, _I, _I],
+    "rnet_kernel_launches": [ctypes.POINTER(ctypes.c_ulonglong)],
+    "rnet_decoder_create": [_P, _I, ctypes.POINTER(_P)],
+    "rnet_decoder_destroy": [_P],
+    "rnet_decoder_prefill": [_P, _P, _I],
+    "rnet_decoder_step": [_P, _P],
+    "rnet_decoder_generate": [_P, _I, _P, _I],
+    "rnet_decoder_outputs": [_P, ctypes.POINTER(_P), ctypes.POINTER(_P)],
+    "rnet_decoder_state": [_P, ctypes.POINTER(_P), ctypes.POINTER(_SZ)],
     "rnet_dist_unique_id": [ctypes.c_char_p],
     "rnet_dist_create": [_I, _I, _I, ctypes.c_char_p, _I, ctypes.POINTER(_P)],
     "rnet_dist_destroy": [_P],
     "rnet_dist_allreduce_sum": [_P, _P, _SZ, _P],
+    "rnet_dist_group_start": [_P],
+    "rnet_dist_group_end": [_P],
+    "rnet_dist_uid_file_write": [ctypes.c_char_p, ctypes.c_char_p],
+    "rnet_dist_uid_file_read": [ctypes.c_char_p, _I, ctypes.c_char_p],
     "rnet_model_set_dist": [_P, _P],
 }
 
@@ -256,8 +270,62 @@ class Model:
     def synchronize(self) -> None:
         check(lib().rnet_model_synchronize(self._h))
 
+    def profile_enable(self, on: bool = True) -> None:
+        check(lib().rnet_model_profile_enable(self._h, int(on)))
+
+    def profile_read(self, reset: bool = True) -> dict:
+        """{kind: {ms, flops, bytes, launches}} of the timed launch groups."""
+        import numpy as np
+        n = len(PROFILE_KINDS)
+        ms, fl, by = (np.zeros(n, np.float64) for _ in range(3))
+        la = np.zeros(n, np.int64)
+        check(lib().rnet_model_profile_read(self._h, _ptr(ms), _ptr(fl), _ptr(by), _ptr(la), n,
+                                            int(reset)))
+        return {k: dict(ms=float(ms[i]), flops=float(fl[i]), bytes=float(by[i]),
+                        launches=int(la[i])) for i, k in enumerate(PROFILE_KINDS)}
+
     def set_dist(self, dist: Optional["Dist"]) -> None:
         check(lib().rnet_model_set_dist(self._h, dist.handle if dist else _P(0)))
+
+
+class Decoder:
+    """Batched recurrent decoder over a Model (n_streams in lock step)."""
+
+    def __init__(self, model: Model, n_streams: int):
+        self.model = model
+        self.M = n_streams
+        self.handle = _P()
+        check(lib().rnet_decoder_create(model.handle, n_streams, ctypes.byref(self.handle)))
+
+    def prefill(self, d_tokens, seq_len: int) -> None:
+        check(lib().rnet_decoder_prefill(self.handle, _ptr(d_tokens), seq_len))
+
+    def step(self, d_tokens=None) -> None:
+        check(lib().rnet_decoder_step(self.handle, _ptr(d_tokens)))
+
+    def generate(self, n_steps: int, d_out=None, use_graph: bool = True) -> None:
+        check(lib().rnet_decoder_generate(self.handle, n_steps, _ptr(d_out), int(use_graph)))
+
+    def outputs(self) -> tuple[int, int]:
+        lg, nx = _P(), _P()
+        check(lib().rnet_decoder_outputs(self.handle, ctypes.byref(lg), ctypes.byref(nx)))
+        return lg.value, nx.value
+
+    def state(self) -> tuple[int, int]:
+        p, n = _P(), _SZ()
+        check(lib().rnet_decoder_state(self.handle, ctypes.byref(p), ctypes.byref(n)))
+        return p.value, n.value
+
+    def close(self) -> None:
+        if self.handle:
+            lib().rnet_decoder_destroy(self.handle)
+            self.handle = _P()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Dist:
@@ -284,6 +352,16 @@ class Dist:
         if self.handle:
             lib().rnet_dist_destroy(self.handle)
             self.handle = _P()
+
+
+PROFILE_KINDS = ("gemm", "scan_fwd", "scan_bwd", "conv_fwd", "conv_bwd", "rms_fwd", "rms_bwd",
+                 "slot_gather", "slot_sparse_bwd", "embed", "cross_entropy", "sgd", "other")
+
+
+def kernel_launches() -> int:
+    n = ctypes.c_ulonglong(0)
+    check(lib().rnet_kernel_launches(ctypes.byref(n)))
+    return n.value
 
 
 def device_error(clear: bool = True) -> int:

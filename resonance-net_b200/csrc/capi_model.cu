@@ -1,6 +1,11 @@
 // C-ABI of the model engine and of the data-parallel plumbing.
+#include <sys/stat.h>
+
+#include <chrono>
 #include <cstdio>
 #include <new>
+#include <string>
+#include <thread>
 
 #include "dist.h"
 #include "engine.h"
@@ -19,6 +24,11 @@ struct rnet_model {
 
 struct rnet_dist {
   rnet_engine::DistComm* c = nullptr;
+};
+
+struct rnet_decoder {
+  rnet_model* m = nullptr;
+  rnet_engine::Decoder d;
 };
 
 #define CHECK_M(m)                                                      \
@@ -226,6 +236,80 @@ int rnet_model_synchronize(rnet_model* m) {
   return RNET_OK;
 }
 
+int rnet_decoder_create(rnet_model* m, int n_streams, rnet_decoder** out) {
+  CHECK_M(m);
+  if (!out) return rnet_status::fail(RNET_ERR_ARG, "null output");
+  *out = nullptr;
+  rnet_decoder* d = new rnet_decoder();
+  d->m = m;
+  int rc = m->e->decoder_init(&d->d, n_streams);
+  if (rc) {
+    delete d;
+    return rc;
+  }
+  *out = d;
+  return RNET_OK;
+}
+
+int rnet_decoder_destroy(rnet_decoder* d) {
+  if (!d) return RNET_OK;
+  d->m->e->decoder_free(&d->d);
+  delete d;
+  return RNET_OK;
+}
+
+int rnet_decoder_prefill(rnet_decoder* d, const int* d_tokens, int seq_len) {
+  if (!d || !d_tokens) return rnet_status::fail(RNET_ERR_ARG, "null argument");
+  return d->m->e->prefill(&d->d, d_tokens, seq_len);
+}
+
+int rnet_decoder_step(rnet_decoder* d, const int* d_tokens) {
+  if (!d) return rnet_status::fail(RNET_ERR_ARG, "null decoder");
+  return d->m->e->decode_step(&d->d, d_tokens);
+}
+
+int rnet_decoder_generate(rnet_decoder* d, int n_steps, int* d_out, int use_graph) {
+  if (!d || n_steps < 0) return rnet_status::fail(RNET_ERR_ARG, "bad argument");
+  return d->m->e->generate(&d->d, n_steps, d_out, use_graph != 0);
+}
+
+int rnet_decoder_outputs(rnet_decoder* d, const float** d_logits, const int** d_next) {
+  if (!d) return rnet_status::fail(RNET_ERR_ARG, "null decoder");
+  if (d_logits) *d_logits = d->d.logits;
+  if (d_next) *d_next = d->d.tok;
+  return RNET_OK;
+}
+
+int rnet_decoder_state(rnet_decoder* d, float** d_state, size_t* floats_per_stream) {
+  if (!d) return rnet_status::fail(RNET_ERR_ARG, "null decoder");
+  if (d_state) *d_state = d->d.state;
+  if (floats_per_stream)
+    *floats_per_stream = d->d.floats_per_layer / d->d.M * d->m->e->config().n_layers;
+  return RNET_OK;
+}
+
+int rnet_model_profile_enable(rnet_model* m, int on) {
+  CHECK_M(m);
+  m->e->profile_enable(on != 0);
+  return RNET_OK;
+}
+
+int rnet_model_profile_read(rnet_model* m, double* ms, double* flops, double* bytes,
+                            long long* launches, int n_kinds, int reset) {
+  CHECK_M(m);
+  rnet_engine::ProfStats st;
+  int rc = m->e->profile_read(&st, reset != 0);
+  if (rc) return rc;
+  const int n = n_kinds < rnet_engine::PK_COUNT ? n_kinds : rnet_engine::PK_COUNT;
+  for (int i = 0; i < n; ++i) {
+    if (ms) ms[i] = st.ms[i];
+    if (flops) flops[i] = st.flops[i];
+    if (bytes) bytes[i] = st.bytes[i];
+    if (launches) launches[i] = st.launches[i];
+  }
+  return RNET_OK;
+}
+
 int rnet_dist_unique_id(unsigned char uid[128]) {
   if (!uid) return rnet_status::fail(RNET_ERR_ARG, "null uid");
   return rnet_engine::dist_unique_id(uid);
@@ -252,6 +336,39 @@ int rnet_dist_destroy(rnet_dist* d) {
 int rnet_dist_allreduce_sum(rnet_dist* d, float* d_buf, size_t count, void* stream) {
   if (!d) return RNET_OK;  // inactive: no-op, like the reference
   return rnet_engine::dist_allreduce_on(d->c, d_buf, count, (cudaStream_t)stream);
+}
+
+int rnet_dist_group_start(rnet_dist* d) { return d ? rnet_engine::dist_group_start(d->c) : 0; }
+int rnet_dist_group_end(rnet_dist* d) { return d ? rnet_engine::dist_group_end(d->c) : 0; }
+
+int rnet_dist_uid_file_write(const char* path, const unsigned char uid[128]) {
+  if (!path || !uid) return rnet_status::fail(RNET_ERR_ARG, "null argument");
+  const std::string tmp = std::string(path) + ".tmp";
+  FILE* f = fopen(tmp.c_str(), "wb");
+  if (!f) return rnet_status::fail(RNET_ERR_IO, "cannot write " + tmp);
+  const bool ok = fwrite(uid, 1, 128, f) == 128;
+  if (fclose(f) != 0 || !ok) return rnet_status::fail(RNET_ERR_IO, "short write " + tmp);
+  if (std::rename(tmp.c_str(), path) != 0)
+    return rnet_status::fail(RNET_ERR_IO, std::string("rename to ") + path + " failed");
+  return RNET_OK;
+}
+
+int rnet_dist_uid_file_read(const char* path, int timeout_ms, unsigned char uid[128]) {
+  if (!path || !uid) return rnet_status::fail(RNET_ERR_ARG, "null argument");
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    struct stat sb;
+    if (stat(path, &sb) == 0 && sb.st_size >= 128) break;
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms))
+      return rnet_status::fail(RNET_ERR_TIMEOUT, std::string("timeout waiting for ") + path);
+    std::this_thread::sleep_for(std::chrono::milliseconds(20));
+  }
+  FILE* f = fopen(path, "rb");
+  if (!f) return rnet_status::fail(RNET_ERR_IO, std::string("cannot read ") + path);
+  const bool ok = fread(uid, 1, 128, f) == 128;
+  fclose(f);
+  if (!ok) return rnet_status::fail(RNET_ERR_IO, std::string("short uid file ") + path);
+  return RNET_OK;
 }
 
 int rnet_model_set_dist(rnet_model* m, rnet_dist* d) {

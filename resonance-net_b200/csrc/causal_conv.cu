@@ -165,7 +165,7 @@ cudaError_t conv_fwd(const float* x, const float* w3, const float* w7, const flo
   const int nchunks = (T + TC - 1) / TC;
   dim3 grid((D + CPB - 1) / CPB, B * nchunks);
   conv_fwd_kernel<<<grid, CPB, 0, s>>>(x, w3, w7, w15, S, Sq, c7, c15, T, D, nchunks);
-  return cudaGetLastError();
+  return launched();
 }
 
 size_t conv_bwd_partials_floats(int B, int T, int D) {
@@ -184,7 +184,7 @@ cudaError_t conv_bwd(const float* dS, const float* x, const float* w3, const flo
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   conv_wgrad_reduce<<<(25 * D + 255) / 256, 256, 0, s>>>(partials, np, D, dw3, dw7, dw15);
-  return cudaGetLastError();
+  return launched(2);
 }
 
 }  // namespace rnet_k

@@ -1,0 +1,152 @@
+// Kernels of the recurrent (O(1)-state) decode path.
+//
+// The reference has no decode path: its `infer` re-runs the whole prefix for
+// every token at batch 1 (src/main.cpp:316-325) and `generate()` is declared
+// but never defined (include/resonance_net.h:82-83). The state that makes a
+// single-token step exact is, per layer and stream: the last 14 inputs of the
+// causal convolutions (a ring indexed by position mod 14) and the MinGRU h.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace rnet_k {
+using namespace rnet_dev;
+
+namespace {
+
+constexpr int RING = 14;
+
+// S = c3 + c7 + c15 of the current input row n[m] and the ring of the 14
+// previous rows; then the current row is written into the ring at pos % 14.
+// Positions before the start of the sequence contribute zero (the ring is
+// zero-initialised / filled by prefill).
+__global__ void decode_conv_kernel(const float* __restrict__ n, float* __restrict__ ring,
+                                   const int* __restrict__ pos_ptr, const float* __restrict__ w3,
+                                   const float* __restrict__ w7, const float* __restrict__ w15,
+                                   float* __restrict__ S, int M, int D) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * D) return;
+  const int m = i / D, d = i % D;
+  const int pos = *pos_ptr;
+  float* rg = ring + (size_t)m * RING * D + d;
+  // win[o] = x[pos - o], o = 0..14
+  float win[RING + 1];
+  win[0] = n[i];
+#pragma unroll
+  for (int o = 1; o <= RING; ++o) {
+    const int t = pos - o;
+    win[o] = t >= 0 ? rg[(size_t)(t % RING) * D] : 0.f;
+  }
+  // same per-scale order as the training kernel: sum over taps k ascending,
+  // tap k reads x[t - (K-1) + k] = win[K-1-k]
+  float s3 = 0.f, s7 = 0.f, s15 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 3; ++k) s3 += win[2 - k] * w3[k * D + d];
+#pragma unroll
+  for (int k = 0; k < 7; ++k) s7 += win[6 - k] * w7[k * D + d];
+#pragma unroll
+  for (int k = 0; k < 15; ++k) s15 += win[14 - k] * w15[k * D + d];
+  S[i] = s3 + s7 + s15;
+  rg[(size_t)(pos % RING) * D] = win[0];
+}
+
+// h = (1 - z) h + z h~, z = sigmoid(pz + bz), h~ = ph + bh; x += h.
+__global__ void decode_gru_kernel(const float* __restrict__ P, const float* __restrict__ bz,
+                                  const float* __restrict__ bh, float* __restrict__ h,
+                                  float* __restrict__ x, int M, int D) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * D) return;
+  const int m = i / D, d = i % D;
+  const float z = 1.0f / (1.0f + __expf(-(P[(size_t)m * 2 * D + d] + bz[d])));
+  const float ht = P[(size_t)m * 2 * D + D + d] + bh[d];
+  const float hn = (1.f - z) * h[i] + z * ht;
+  h[i] = hn;
+  x[i] += hn;
+}
+
+// After a prefill of T steps: h_state[m] = h[m, T-1]; ring[t % 14] = n1[m, t]
+// for t in [T-14, T-1] (zero for t < 0).
+__global__ void extract_state_kernel(const float* __restrict__ n1, const float* __restrict__ h,
+                                     float* __restrict__ ring, float* __restrict__ hs, int M,
+                                     int T, int D) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * D) return;
+  const int m = i / D, d = i % D;
+  hs[i] = h[((size_t)m * T + T - 1) * D + d];
+  float* rg = ring + (size_t)m * RING * D + d;
+  for (int j = 0; j < RING; ++j) {
+    const int t = T - RING + j;
+    if (t >= 0) rg[(size_t)(t % RING) * D] = n1[((size_t)m * T + t) * D + d];
+    else rg[(size_t)(((t % RING) + RING) % RING) * D] = 0.f;
+  }
+}
+
+// Row gather: out[m] = x[m*T + T-1]
+__global__ void last_rows_kernel(const float* __restrict__ x, float* __restrict__ out, int M,
+                                 int T, int D) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * D) return;
+  const int m = i / D, d = i % D;
+  out[i] = x[((size_t)m * T + T - 1) * D + d];
+}
+
+// Greedy argmax per row (first maximum wins), one warp per row; writes the
+// token to tok[m], to out[m] (if given) and advances the device position once.
+__global__ void argmax_kernel(const float* __restrict__ logits, int M, int V,
+                              int* __restrict__ tok, int* __restrict__ out,
+                              int* __restrict__ pos_ptr) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp < M) {
+    const float* l = logits + (size_t)warp * V;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = lane; c < V; c += 32) {
+      const float v = l[c];
+      if (v > best || (v == best && c < bi)) { best = v; bi = c; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (lane == 0) {
+      tok[warp] = bi;
+      if (out) out[warp] = bi;
+    }
+  }
+  if (pos_ptr && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(pos_ptr, 1);
+}
+
+}  // namespace
+
+cudaError_t decode_conv(const float* n, float* ring, const int* pos, const float* w3,
+                        const float* w7, const float* w15, float* S, int M, int D,
+                        cudaStream_t s) {
+  decode_conv_kernel<<<(M * D + 255) / 256, 256, 0, s>>>(n, ring, pos, w3, w7, w15, S, M, D);
+  return launched();
+}
+
+cudaError_t decode_gru(const float* P, const float* bz, const float* bh, float* h, float* x,
+                       int M, int D, cudaStream_t s) {
+  decode_gru_kernel<<<(M * D + 255) / 256, 256, 0, s>>>(P, bz, bh, h, x, M, D);
+  return launched();
+}
+
+cudaError_t decode_extract_state(const float* n1, const float* h, float* ring, float* hs, int M,
+                                 int T, int D, cudaStream_t s) {
+  extract_state_kernel<<<(M * D + 255) / 256, 256, 0, s>>>(n1, h, ring, hs, M, T, D);
+  return launched();
+}
+
+cudaError_t last_rows(const float* x, float* out, int M, int T, int D, cudaStream_t s) {
+  last_rows_kernel<<<(M * D + 255) / 256, 256, 0, s>>>(x, out, M, T, D);
+  return launched();
+}
+
+cudaError_t argmax_rows(const float* logits, int M, int V, int* tok, int* out, int* pos,
+                        cudaStream_t s) {
+  argmax_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(logits, M, V, tok, out, pos);
+  return launched();
+}
+
+}  // namespace rnet_k

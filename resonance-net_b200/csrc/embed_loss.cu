@@ -158,7 +158,7 @@ cudaError_t embed_fwd(const int* tok, const float* table, float* out, int N, int
   if (N <= 0) return cudaSuccess;
   if (D % 4) return cudaErrorInvalidValue;
   embed_fwd_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(tok, table, out, N, V, D, err);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t embed_bwd(const float* dout, const int* tok, float* dtable, int N, int V, int D,
@@ -179,7 +179,7 @@ cudaError_t embed_bwd(const float* dout, const int* tok, float* dtable, int N, i
   if (per < 64) per = 64;
   dim3 grid(cols, (N + per - 1) / per);
   embed_bwd_kernel<<<grid, 512, smem, s>>>(dout, tok, dtable, N, V, D, per);
-  return cudaGetLastError();
+  return launched();
 }
 
 size_t ce_partials_floats(int N) { return (size_t)(N + 7) / 8 + 1; }
@@ -195,30 +195,30 @@ cudaError_t cross_entropy(const float* logits, const int* tgt, float* loss_sum, 
     if (e != cudaSuccess) return e;
   }
   sum_partials<<<1, 256, 0, s>>>(partials, blocks, loss_sum);
-  return cudaGetLastError();
+  return launched(N > 0 ? 2 : 1);
 }
 
 cudaError_t residual_add(float* x, const float* y, size_t n, cudaStream_t s) {
   if (!n) return cudaSuccess;
   residual_kernel<<<ew_grid(n), 256, 0, s>>>(x, y, n);
-  return cudaGetLastError();
+  return launched();
 }
 cudaError_t scale(float* x, float a, size_t n, cudaStream_t s) {
   if (!n) return cudaSuccess;
   scale_kernel<<<ew_grid(n), 256, 0, s>>>(x, a, n);
-  return cudaGetLastError();
+  return launched();
 }
 cudaError_t add3(const float* a, const float* b, const float* c, float* out, size_t n,
                  cudaStream_t s) {
   if (!n) return cudaSuccess;
   add3_kernel<<<ew_grid(n), 256, 0, s>>>(a, b, c, out, n);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t silu_mul(const float* g, const float* u, float* h, size_t n, cudaStream_t s) {
   if (!n) return cudaSuccess;
   silu_mul_kernel<<<ew_grid(n), 256, 0, s>>>(g, u, h, n);
-  return cudaGetLastError();
+  return launched();
 }
 
 }  // namespace rnet_k

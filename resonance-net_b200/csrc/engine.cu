@@ -266,6 +266,62 @@ int Engine::ensure_capacity(int N, bool with_caches) {
   return RNET_OK;
 }
 
+// ------------------------------------------------------------------ profiling
+cudaEvent_t Engine::prof_event() {
+  if (ev_used_ == ev_pool_.size()) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    ev_pool_.push_back(e);
+  }
+  return ev_pool_[ev_used_++];
+}
+
+void Engine::prof_begin(cudaEvent_t* a) {
+  *a = prof_event();
+  cudaEventRecord(*a, stream_);
+}
+
+void Engine::prof_end(cudaEvent_t a, int kind, double flops, double bytes) {
+  cudaEvent_t b = prof_event();
+  cudaEventRecord(b, stream_);
+  prof_.push_back(ProfRec{kind, flops, bytes, a, b});
+}
+
+int Engine::profile_read(ProfStats* out, bool reset) {
+  CK(cudaStreamSynchronize(stream_));
+  std::memset(out, 0, sizeof(*out));
+  for (const ProfRec& r : prof_) {
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, r.a, r.b));
+    out->ms[r.kind] += ms;
+    out->flops[r.kind] += r.flops;
+    out->bytes[r.kind] += r.bytes;
+    out->launches[r.kind] += 1;
+  }
+  if (reset) {
+    prof_.clear();
+    ev_used_ = 0;
+  }
+  return RNET_OK;
+}
+
+// Time one launch group of a kernel class when profiling is on.
+#define PROF(kind, flops, bytes, expr)                    \
+  do {                                                    \
+    cudaEvent_t _pa = nullptr;                            \
+    if (prof_on_) prof_begin(&_pa);                       \
+    CK(expr);                                             \
+    if (prof_on_) prof_end(_pa, (kind), (flops), (bytes)); \
+  } while (0)
+
+// GEMM through the engine: algorithmic FLOPs 2MNK, bytes = operands + output
+// (+ output read for residual / accumulate epilogues).
+#define MM(M, N, K, A, B, E, PAIR)                                                        \
+  PROF(PK_GEMM, 2.0 * (M) * (N) * (K),                                                    \
+       4.0 * ((double)(M) * (K) + (double)(N) * (K) +                                     \
+              (double)(M) * (N) * (((E).kind == EPI_RESID || (E).kind == EPI_ACCUM) ? 2 : 1)), \
+       gemm_tf32x3(stream_, (M), (N), (K), (A), (B), (E), (PAIR), 0, err))
+
 // ------------------------------------------------------------------ forward
 int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B, int T) {
   const int N = B * T, D = cfg_.d_model, F = cfg_.d_ff, S = cfg_.n_slots, k = cfg_.slot_top_k;
@@ -275,33 +331,37 @@ int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B,
   cudaStream_t s = stream_;
   const float* KT = KT_ + (size_t)l * S * D;
   const float* VT = VT_ + (size_t)l * S * D;
+  const double ND4 = 4.0 * N * D;
   // 1. multi-scale causal conv (reference layer_forward :287-299)
-  CK(rnet_k::rms_norm_fwd(Xl, w.n1, a.n1, a.rinv1, N, D, eps, s));
-  CK(rnet_k::conv_fwd(a.n1, w.c3, w.c7, w.c15, a.S, conv_quirk ? a.Sq : nullptr, nullptr,
-                      nullptr, B, T, D, s));
-  CK(gemm_tf32x3(s, N, D, D, kmaj(a.S, D), kmaj(w.mix, D), epi_resid(a.r1, Xl, D), 0, 0, err));
+  PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(Xl, w.n1, a.n1, a.rinv1, N, D, eps, s));
+  PROF(PK_CONV_FWD, 50.0 * N * D, (conv_quirk ? 3 : 2) * ND4,
+       rnet_k::conv_fwd(a.n1, w.c3, w.c7, w.c15, a.S, conv_quirk ? a.Sq : nullptr, nullptr,
+                        nullptr, B, T, D, s));
+  MM(N, D, D, kmaj(a.S, D), kmaj(w.mix, D), epi_resid(a.r1, Xl, D), 0);
   // 2. MinGRU (:301-313): P = n2 [Wz;Wh]^T, fused gate + scan + residual
-  CK(rnet_k::rms_norm_fwd(a.r1, w.n2, a.n2, a.rinv2, N, D, eps, s));
-  CK(gemm_tf32x3(s, N, 2 * D, D, kmaj(a.n2, D), kmaj(w.Wz, D), epi_store(a.P, 2 * D), 0, 0, err));
-  CK(rnet_k::gru_scan_fwd(a.P, a.P + D, 2 * D, w.bz, w.bh, a.z, a.h, nullptr, a.r1, a.r2, B, T,
-                          D, s));
+  PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(a.r1, w.n2, a.n2, a.rinv2, N, D, eps, s));
+  MM(N, 2 * D, D, kmaj(a.n2, D), kmaj(w.Wz, D), epi_store(a.P, 2 * D), 0);
+  PROF(PK_SCAN_FWD, 0, 6 * ND4,
+       rnet_k::gru_scan_fwd(a.P, a.P + D, 2 * D, w.bz, w.bh, a.z, a.h, nullptr, a.r1, a.r2, B, T,
+                            D, s));
   // 3. slot memory (:315-330)
-  CK(rnet_k::rms_norm_fwd(a.r2, w.n3, a.n3, a.rinv3, N, D, eps, s));
-  CK(gemm_tf32x3(s, N, D, D, kmaj(a.n3, D), kmaj(w.pq, D), epi_store(a.q, D), 0, 0, err));
+  PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(a.r2, w.n3, a.n3, a.rinv3, N, D, eps, s));
+  MM(N, D, D, kmaj(a.n3, D), kmaj(w.pq, D), epi_store(a.q, D), 0);
   if (k == 2) {
     Epilogue e;
     e.kind = EPI_TOP2;
     e.topk_idx = a.idx;
     e.topk_w = a.w;
-    CK(gemm_tf32x3(s, N, S, D, kmaj(a.q, D), kmaj(KT, D), e, 0, 0, err));
+    MM(N, S, D, kmaj(a.q, D), kmaj(KT, D), e, 0);
   } else {
-    CK(gemm_tf32x3(s, N, S, D, kmaj(a.q, D), kmaj(KT, D), epi_store(scores_, S), 0, 0, err));
-    CK(rnet_k::topk_rows(scores_, a.idx, a.w, N, S, k, s));
+    MM(N, S, D, kmaj(a.q, D), kmaj(KT, D), epi_store(scores_, S), 0);
+    PROF(PK_OTHER, 0, 4.0 * N * S, rnet_k::topk_rows(scores_, a.idx, a.w, N, S, k, s));
   }
-  CK(rnet_k::slot_gather(a.idx, a.w, VT, a.r, N, D, S, k, err, s));
-  CK(gemm_tf32x3(s, N, D, D, kmaj(a.r, D), kmaj(w.pout, D), epi_resid(a.r3, a.r2, D), 0, 0, err));
+  PROF(PK_SLOT_GATHER, 2.0 * k * N * D, (1 + k) * ND4,
+       rnet_k::slot_gather(a.idx, a.w, VT, a.r, N, D, S, k, err, s));
+  MM(N, D, D, kmaj(a.r, D), kmaj(w.pout, D), epi_resid(a.r3, a.r2, D), 0);
   // 4. SwiGLU FFN (:332-342): paired gate|up tiles, SiLU*up in the epilogue
-  CK(rnet_k::rms_norm_fwd(a.r3, w.n4, a.n4, a.rinv4, N, D, eps, s));
+  PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(a.r3, w.n4, a.n4, a.rinv4, N, D, eps, s));
   {
     Epilogue e;
     e.kind = EPI_SWIGLU_FWD;
@@ -309,9 +369,10 @@ int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B,
     e.U = a.U;
     e.H = a.H;
     e.ldf = F;
-    CK(gemm_tf32x3(s, N, F, D, kmaj(a.n4, D), kmaj(w.gate, D), e, F, 0, err));
+    MM(N, F, D, kmaj(a.n4, D), kmaj(w.gate, D), e, F);  // 2*N*F*D each for gate and up
+    if (prof_on_) prof_.back().flops *= 2.0;
   }
-  CK(gemm_tf32x3(s, N, D, F, kmaj(a.H, F), kmaj(w.down, F), epi_resid(Xn, a.r3, D), 0, 0, err));
+  MM(N, D, F, kmaj(a.H, F), kmaj(w.down, F), epi_resid(Xn, a.r3, D), 0);
   return RNET_OK;
 }
 
@@ -325,7 +386,7 @@ int Engine::forward(const int* d_tokens, float* d_logits, int B, int T) {
   cudaStream_t s = stream_;
   unsigned* err = rnet_status::device_error_word();
   const size_t ND = (size_t)N * D;
-  CK(rnet_k::embed_fwd(d_tokens, embed_, X_, N, V, D, err, s));
+  PROF(PK_EMBED, 0, 4.0 * ND, rnet_k::embed_fwd(d_tokens, embed_, X_, N, V, D, err, s));
   for (int l = 0; l < cfg_.n_layers; ++l) {
     const float* Xl = caches ? X_ + (size_t)l * ND : X_ + (size_t)(l & 1) * ND;
     float* Xn = caches ? X_ + (size_t)(l + 1) * ND : X_ + (size_t)((l + 1) & 1) * ND;
@@ -333,8 +394,8 @@ int Engine::forward(const int* d_tokens, float* d_logits, int B, int T) {
     if (rc) return rc;
   }
   const float* XL = caches ? X_ + (size_t)cfg_.n_layers * ND : X_ + (size_t)(cfg_.n_layers & 1) * ND;
-  CK(rnet_k::rms_norm_fwd(XL, fnorm_, nf_, rinvf_, N, D, cfg_.rms_eps, s));
-  CK(gemm_tf32x3(s, N, V, D, kmaj(nf_, D), kmaj(outw_, D), epi_store(d_logits, V), 0, 0, err));
+  PROF(PK_RMS_FWD, 0, 8.0 * ND, rnet_k::rms_norm_fwd(XL, fnorm_, nf_, rinvf_, N, D, cfg_.rms_eps, s));
+  MM(N, V, D, kmaj(nf_, D), kmaj(outw_, D), epi_store(d_logits, V), 0);
   have_cache_ = caches;
   last_B_ = B;
   last_T_ = T;
@@ -347,10 +408,11 @@ int Engine::head_backward(const float* d_dlogits, int N) {
   unsigned* err = rnet_status::device_error_word();
   cudaStream_t s = stream_;
   // src/resonance_net.cpp:428-442
-  CK(gemm_tf32x3(s, N, D, V, kmaj(d_dlogits, V), mnmaj(outw_, D), epi_store(dnf_, D), 0, 0, err));
-  CK(gemm_tf32x3(s, V, D, N, mnmaj(d_dlogits, V), mnmaj(nf_, D), epi_accum(g_outw_, D), 0, 0, err));
+  MM(N, D, V, kmaj(d_dlogits, V), mnmaj(outw_, D), epi_store(dnf_, D), 0);
+  MM(V, D, N, mnmaj(d_dlogits, V), mnmaj(nf_, D), epi_accum(g_outw_, D), 0);
   const float* XL = X_ + (size_t)cfg_.n_layers * N * D;
-  CK(rnet_k::rms_norm_bwd(dnf_, XL, fnorm_, rinvf_, dX_, g_fnorm_, N, D, 0, s));
+  PROF(PK_RMS_BWD, 0, 12.0 * N * D,
+       rnet_k::rms_norm_bwd(dnf_, XL, fnorm_, rinvf_, dX_, g_fnorm_, N, D, 0, s));
   return RNET_OK;
 }
 
@@ -364,6 +426,7 @@ int Engine::layer_backward(int l, int B, int T) {
   const float* Xl = X_ + (size_t)l * N * D;
   float* dKT = dKT_ + (size_t)l * S * D;
   float* dVT = dVT_ + (size_t)l * S * D;
+  const double ND4 = 4.0 * N * D;
   // 4. SwiGLU (src/resonance_net.cpp:468-490, src/swiglu_ffn.cu:88-152)
   {
     Epilogue e;
@@ -373,37 +436,39 @@ int Engine::layer_backward(int l, int B, int T) {
     e.Gc = a.G;
     e.Uc = a.U;
     e.ldf = F;
-    CK(gemm_tf32x3(s, N, F, D, kmaj(dX_, D), mnmaj(w.down, F), e, 0, 0, err));
+    MM(N, F, D, kmaj(dX_, D), mnmaj(w.down, F), e, 0);
   }
-  CK(gemm_tf32x3(s, D, F, N, mnmaj(dX_, D), mnmaj(a.H, F), epi_accum(g.down, F), 0, 0, err));
-  CK(gemm_tf32x3(s, N, D, 2 * F, kmaj(dGU_, 2 * F), mnmaj(w.gate, D), epi_store(dsub_, D), 0, 0, err));
-  CK(gemm_tf32x3(s, 2 * F, D, N, mnmaj(dGU_, 2 * F), mnmaj(a.n4, D), epi_accum(g.gate, D), 0, 0, err));
-  CK(rnet_k::rms_norm_bwd(dsub_, a.r3, w.n4, a.rinv4, dX_, g.n4, N, D, 1, s));
+  MM(D, F, N, mnmaj(dX_, D), mnmaj(a.H, F), epi_accum(g.down, F), 0);
+  MM(N, D, 2 * F, kmaj(dGU_, 2 * F), mnmaj(w.gate, D), epi_store(dsub_, D), 0);
+  MM(2 * F, D, N, mnmaj(dGU_, 2 * F), mnmaj(a.n4, D), epi_accum(g.gate, D), 0);
+  PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, a.r3, w.n4, a.rinv4, dX_, g.n4, N, D, 1, s));
   // 3. slot memory (:492-510, src/slot_memory.cu:171-244) — sparse top-k path
-  CK(gemm_tf32x3(s, N, D, D, kmaj(dX_, D), mnmaj(w.pout, D), epi_store(dr_, D), 0, 0, err));
-  CK(gemm_tf32x3(s, D, D, N, mnmaj(dX_, D), mnmaj(a.r, D), epi_accum(g.pout, D), 0, 0, err));
+  MM(N, D, D, kmaj(dX_, D), mnmaj(w.pout, D), epi_store(dr_, D), 0);
+  MM(D, D, N, mnmaj(dX_, D), mnmaj(a.r, D), epi_accum(g.pout, D), 0);
   CK(cudaMemsetAsync(dKT, 0, (size_t)S * D * sizeof(float), s));
   CK(cudaMemsetAsync(dVT, 0, (size_t)S * D * sizeof(float), s));
-  CK(rnet_k::slot_sparse_bwd(dr_, a.idx, a.w, VT_ + (size_t)l * S * D, KT_ + (size_t)l * S * D,
-                             a.q, dq_, dVT, dKT, N, D, S, k, err, s));
-  CK(rnet_k::transpose(dKT, g.keys, S, D, 1, s));
-  CK(rnet_k::transpose(dVT, g.vals, S, D, 1, s));
-  CK(gemm_tf32x3(s, N, D, D, kmaj(dq_, D), mnmaj(w.pq, D), epi_store(dsub_, D), 0, 0, err));
-  CK(gemm_tf32x3(s, D, D, N, mnmaj(dq_, D), mnmaj(a.n3, D), epi_accum(g.pq, D), 0, 0, err));
-  CK(rnet_k::rms_norm_bwd(dsub_, a.r2, w.n3, a.rinv3, dX_, g.n3, N, D, 1, s));
+  PROF(PK_SLOT_SPARSE_BWD, 8.0 * k * N * D, (3 + 4 * k) * ND4,
+       rnet_k::slot_sparse_bwd(dr_, a.idx, a.w, VT_ + (size_t)l * S * D, KT_ + (size_t)l * S * D,
+                               a.q, dq_, dVT, dKT, N, D, S, k, err, s));
+  PROF(PK_OTHER, 0, 16.0 * S * D, rnet_k::transpose(dKT, g.keys, S, D, 1, s));
+  PROF(PK_OTHER, 0, 16.0 * S * D, rnet_k::transpose(dVT, g.vals, S, D, 1, s));
+  MM(N, D, D, kmaj(dq_, D), mnmaj(w.pq, D), epi_store(dsub_, D), 0);
+  MM(D, D, N, mnmaj(dq_, D), mnmaj(a.n3, D), epi_accum(g.pq, D), 0);
+  PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, a.r2, w.n3, a.rinv3, dX_, g.n3, N, D, 1, s));
   // 2. MinGRU (:512-528, src/min_gru.cu:128-191)
-  CK(rnet_k::gru_scan_bwd(dX_, a.z, a.h, a.P + D, 2 * D, w.bh, dPZH_, dPZH_ + D, 2 * D, g.bz,
-                          g.bh, B, T, D, s));
-  CK(gemm_tf32x3(s, N, D, 2 * D, kmaj(dPZH_, 2 * D), mnmaj(w.Wz, D), epi_store(dsub_, D), 0, 0, err));
-  CK(gemm_tf32x3(s, 2 * D, D, N, mnmaj(dPZH_, 2 * D), mnmaj(a.n2, D), epi_accum(g.Wz, D), 0, 0, err));
-  CK(rnet_k::rms_norm_bwd(dsub_, a.r1, w.n2, a.rinv2, dX_, g.n2, N, D, 1, s));
+  PROF(PK_SCAN_BWD, 0, 6 * ND4,
+       rnet_k::gru_scan_bwd(dX_, a.z, a.h, a.P + D, 2 * D, w.bh, dPZH_, dPZH_ + D, 2 * D, g.bz,
+                            g.bh, B, T, D, s));
+  MM(N, D, 2 * D, kmaj(dPZH_, 2 * D), mnmaj(w.Wz, D), epi_store(dsub_, D), 0);
+  MM(2 * D, D, N, mnmaj(dPZH_, 2 * D), mnmaj(a.n2, D), epi_accum(g.Wz, D), 0);
+  PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, a.r1, w.n2, a.rinv2, dX_, g.n2, N, D, 1, s));
   // 1. causal conv (:530-545, src/causal_conv.cu:132-190)
-  CK(gemm_tf32x3(s, N, D, D, kmaj(dX_, D), mnmaj(w.mix, D), epi_store(dS_, D), 0, 0, err));
-  CK(gemm_tf32x3(s, D, D, N, mnmaj(dX_, D), mnmaj(conv_quirk ? a.Sq : a.S, D),
-                 epi_accum(g.mix, D), 0, 0, err));
-  CK(rnet_k::conv_bwd(dS_, a.n1, w.c3, w.c7, w.c15, dsub_, g.c3, g.c7, g.c15, conv_parts_, B, T,
-                      D, 0, s));
-  CK(rnet_k::rms_norm_bwd(dsub_, Xl, w.n1, a.rinv1, dX_, g.n1, N, D, 1, s));
+  MM(N, D, D, kmaj(dX_, D), mnmaj(w.mix, D), epi_store(dS_, D), 0);
+  MM(D, D, N, mnmaj(dX_, D), mnmaj(conv_quirk ? a.Sq : a.S, D), epi_accum(g.mix, D), 0);
+  PROF(PK_CONV_BWD, 100.0 * N * D, 3 * ND4,
+       rnet_k::conv_bwd(dS_, a.n1, w.c3, w.c7, w.c15, dsub_, g.c3, g.c7, g.c15, conv_parts_, B, T,
+                        D, 0, s));
+  PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, Xl, w.n1, a.rinv1, dX_, g.n1, N, D, 1, s));
   return RNET_OK;
 }
 
@@ -422,7 +487,8 @@ int Engine::backward(const float* d_dlogits, const int* d_tokens, int B, int T) 
       if (rc) return rc;
     }
   }
-  CK(rnet_k::embed_bwd(dX_, d_tokens, g_embed_, N, cfg_.vocab_size, cfg_.d_model, stream_));
+  PROF(PK_EMBED, 0, 4.0 * N * cfg_.d_model,
+       rnet_k::embed_bwd(dX_, d_tokens, g_embed_, N, cfg_.vocab_size, cfg_.d_model, stream_));
   if (dist) {
     rc = dist_reduce_range(dist, grads_, 2 * (size_t)cfg_.vocab_size * cfg_.d_model + cfg_.d_model,
                            stream_);
@@ -430,7 +496,6 @@ int Engine::backward(const float* d_dlogits, const int* d_tokens, int B, int T) 
   }
   return RNET_OK;
 }
-
 int Engine::zero_grad() {
   CK(cudaMemsetAsync(grads_, 0, P_ * sizeof(float), stream_));
   return RNET_OK;
@@ -443,8 +508,13 @@ int Engine::step(float lr, float clip) {
     if (rc) return rc;
     world = dist_world(dist);
   }
-  CK(rnet_k::sgd_clip_step(params_, grads_, P_, lr, clip, world, scratch_, norm_dev_, stream_));
-  return refresh_shadows();
+  PROF(PK_SGD, 2.0 * P_, 16.0 * P_,
+       rnet_k::sgd_clip_step(params_, grads_, P_, lr, clip, world, scratch_, norm_dev_, stream_));
+  cudaEvent_t pa = nullptr;
+  if (prof_on_) prof_begin(&pa);
+  int rc = refresh_shadows();
+  if (prof_on_) prof_end(pa, PK_OTHER, 0, 16.0 * 2 * cfg_.n_layers * cfg_.n_slots * cfg_.d_model);
+  return rc;
 }
 
 int Engine::train_step(const int* d_in, const int* d_tgt, int B, int T, float lr, float clip,
@@ -458,12 +528,165 @@ int Engine::train_step(const int* d_in, const int* d_tgt, int B, int T, float lr
   if (rc) return rc;
   rc = forward(d_in, logits_, B, T);
   if (rc) return rc;
-  CK(rnet_k::cross_entropy(logits_, d_tgt, d_loss_sum ? d_loss_sum : loss_dev_, dlogits_,
-                           1.0f / (float)N, conv_parts_, N, V, rnet_status::device_error_word(),
-                           stream_));
+  PROF(PK_CE, 0, 8.0 * N * V,
+       rnet_k::cross_entropy(logits_, d_tgt, d_loss_sum ? d_loss_sum : loss_dev_, dlogits_,
+                             1.0f / (float)N, conv_parts_, N, V, rnet_status::device_error_word(),
+                             stream_));
   rc = backward(dlogits_, d_in, B, T);
   if (rc) return rc;
   return step(lr, clip);
+}
+
+// ------------------------------------------------------------------ decode
+int Engine::decoder_init(Decoder* d, int M) {
+  if (M <= 0) return rnet_status::fail(RNET_ERR_ARG, "decoder: n_streams must be > 0");
+  const size_t D = cfg_.d_model, F = cfg_.d_ff, V = cfg_.vocab_size, L = cfg_.n_layers;
+  const size_t k = cfg_.slot_top_k, m = M;
+  if (k != 2) return rnet_status::fail(RNET_ERR_UNSUPPORTED, "decoder: slot_top_k must be 2");
+  d->M = M;
+  d->floats_per_layer = m * 15 * D;
+  std::vector<std::pair<void**, size_t>> plan;
+  auto f = [&](float** p, size_t n) { plan.push_back({(void**)p, n * sizeof(float)}); };
+  f(&d->state, L * d->floats_per_layer);
+  f(&d->x, m * D); f(&d->n, m * D); f(&d->S, m * D); f(&d->P, 2 * m * D); f(&d->q, m * D);
+  f(&d->r, m * D); f(&d->G, m * F); f(&d->U, m * F); f(&d->H, m * F); f(&d->logits, m * V);
+  f(&d->w, m * k);
+  plan.push_back({(void**)&d->idx, m * k * sizeof(int)});
+  plan.push_back({(void**)&d->tok, m * sizeof(int)});
+  plan.push_back({(void**)&d->pos, sizeof(int)});
+  size_t total = 0;
+  for (auto& e : plan) total += (e.second + 255) & ~size_t(255);
+  CK(cudaMalloc(&d->arena, total));
+  CK(cudaMemsetAsync(d->arena, 0, total, stream_));
+  char* p = (char*)d->arena;
+  for (auto& e : plan) {
+    *e.first = p;
+    p += (e.second + 255) & ~size_t(255);
+  }
+  return RNET_OK;
+}
+
+void Engine::decoder_free(Decoder* d) {
+  if (d->exec) cudaGraphExecDestroy(d->exec);
+  if (d->graph) cudaGraphDestroy(d->graph);
+  cudaStreamSynchronize(stream_);
+  cudaFree(d->arena);
+  d->arena = nullptr;
+  d->exec = nullptr;
+  d->graph = nullptr;
+}
+
+int Engine::prefill(Decoder* d, const int* d_tokens, int T) {
+  if (T <= 0) return rnet_status::fail(RNET_ERR_ARG, "prefill: empty prompt");
+  const int M = d->M, N = M * T, D = cfg_.d_model, V = cfg_.vocab_size;
+  int rc = ensure_capacity(N, false);
+  if (rc) return rc;
+  cudaStream_t s = stream_;
+  unsigned* err = rnet_status::device_error_word();
+  const size_t ND = (size_t)N * D;
+  PROF(PK_EMBED, 0, 4.0 * ND, rnet_k::embed_fwd(d_tokens, embed_, X_, N, V, D, err, s));
+  for (int l = 0; l < cfg_.n_layers; ++l) {
+    const float* Xl = X_ + (size_t)(l & 1) * ND;
+    float* Xn = X_ + (size_t)((l + 1) & 1) * ND;
+    rc = layer_forward(l, Xl, Xn, act_[0], M, T);
+    if (rc) return rc;
+    float* st = d->state + (size_t)l * d->floats_per_layer;
+    CK(rnet_k::decode_extract_state(act_[0].n1, act_[0].h, st, st + (size_t)M * 14 * D, M, T, D,
+                                    s));
+  }
+  have_cache_ = false;
+  const float* XL = X_ + (size_t)(cfg_.n_layers & 1) * ND;
+  CK(rnet_k::last_rows(XL, d->x, M, T, D, s));
+  CK(rnet_k::rms_norm_fwd(d->x, fnorm_, d->n, nullptr, M, D, cfg_.rms_eps, s));
+  MM(M, V, D, kmaj(d->n, D), kmaj(outw_, D), epi_store(d->logits, V), 0);
+  CK(cudaMemcpyAsync(d->pos, &T, sizeof(int), cudaMemcpyHostToDevice, s));
+  CK(cudaStreamSynchronize(s));  // &T is a stack value
+  CK(rnet_k::argmax_rows(d->logits, M, V, d->tok, nullptr, nullptr, s));
+  return RNET_OK;
+}
+
+int Engine::decode_step(Decoder* d, const int* d_tokens) {
+  const int M = d->M, D = cfg_.d_model, F = cfg_.d_ff, S = cfg_.n_slots, V = cfg_.vocab_size;
+  const float eps = cfg_.rms_eps;
+  cudaStream_t s = stream_;
+  unsigned* err = rnet_status::device_error_word();
+  if (d_tokens) CK(cudaMemcpyAsync(d->tok, d_tokens, M * sizeof(int), cudaMemcpyDeviceToDevice, s));
+  CK(rnet_k::embed_fwd(d->tok, embed_, d->x, M, V, D, err, s));
+  for (int l = 0; l < cfg_.n_layers; ++l) {
+    const LayerParams& w = W_[l];
+    float* ring = d->state + (size_t)l * d->floats_per_layer;
+    float* h = ring + (size_t)M * 14 * D;
+    CK(rnet_k::rms_norm_fwd(d->x, w.n1, d->n, nullptr, M, D, eps, s));
+    CK(rnet_k::decode_conv(d->n, ring, d->pos, w.c3, w.c7, w.c15, d->S, M, D, s));
+    MM(M, D, D, kmaj(d->S, D), kmaj(w.mix, D), epi_resid(d->x, d->x, D), 0);
+    CK(rnet_k::rms_norm_fwd(d->x, w.n2, d->n, nullptr, M, D, eps, s));
+    MM(M, 2 * D, D, kmaj(d->n, D), kmaj(w.Wz, D), epi_store(d->P, 2 * D), 0);
+    CK(rnet_k::decode_gru(d->P, w.bz, w.bh, h, d->x, M, D, s));
+    CK(rnet_k::rms_norm_fwd(d->x, w.n3, d->n, nullptr, M, D, eps, s));
+    MM(M, D, D, kmaj(d->n, D), kmaj(w.pq, D), epi_store(d->q, D), 0);
+    {
+      Epilogue e;
+      e.kind = EPI_TOP2;
+      e.topk_idx = d->idx;
+      e.topk_w = d->w;
+      MM(M, S, D, kmaj(d->q, D), kmaj(KT_ + (size_t)l * S * D, D), e, 0);
+    }
+    CK(rnet_k::slot_gather(d->idx, d->w, VT_ + (size_t)l * S * D, d->r, M, D, S, 2, err, s));
+    MM(M, D, D, kmaj(d->r, D), kmaj(w.pout, D), epi_resid(d->x, d->x, D), 0);
+    CK(rnet_k::rms_norm_fwd(d->x, w.n4, d->n, nullptr, M, D, eps, s));
+    {
+      Epilogue e;
+      e.kind = EPI_SWIGLU_FWD;
+      e.G = d->G;
+      e.U = d->U;
+      e.H = d->H;
+      e.ldf = F;
+      MM(M, F, D, kmaj(d->n, D), kmaj(w.gate, D), e, F);
+    }
+    MM(M, D, F, kmaj(d->H, F), kmaj(w.down, F), epi_resid(d->x, d->x, D), 0);
+  }
+  CK(rnet_k::rms_norm_fwd(d->x, fnorm_, d->n, nullptr, M, D, eps, s));
+  MM(M, V, D, kmaj(d->n, D), kmaj(outw_, D), epi_store(d->logits, V), 0);
+  CK(rnet_k::argmax_rows(d->logits, M, V, d->tok, nullptr, d->pos, s));
+  return RNET_OK;
+}
+
+int Engine::generate(Decoder* d, int n_steps, int* d_out, bool use_graph) {
+  cudaStream_t s = stream_;
+  if (use_graph && !d->exec) {
+    // one eager step first so every kernel attribute / tensor map is set up,
+    // then capture the step (all arguments are fixed device pointers; the
+    // position lives in device memory and is advanced by the argmax kernel)
+    int rc = decode_step(d, nullptr);
+    if (rc) return rc;
+    if (d_out) CK(cudaMemcpyAsync(d_out, d->tok, d->M * sizeof(int), cudaMemcpyDeviceToDevice, s));
+    --n_steps;
+    d_out = d_out ? d_out + d->M : nullptr;
+    CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    rc = decode_step(d, nullptr);
+    cudaGraph_t g = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(s, &g);
+    if (rc) return rc;
+    CK(ce);
+    d->graph = g;
+    size_t nodes = 0;
+    CK(cudaGraphGetNodes(g, nullptr, &nodes));
+    d->graph_kernels = (int)nodes;  // the captured step contains kernel nodes only
+    CK(cudaGraphInstantiate(&d->exec, g, 0));
+  }
+  for (int i = 0; i < n_steps; ++i) {
+    if (d->exec) {
+      CK(cudaGraphLaunch(d->exec, s));
+      rnet_status::count_launch((unsigned)d->graph_kernels);
+    } else {
+      int rc = decode_step(d, nullptr);
+      if (rc) return rc;
+    }
+    if (d_out)
+      CK(cudaMemcpyAsync(d_out + (size_t)i * d->M, d->tok, d->M * sizeof(int),
+                         cudaMemcpyDeviceToDevice, s));
+  }
+  return RNET_OK;
 }
 
 int Engine::topk(int layer, int** idx, float** w) {

@@ -38,8 +38,62 @@ struct LayerAct {
 
 class DistComm;  // dist.cu
 
+// Per-kernel-class event timing (enabled on demand; one event pair per launch
+// group, on the engine stream).
+enum ProfKind {
+  PK_GEMM = 0,
+  PK_SCAN_FWD,
+  PK_SCAN_BWD,
+  PK_CONV_FWD,
+  PK_CONV_BWD,
+  PK_RMS_FWD,
+  PK_RMS_BWD,
+  PK_SLOT_GATHER,
+  PK_SLOT_SPARSE_BWD,
+  PK_EMBED,
+  PK_CE,
+  PK_SGD,
+  PK_OTHER,
+  PK_COUNT
+};
+
+struct ProfStats {
+  double ms[PK_COUNT];
+  double flops[PK_COUNT];
+  double bytes[PK_COUNT];
+  long long launches[PK_COUNT];
+};
+
+// Recurrent decode state and buffers for M lock-step streams.
+struct Decoder {
+  int M = 0;
+  float* state = nullptr;  // per layer: ring [M][14][D] then h [M][D]
+  size_t floats_per_layer = 0;
+  float *x, *n, *S, *P, *q, *r, *G, *U, *H, *logits;
+  int* idx;
+  float* w;
+  int* tok;  // current / next token per stream
+  int* pos;  // device scalar: index of the token being processed
+  void* arena = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  cudaGraph_t graph = nullptr;
+  int graph_kernels = 0;
+};
+
 class Engine {
  public:
+  // ---- decode (O(1) recurrent state) ----
+  int decoder_init(Decoder* d, int M);
+  void decoder_free(Decoder* d);
+  // Chunked-scan forward over d_tokens [M, T]; leaves the state after T
+  // tokens, last-position logits in d->logits and their argmax in d->tok.
+  int prefill(Decoder* d, const int* d_tokens, int T);
+  // One token per stream (d_tokens, or the previous argmax when null);
+  // logits in d->logits, argmax in d->tok.
+  int decode_step(Decoder* d, const int* d_tokens);
+  // n_steps greedy steps; d_out [n_steps][M] receives the generated tokens.
+  int generate(Decoder* d, int n_steps, int* d_out, bool use_graph);
+
   explicit Engine(const rnet_model_config& c);
   ~Engine();
   int init(int device, bool reference_init);  // allocate + initialise weights
@@ -75,7 +129,24 @@ class Engine {
   // workspace capacity in tokens
   int ensure_capacity(int N, bool with_caches);
 
+  // profiling
+  void profile_enable(bool on) { prof_on_ = on; }
+  int profile_read(ProfStats* out, bool reset);
+
  private:
+  struct ProfRec {
+    int kind;
+    double flops, bytes;
+    cudaEvent_t a, b;
+  };
+  bool prof_on_ = false;
+  std::vector<ProfRec> prof_;
+  std::vector<cudaEvent_t> ev_pool_;
+  size_t ev_used_ = 0;
+  cudaEvent_t prof_event();
+  void prof_begin(cudaEvent_t* a);
+  void prof_end(cudaEvent_t a, int kind, double flops, double bytes);
+
   int gemm_err(cudaError_t e, const char* what);
   int layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B, int T);
   int layer_backward(int l, int B, int T);

@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "gemm.cuh"
+#include "kernels.cuh"
 
 namespace rnet_gemm {
 using namespace rnet_dev;
@@ -486,7 +487,7 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
   }
   const int grid = kp.num_units < num_sms() ? kp.num_units : num_sms();
   gemm_tf32x3_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ta, tb, kp);
-  return cudaGetLastError();
+  return rnet_k::launched();
 }
 
 cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand& A,

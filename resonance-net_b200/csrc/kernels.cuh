@@ -5,6 +5,10 @@
 
 namespace rnet_k {
 
+// Launch bookkeeping: count `n` kernels launched by this library and return
+// the launch status (defined in status.cu).
+cudaError_t launched(unsigned n = 1);
+
 // ---- RMSNorm (rms_norm.cu) ------------------------------------------------
 // y = x * rinv * w, rinv = rsqrt(mean(x^2) + eps)        (y may be null)
 cudaError_t rms_norm_fwd(const float* x, const float* w, float* y, float* rinv, int rows,
@@ -78,6 +82,20 @@ cudaError_t add3(const float* a, const float* b, const float* c, float* out, siz
                  cudaStream_t s);
 // h = g * sigmoid(g) * u   (reference silu_mul_kernel, src/swiglu_ffn.cu:11-21)
 cudaError_t silu_mul(const float* g, const float* u, float* h, size_t n, cudaStream_t s);
+
+// ---- recurrent decode (decode.cu) -----------------------------------------
+// ring: [M][14][D] last conv inputs indexed by position mod 14; *pos = index
+// of the current token (device scalar, advanced by argmax_rows).
+cudaError_t decode_conv(const float* n, float* ring, const int* pos, const float* w3,
+                        const float* w7, const float* w15, float* S, int M, int D,
+                        cudaStream_t s);
+cudaError_t decode_gru(const float* P, const float* bz, const float* bh, float* h, float* x,
+                       int M, int D, cudaStream_t s);
+cudaError_t decode_extract_state(const float* n1, const float* h, float* ring, float* hs, int M,
+                                 int T, int D, cudaStream_t s);
+cudaError_t last_rows(const float* x, float* out, int M, int T, int D, cudaStream_t s);
+cudaError_t argmax_rows(const float* logits, int M, int V, int* tok, int* out, int* pos,
+                        cudaStream_t s);
 
 // ---- optimizer (optimizer.cu) ---------------------------------------------
 // Global-norm clip + SGD over one flat buffer, no host synchronisation:

@@ -168,7 +168,7 @@ cudaError_t gru_scan_fwd(const float* pz, const float* ph, int ldp, const float*
   if (B <= 0 || T <= 0) return cudaSuccess;
   const int grid = B * ((D + 31) / 32);
   scan_fwd_kernel<<<grid, W * 32, 0, s>>>(pz, ph, ldp, bz, bh, z, h, y, res, out, T, D);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t gru_scan_bwd(const float* dy, const float* z, const float* h, const float* ph,
@@ -177,7 +177,7 @@ cudaError_t gru_scan_bwd(const float* dy, const float* z, const float* h, const 
   if (B <= 0 || T <= 0) return cudaSuccess;
   const int grid = B * ((D + 31) / 32);
   scan_bwd_kernel<<<grid, W * 32, 0, s>>>(dy, z, h, ph, ldp, bh, dz, dht, ldd, dbz, dbh, T, D);
-  return cudaGetLastError();
+  return launched();
 }
 
 }  // namespace rnet_k

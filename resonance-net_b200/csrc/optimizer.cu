@@ -90,7 +90,7 @@ cudaError_t sgd_clip_step(float* params, const float* grads, size_t n, float lr,
   sumsq_kernel<<<NORM_BLOCKS, 256, 0, s>>>(grads, n, part);
   finalize_kernel<<<1, 256, 0, s>>>(part, NORM_BLOCKS, lr, clip, world, lr_dev, norm_out);
   update_kernel<<<148 * 8, 256, 0, s>>>(params, grads, n, lr_dev);
-  return cudaGetLastError();
+  return launched(3);
 }
 
 }  // namespace rnet_k

@@ -136,7 +136,7 @@ cudaError_t rms_norm_fwd(const float* x, const float* w, float* y, float* rinv, 
   if (rows <= 0) return cudaSuccess;
   if (D % 4 != 0 || D > 4 * 32 * MAXV) return cudaErrorInvalidValue;
   rms_fwd_kernel<<<grid_for_rows(rows), WARPS * 32, 0, s>>>(x, w, y, rinv, rows, D, eps);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t rms_norm_bwd(const float* dy, const float* x, const float* w, const float* rinv,
@@ -151,7 +151,7 @@ cudaError_t rms_norm_bwd(const float* dy, const float* x, const float* w, const 
   if (grid < 1) grid = 1;
   rms_bwd_kernel<<<grid, WARPS * 32, D * sizeof(float), s>>>(dy, x, w, rinv, dx, dw, rows, D,
                                                              mode);
-  return cudaGetLastError();
+  return launched();
 }
 
 }  // namespace rnet_k

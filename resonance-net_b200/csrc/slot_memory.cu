@@ -146,7 +146,7 @@ cudaError_t transpose(const float* in, float* out, int R, int C, int acc, cudaSt
   if (R <= 0 || C <= 0) return cudaSuccess;
   dim3 grid((C + 31) / 32, (R + 31) / 32);
   transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(in, out, R, C, acc);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t slot_gather(const int* idx, const float* w, const float* VT, float* r, int N, int D,
@@ -154,7 +154,7 @@ cudaError_t slot_gather(const int* idx, const float* w, const float* VT, float* 
   if (N <= 0) return cudaSuccess;
   if (k < 1 || k > 8 || D % 4) return cudaErrorInvalidValue;
   gather_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(idx, w, VT, r, N, D, S, k, err);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t slot_sparse_bwd(const float* dr, const int* idx, const float* w, const float* VT,
@@ -164,7 +164,7 @@ cudaError_t slot_sparse_bwd(const float* dr, const int* idx, const float* w, con
   if (k < 1 || k > 8 || D % 4) return cudaErrorInvalidValue;
   sparse_bwd_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dr, idx, w, VT, KT, q, dq, dVT, dKT, N,
                                                          D, S, k, err);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t topk_rows(const float* scores, int* idx, float* w, int N, int S, int k,
@@ -172,7 +172,7 @@ cudaError_t topk_rows(const float* scores, int* idx, float* w, int N, int S, int
   if (N <= 0) return cudaSuccess;
   if (k < 1 || k > 8) return cudaErrorInvalidValue;
   topk_kernel<<<(N + 127) / 128, 128, 0, s>>>(scores, idx, w, N, S, k);
-  return cudaGetLastError();
+  return launched();
 }
 
 }  // namespace rnet_k

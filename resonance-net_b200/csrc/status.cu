@@ -1,4 +1,5 @@
 // Status / error plumbing of the C ABI.
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -38,9 +39,26 @@ unsigned* device_error_word() {
   return words[dev];
 }
 
+static std::atomic<unsigned long long> g_launches{0};
+void count_launch(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+unsigned long long launches() { return g_launches.load(std::memory_order_relaxed); }
+
 }  // namespace rnet_status
 
+namespace rnet_k {
+cudaError_t launched(unsigned n) {
+  rnet_status::count_launch(n);
+  return cudaGetLastError();
+}
+}  // namespace rnet_k
+
 extern "C" const char* rnet_last_error(void) { return rnet_status::g_last_error.c_str(); }
+
+extern "C" int rnet_kernel_launches(unsigned long long* n) {
+  if (!n) return rnet_status::fail(RNET_ERR_ARG, "null output");
+  *n = rnet_status::launches();
+  return RNET_OK;
+}
 
 extern "C" int rnet_abi_version(void) { return 100; }
 

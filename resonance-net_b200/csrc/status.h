@@ -15,6 +15,10 @@ int fail_cuda(cudaError_t e, const char* what);
 // of this library on the current device.
 unsigned* device_error_word();
 
+// Count of kernels launched by this library (process-wide).
+void count_launch(unsigned n = 1);
+unsigned long long launches();
+
 }  // namespace rnet_status
 
 #define RNET_TRY_CUDA(expr)                                            \
