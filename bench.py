@@ -50,6 +50,14 @@ def parse():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--seq", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # single-operation mode (profiling captures of one kernel class)
+    ap.add_argument("--op", default=None,
+                    help="gemm | scan_fwd | scan_bwd | conv_fwd | conv_bwd | rms_fwd | rms_bwd")
+    ap.add_argument("--m", type=int, default=16384)
+    ap.add_argument("--n", type=int, default=512)
+    ap.add_argument("--k", type=int, default=512)
+    ap.add_argument("--amn", type=int, default=0)
+    ap.add_argument("--bmn", type=int, default=0)
     return ap.parse_args()
 
 
@@ -359,9 +367,99 @@ def run_reference(args, rank, world, local):
     print(json.dumps(out), flush=True)
 
 
+def run_op(args):
+    """One operation in a loop at config-2 shapes through the C ABI (used for
+    ncu captures of one kernel class); prints the device time per call."""
+    import torch
+    rnet = importlib.import_module("resonance-net_b200")
+    torch.cuda.set_device(0)
+    F32 = ctypes.c_float
+    p = rnet.ptr
+    B, T, D = args.batch, args.seq, CFG["d_model"]
+    N = B * T
+    g = torch.Generator(device="cuda").manual_seed(0)
+
+    def rnd(*shape, scale=1.0):
+        return torch.randn(*shape, device="cuda", generator=g) * scale
+
+    def z(*shape):
+        return torch.zeros(*shape, device="cuda")
+
+    if args.op == "gemm":
+        M, Nn, K = args.m, args.n, args.k
+        A = rnd(K, M) if args.amn else rnd(M, K)
+        Bm = rnd(K, Nn) if args.bmn else rnd(Nn, K)
+        C = z(M, Nn)
+        lda, ldb = (M if args.amn else K), (Nn if args.bmn else K)
+        fn = lambda: rnet.call("rnet_gemm_f32", M, Nn, K, p(A), lda, args.amn, p(Bm), ldb,
+                               args.bmn, p(C), Nn, p(C), Nn, 0, F32(1.0), None)
+        work = f"gemm M={M} N={Nn} K={K} a_mn={args.amn} b_mn={args.bmn}"
+    elif args.op in ("scan_fwd", "scan_bwd"):
+        x = rnd(N, D)
+        Wz, Wh = rnd(D, D, scale=D ** -0.5), rnd(D, D, scale=D ** -0.5)
+        bz, bh = rnd(D), rnd(D)
+        y, zc, h = z(N, D), z(N, D), z(N, D)
+        fwd = lambda: rnet.call("rnet_min_gru_forward", p(x), p(y), p(Wz), p(Wh), p(bz), p(bh),
+                                p(zc), p(h), B, T, D, None)
+        fwd()
+        if args.op == "scan_fwd":
+            fn = fwd
+        else:
+            dy, dx = rnd(N, D), z(N, D)
+            gz, gh, gbz, gbh = z(D, D), z(D, D), z(D), z(D)
+            fn = lambda: rnet.call("rnet_min_gru_backward", p(dy), p(x), p(Wz), p(Wh), p(bz),
+                                   p(bh), p(zc), p(h), p(dx), p(gz), p(gh), p(gbz), p(gbh), B, T,
+                                   D, None)
+        work = f"min_gru {args.op[5:]} B={B} T={T} D={D}"
+    elif args.op in ("conv_fwd", "conv_bwd"):
+        x = rnd(N, D)
+        w3, w7, w15, mix = rnd(3, D), rnd(7, D), rnd(15, D), rnd(D, D, scale=D ** -0.5)
+        y, cb = z(N, D), z(3, N, D)
+        fwd = lambda: rnet.call("rnet_causal_conv_forward", p(x), p(y), p(w3), p(w7), p(w15),
+                                p(mix), p(cb), B, T, D, None)
+        fwd()
+        if args.op == "conv_fwd":
+            fn = fwd
+        else:
+            dy, dx = rnd(N, D), z(N, D)
+            gw = [z(3, D), z(7, D), z(15, D), z(D, D)]
+            fn = lambda: rnet.call("rnet_causal_conv_backward", p(dy), p(x), p(w3), p(w7),
+                                   p(w15), p(mix), p(cb), p(dx), *(p(a) for a in gw), B, T, D, 1,
+                                   None)
+        work = f"causal_conv {args.op[5:]} B={B} T={T} D={D}"
+    elif args.op in ("rms_fwd", "rms_bwd"):
+        x, w, y, ri = rnd(N, D), rnd(D), z(N, D), z(N)
+        fwd = lambda: rnet.call("rnet_rms_norm_forward", p(x), p(w), p(y), p(ri), N, D,
+                                F32(1e-6), None)
+        fwd()
+        if args.op == "rms_fwd":
+            fn = fwd
+        else:
+            dy, dx, dw = rnd(N, D), z(N, D), z(D)
+            fn = lambda: rnet.call("rnet_rms_norm_backward", p(dy), p(x), p(w), p(ri), p(dx),
+                                   p(dw), N, D, None)
+        work = f"rms_norm {args.op[4:]} N={N} D={D}"
+    else:
+        raise SystemExit(f"unknown --op {args.op}")
+    for _ in range(max(1, args.warmup)):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"op": args.op, "workload": work,
+                      "ms_per_call": round(e0.elapsed_time(e1) / args.steps, 4)}), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = env_rank()
+    if args.op:
+        run_op(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world, local)
     else:

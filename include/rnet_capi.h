@@ -206,6 +206,8 @@ int rnet_decoder_generate(rnet_decoder* d, int n_steps, int* d_out, int use_grap
 /* Device pointers to the current logits [n_streams, vocab] and next tokens
  * [n_streams], and the state buffer with its size per stream in floats. */
 int rnet_decoder_outputs(rnet_decoder* d, const float** d_logits, const int** d_next);
+/* Host copies of the same (either pointer may be NULL); waits for the stream. */
+int rnet_decoder_outputs_host(rnet_decoder* d, float* h_logits, int* h_next);
 int rnet_decoder_state(rnet_decoder* d, float** d_state, size_t* floats_per_stream);
 
 /* ------------------------------------------------------------------ data parallel

@@ -95,6 +95,7 @@ _SIGS = {
     "rnet_decoder_generate": [_P, _I, _P, _I],
     "rnet_decoder_outputs": [_P, ctypes.POINTER(_P), ctypes.POINTER(_P)],
     "rnet_decoder_state": [_P, ctypes.POINTER(_P), ctypes.POINTER(_SZ)],
+    "rnet_decoder_outputs_host": [_P, _P, _P],
     "rnet_dist_unique_id": [ctypes.c_char_p],
     "rnet_dist_create": [_I, _I, _I, ctypes.c_char_p, _I, ctypes.POINTER(_P)],
     "rnet_dist_destroy": [_P],
@@ -310,6 +311,14 @@ class Decoder:
         lg, nx = _P(), _P()
         check(lib().rnet_decoder_outputs(self.handle, ctypes.byref(lg), ctypes.byref(nx)))
         return lg.value, nx.value
+
+    def outputs_host(self):
+        """(logits [M, V], next tokens [M]) as numpy arrays."""
+        import numpy as np
+        lg = np.empty((self.M, self.model.cfg.vocab_size), np.float32)
+        nx = np.empty(self.M, np.int32)
+        check(lib().rnet_decoder_outputs_host(self.handle, _ptr(lg), _ptr(nx)))
+        return lg, nx
 
     def state(self) -> tuple[int, int]:
         p, n = _P(), _SZ()

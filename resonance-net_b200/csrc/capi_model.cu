@@ -280,6 +280,19 @@ int rnet_decoder_outputs(rnet_decoder* d, const float** d_logits, const int** d_
   return RNET_OK;
 }
 
+int rnet_decoder_outputs_host(rnet_decoder* d, float* h_logits, int* h_next) {
+  if (!d) return rnet_status::fail(RNET_ERR_ARG, "null decoder");
+  cudaStream_t s = d->m->e->stream();
+  const size_t M = d->d.M, V = d->m->e->config().vocab_size;
+  if (h_logits)
+    RNET_TRY_CUDA(cudaMemcpyAsync(h_logits, d->d.logits, M * V * sizeof(float),
+                                  cudaMemcpyDeviceToHost, s));
+  if (h_next)
+    RNET_TRY_CUDA(cudaMemcpyAsync(h_next, d->d.tok, M * sizeof(int), cudaMemcpyDeviceToHost, s));
+  RNET_TRY_CUDA(cudaStreamSynchronize(s));
+  return RNET_OK;
+}
+
 int rnet_decoder_state(rnet_decoder* d, float** d_state, size_t* floats_per_stream) {
   if (!d) return rnet_status::fail(RNET_ERR_ARG, "null decoder");
   if (d_state) *d_state = d->d.state;
