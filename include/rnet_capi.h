@@ -115,6 +115,20 @@ int rnet_swiglu_backward(const float* dy, const float* x, const float* gate_w,
                          float* d_down_w, int batch_seq, int dim, int d_ff, void* stream);
 int rnet_cross_entropy_forward(const float* logits, const int* targets, float* loss,
                                float* dlogits, int batch_seq, int vocab, void* stream);
+/* Same result as rnet_cross_entropy_forward, but allocates nothing: for
+ * callers that cannot allocate device memory while they run (a framework that
+ * owns all device memory through its own pool, or a context where a
+ * cudaMalloc/cudaMallocAsync is not allowed). No counterpart in the reference.
+ * Scratch is a fixed 256 KiB array inside the library's device image, held on
+ * every GPU that loads the library until exit, which limits batch_seq to
+ * 524,280 tokens (larger sizes return RNET_ERR_ARG). The first call on each
+ * device looks up that array's device address; make that first call before
+ * any stream capture. All calls share the array, so calls that overlap on the
+ * GPU (different streams, no ordering between them) race; calls ordered on
+ * one stream are safe. Out-of-range targets are clamped to class 0 without
+ * setting the device error word. */
+int rnet_cross_entropy_forward_noalloc(const float* logits, const int* targets, float* loss,
+                                       float* dlogits, int batch_seq, int vocab, void* stream);
 int rnet_residual_add(float* x, const float* y, size_t n, void* stream);
 int rnet_scale_grads(float* grads, float scale, size_t n, void* stream);
 

@@ -60,6 +60,7 @@ _SIGS = {
     "rnet_swiglu_forward": [_P] * 7 + [_I, _I, _I, _P],
     "rnet_swiglu_backward": [_P] * 11 + [_I, _I, _I, _P],
     "rnet_cross_entropy_forward": [_P, _P, _P, _P, _I, _I, _P],
+    "rnet_cross_entropy_forward_noalloc": [_P, _P, _P, _P, _I, _I, _P],
     "rnet_residual_add": [_P, _P, _SZ, _P],
     "rnet_scale_grads": [_P, _F, _SZ, _P],
     "rnet_model_create": [ctypes.POINTER(ModelConfig), _I, _I, ctypes.POINTER(_P)],
