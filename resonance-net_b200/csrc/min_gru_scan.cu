@@ -6,8 +6,11 @@
 //
 // Layout: one CTA = 8 warps = one sequence b x 32 channels; lane = channel,
 // warp w = time chunk [32w, 32w+32) of the current 256-step segment.
+//   stage:  the segment's inputs ([256 steps x 32 channels] tiles) are copied
+//           global -> shared with cp.async (16 B per copy, all in flight at
+//           once), so the serial part of the scan never waits on DRAM
 //   pass 1: each warp composes its chunk into an affine map h -> A*h + H
-//   exchange (shared memory): carry-in of chunk w = maps of chunks < w
+//   carry:  chunk w's carry-in = the maps of chunks < w (shared memory)
 //   pass 2: each warp re-runs its chunk from the exact carry-in with the
 //           reference's own update h = (1-z) h + z h~ and writes outputs.
 // Segments of 256 steps are chained through a carry so any T works.
@@ -15,47 +18,78 @@
 #include "kernels.cuh"
 
 namespace rnet_k {
+using namespace rnet_dev;
 
 namespace {
 
 constexpr int W = 8;    // warps per CTA = chunks per segment
 constexpr int CL = 32;  // steps per chunk
 constexpr int SEG = W * CL;
+constexpr int CW = 32;  // channels per CTA
+constexpr int TILE = SEG * CW;  // floats per staged tile
 
 __device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + __expf(-v)); }
+
+__device__ __forceinline__ void cp_async16(float* smem, const float* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)),
+               "l"(gmem), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Stage rows [seg0, seg0+SEG) x channels [c0, c0+32) of a row-major [B*T, ld]
+// array into a [SEG][CW] tile (zero-filled outside T / D).
+__device__ __forceinline__ void stage(float* tile, const float* src, int ld, int b, int T, int D,
+                                      int seg0, int c0) {
+  for (int q = threadIdx.x; q < SEG * 8; q += W * 32) {
+    const int row = q >> 3, part = q & 7;
+    const int t = seg0 + row, ch = c0 + part * 4;
+    const bool valid = t < T && ch < D;
+    const float* g = valid ? src + ((size_t)b * T + t) * ld + ch : src;
+    cp_async16(tile + row * CW + part * 4, g, valid);
+  }
+}
 
 __global__ void __launch_bounds__(W * 32)
     scan_fwd_kernel(const float* __restrict__ pz, const float* __restrict__ ph, int ldp,
                     const float* __restrict__ bz, const float* __restrict__ bh,
                     float* __restrict__ zo, float* __restrict__ ho, float* __restrict__ yo,
                     const float* __restrict__ res, float* __restrict__ out, int T, int D) {
+  extern __shared__ float smem[];
+  float* sZ = smem;             // pz, then z
+  float* sT = smem + TILE;      // ph, then h~
+  float* sR = smem + 2 * TILE;  // residual input (only when out != null)
   __shared__ float sA[W][32], sH[W][32];
   __shared__ float carry[32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int groups = (D + 31) / 32;
+  const int groups = (D + CW - 1) / CW;
   const int b = blockIdx.x / groups;
-  const int d = (blockIdx.x % groups) * 32 + lane;
+  const int c0 = (blockIdx.x % groups) * CW;
+  const int d = c0 + lane;
   const bool act = d < D;
   const float bzd = act ? bz[d] : 0.f, bhd = act ? bh[d] : 0.f;
   if (warp == 0) carry[lane] = 0.f;
-  __syncthreads();
   for (int seg0 = 0; seg0 < T; seg0 += SEG) {
-    const int t0 = seg0 + warp * CL;
-    float z[CL], ht[CL];
+    stage(sZ, pz, ldp, b, T, D, seg0, c0);
+    stage(sT, ph, ldp, b, T, D, seg0, c0);
+    if (out) stage(sR, res, D, b, T, D, seg0, c0);
+    cp_async_wait_all();
+    __syncthreads();
+    const int r0 = warp * CL;
     float A = 1.f, H = 0.f;
-#pragma unroll
+#pragma unroll 8
     for (int i = 0; i < CL; ++i) {
-      const int t = t0 + i;
-      if (act && t < T) {
-        const size_t rp = ((size_t)b * T + t) * ldp + d;
-        z[i] = sigmoidf_(pz[rp] + bzd);
-        ht[i] = ph[rp] + bhd;
-      } else {
-        z[i] = 0.f;  // identity step: h unchanged
-        ht[i] = 0.f;
-      }
-      const float a = 1.f - z[i];
-      H = a * H + z[i] * ht[i];
+      const int row = r0 + i;
+      const bool live = act && seg0 + row < T;
+      // steps past T are identity steps (z = 0: h unchanged)
+      const float z = live ? sigmoidf_(sZ[row * CW + lane] + bzd) : 0.f;
+      const float ht = live ? sT[row * CW + lane] + bhd : 0.f;
+      sZ[row * CW + lane] = z;
+      sT[row * CW + lane] = ht;
+      const float a = 1.f - z;
+      H = a * H + z * ht;
       A = a * A;
     }
     sA[warp][lane] = A;
@@ -63,16 +97,18 @@ __global__ void __launch_bounds__(W * 32)
     __syncthreads();
     float h = carry[lane];
     for (int j = 0; j < warp; ++j) h = sA[j][lane] * h + sH[j][lane];
-#pragma unroll
+#pragma unroll 8
     for (int i = 0; i < CL; ++i) {
-      const int t = t0 + i;
-      h = (1.f - z[i]) * h + z[i] * ht[i];
+      const int row = r0 + i;
+      const int t = seg0 + row;
+      const float z = sZ[row * CW + lane];
+      h = (1.f - z) * h + z * sT[row * CW + lane];
       if (act && t < T) {
         const size_t o = ((size_t)b * T + t) * D + d;
-        zo[o] = z[i];
+        zo[o] = z;
         ho[o] = h;
         if (yo) yo[o] = h;
-        if (out) out[o] = res[o] + h;
+        if (out) out[o] = sR[row * CW + lane] + h;
       }
     }
     __syncthreads();
@@ -87,37 +123,38 @@ __global__ void __launch_bounds__(W * 32)
                     const float* __restrict__ bh, float* __restrict__ dz,
                     float* __restrict__ dht, int ldd, float* __restrict__ dbz,
                     float* __restrict__ dbh, int T, int D) {
+  extern __shared__ float smem[];
+  float* sZ = smem;
+  float* sG = smem + TILE;
+  float* sP = smem + 2 * TILE;
   __shared__ float sA[W][32], sH[W][32];
   __shared__ float carry[32];
   __shared__ float sbz[W][32], sbh[W][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int groups = (D + 31) / 32;
+  const int groups = (D + CW - 1) / CW;
   const int b = blockIdx.x / groups;
-  const int d = (blockIdx.x % groups) * 32 + lane;
+  const int c0 = (blockIdx.x % groups) * CW;
+  const int d = c0 + lane;
   const bool act = d < D;
   const float bhd = act ? bh[d] : 0.f;
   if (warp == 0) carry[lane] = 0.f;
   float accz = 0.f, acch = 0.f;
-  __syncthreads();
   const int nseg = (T + SEG - 1) / SEG;
   for (int sg = nseg - 1; sg >= 0; --sg) {
-    // chunk of this warp in reverse order: warp 0 owns the LAST chunk
-    const int t0 = sg * SEG + (W - 1 - warp) * CL;
-    float zz[CL], g[CL];
+    const int seg0 = sg * SEG;
+    stage(sZ, z, D, b, T, D, seg0, c0);
+    stage(sG, dy, D, b, T, D, seg0, c0);
+    stage(sP, ph, ldp, b, T, D, seg0, c0);
+    cp_async_wait_all();
+    __syncthreads();
+    // warp 0 owns the LAST chunk of the segment (reverse time order)
+    const int r0 = (W - 1 - warp) * CL;
     float A = 1.f, H = 0.f;  // dh_out = A * dh_in + H  (dh after the *= (1-z) step)
-#pragma unroll
+#pragma unroll 8
     for (int i = CL - 1; i >= 0; --i) {
-      const int t = t0 + i;
-      if (act && t < T) {
-        const size_t o = ((size_t)b * T + t) * D + d;
-        zz[i] = z[o];
-        g[i] = dy[o];
-      } else {
-        zz[i] = 0.f;  // a = 1, no gradient injection
-        g[i] = 0.f;
-      }
-      const float a = 1.f - zz[i];
-      H = a * (H + g[i]);
+      const int row = r0 + i;
+      const float a = 1.f - sZ[row * CW + lane];  // zero-filled past T: a = 1, g = 0
+      H = a * (H + sG[row * CW + lane]);
       A = a * A;
     }
     sA[warp][lane] = A;
@@ -125,17 +162,17 @@ __global__ void __launch_bounds__(W * 32)
     __syncthreads();
     float dh = carry[lane];
     for (int j = 0; j < warp; ++j) dh = sA[j][lane] * dh + sH[j][lane];
-#pragma unroll
+#pragma unroll 8
     for (int i = CL - 1; i >= 0; --i) {
-      const int t = t0 + i;
-      dh += g[i];
+      const int row = r0 + i;
+      const int t = seg0 + row;
+      const float zv = sZ[row * CW + lane];
+      dh += sG[row * CW + lane];
       if (act && t < T) {
         const size_t o = ((size_t)b * T + t) * D + d;
-        const size_t rp = ((size_t)b * T + t) * ldp + d;
         const size_t od = ((size_t)b * T + t) * ldd + d;
-        const float htv = ph[rp] + bhd;
+        const float htv = sP[row * CW + lane] + bhd;
         const float hp = t > 0 ? h[o - D] : 0.f;
-        const float zv = zz[i];
         const float vz = dh * (htv - hp) * zv * (1.f - zv);
         const float vh = dh * zv;
         dz[od] = vz;
@@ -143,7 +180,7 @@ __global__ void __launch_bounds__(W * 32)
         accz += vz;
         acch += vh;
       }
-      dh = dh * (1.f - zz[i]);
+      dh = dh * (1.f - zv);
     }
     __syncthreads();
     if (warp == W - 1) carry[lane] = dh;
@@ -160,14 +197,26 @@ __global__ void __launch_bounds__(W * 32)
   }
 }
 
+template <class K>
+void allow_smem(K kernel, size_t bytes) {
+  static bool done = false;
+  if (!done) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    done = true;
+  }
+}
+
 }  // namespace
 
 cudaError_t gru_scan_fwd(const float* pz, const float* ph, int ldp, const float* bz,
                          const float* bh, float* z, float* h, float* y, const float* res,
                          float* out, int B, int T, int D, cudaStream_t s) {
   if (B <= 0 || T <= 0) return cudaSuccess;
-  const int grid = B * ((D + 31) / 32);
-  scan_fwd_kernel<<<grid, W * 32, 0, s>>>(pz, ph, ldp, bz, bh, z, h, y, res, out, T, D);
+  if (D % 4 || ldp % 4) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)(out ? 3 : 2) * TILE * sizeof(float);
+  allow_smem(scan_fwd_kernel, 3 * TILE * sizeof(float));
+  const int grid = B * ((D + CW - 1) / CW);
+  scan_fwd_kernel<<<grid, W * 32, smem, s>>>(pz, ph, ldp, bz, bh, z, h, y, res, out, T, D);
   return launched();
 }
 
@@ -175,8 +224,11 @@ cudaError_t gru_scan_bwd(const float* dy, const float* z, const float* h, const 
                          int ldp, const float* bh, float* dz, float* dht, int ldd, float* dbz,
                          float* dbh, int B, int T, int D, cudaStream_t s) {
   if (B <= 0 || T <= 0) return cudaSuccess;
-  const int grid = B * ((D + 31) / 32);
-  scan_bwd_kernel<<<grid, W * 32, 0, s>>>(dy, z, h, ph, ldp, bh, dz, dht, ldd, dbz, dbh, T, D);
+  if (D % 4 || ldp % 4) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)3 * TILE * sizeof(float);
+  allow_smem(scan_bwd_kernel, smem);
+  const int grid = B * ((D + CW - 1) / CW);
+  scan_bwd_kernel<<<grid, W * 32, smem, s>>>(dy, z, h, ph, ldp, bh, dz, dht, ldd, dbz, dbh, T, D);
   return launched();
 }
 
