@@ -1,18 +1,25 @@
 // Persistent warp-specialised tcgen05 GEMM for sm_100a with 3xTF32 error
 // compensation, so fp32 operands give fp32-class results on the tensor cores.
 //
-// Every fp32 operand x is split into hi = rna_tf32(x) and lo = x - hi inside
-// shared memory; each 8-deep K slice issues three kind::tf32 UMMAs
-// (hi*lo, lo*hi, hi*hi) into one fp32 TMEM accumulator. The hi*hi product is
-// exact in fp32 terms; the dropped lo*lo term is ~2^-22 relative.
+// A tf32 operand read keeps the top 19 bits of an fp32 word (the low 13
+// mantissa bits are ignored), so the raw fp32 tile already IS the "hi" part.
+// Split warps only compute lo = x - (x with the low 13 bits cleared) into a
+// twin buffer; each 8-deep K slice then issues three kind::tf32 UMMAs
+// (hi*lo, lo*hi, hi*hi) into one fp32 TMEM accumulator. The dropped lo*lo
+// term is ~2^-22 relative.
 //
 // Roles (448 threads = 14 warps):
 //   warps 0-3  epilogue (warp w owns TMEM lanes 32w..32w+31 = tile rows)
-//   warp  4    TMA producer (raw fp32 tiles, SWIZZLE_128B)
+//   warp  4    TMA producer (raw fp32 tiles)
 //   warp  5    TMEM allocator + single-thread UMMA issuer
-//   warps 6-13 split warps (raw -> hi in place, lo into the twin buffer)
+//   warps 6-13 split warps (lo = x - trunc_tf32(x) into the twin buffer)
 // Pipelines: full[s] (TMA tx) -> split[s] (8 warp arrivals) -> empty[s]
 // (tcgen05.commit); accumulators double-buffered in TMEM with accf/acce.
+//
+// K-blocks are 16 fp32 deep (64-byte rows, SWIZZLE_64B for K-major operands,
+// SWIZZLE_128B_ATOM_32B boxes of 32 x 16 for MN-major ones), which fits 4
+// pipeline stages at BN = 256 (6 at BN = 128): the pipeline is latency-bound
+// with fewer stages.
 //
 // Reference parity: replaces every cublasSgemm call of the reference
 // (src/min_gru.cu:64-178, src/causal_conv.cu:76-165, src/slot_memory.cu:91-235,
@@ -30,13 +37,13 @@ namespace rnet_gemm {
 using namespace rnet_dev;
 
 constexpr int BM = 128;
-constexpr int BK = 32;  // fp32 elements = 128 B = one SWIZZLE_128B row
 constexpr int NUM_EPI_WARPS = 4;
 constexpr int PRODUCER_WARP = 4;
 constexpr int MMA_WARP = 5;
 constexpr int FIRST_SPLIT_WARP = 6;
 constexpr int NUM_SPLIT_WARPS = 8;
 constexpr int NUM_THREADS = 32 * (FIRST_SPLIT_WARP + NUM_SPLIT_WARPS);
+constexpr int SMEM_BUDGET = 200 * 1024;  // pipeline stages (barriers etc. extra)
 
 struct KParams {
   int M, N, K;
@@ -49,15 +56,23 @@ struct KParams {
   unsigned* err;
 };
 
-template <int BN>
+template <int BN, int BK>
 struct Cfg {
+  static constexpr int ROW_BYTES = BK * 4;            // K-major row (64 or 128 B)
+  static constexpr int MN_CHUNK = 128 * BK;           // MN-major box: 32 elems x BK rows
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int RAW_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGE_BYTES = 2 * RAW_BYTES;  // raw(hi) + lo
-  static constexpr int STAGES = (BN == 256) ? 2 : 3;
+  static constexpr int STAGE_BYTES = 2 * RAW_BYTES;  // raw (= hi) + lo
+  static constexpr int STAGES_FIT = SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  // UMMA smem-descriptor parameters
+  static constexpr uint32_t K_LAYOUT = BK == 32 ? 2u : 4u;  // SWIZZLE_128B / SWIZZLE_64B
+  static constexpr uint32_t K_SBO = 8 * ROW_BYTES;          // 8-row core-matrix group
+  static_assert(BK == 16 || BK == 32, "BK");
+  static_assert(STAGES >= 2, "stages");
 };
 
 __device__ __forceinline__ void unit_range(const KParams& p, int unit, int& mt, int& nt0,
@@ -83,7 +98,6 @@ __device__ __forceinline__ void unit_range(const KParams& p, int unit, int& mt, 
 __device__ __forceinline__ float silu_fast(float g) { return g / (1.0f + __expf(-g)); }
 
 // ------------------------------------------------------------------ epilogue
-template <int BN>
 __device__ __forceinline__ void store_row_chunk(const KParams& p, int kind, int row, int col0,
                                                 const float (&v)[32]) {
   const Epilogue& e = p.epi;
@@ -187,7 +201,7 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
     for (int c = 0; c < BN / 32; ++c) {
       tmem_ld_32cols(tacc + c * 32, v);
       const int s0 = nt * BN + c * 32;
-      if (e.C != nullptr && row < p.M) store_row_chunk<BN>(p, EPI_STORE, row, s0, v);
+      if (e.C != nullptr && row < p.M) store_row_chunk(p, EPI_STORE, row, s0, v);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int s = s0 + i;
@@ -215,16 +229,16 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
     tmem_ld_32cols(tacc + c * 32, v);
-    store_row_chunk<BN>(p, e.kind, row, nt * BN + c * 32, v);
+    store_row_chunk(p, e.kind, row, nt * BN + c * 32, v);
   }
 }
 
 // ------------------------------------------------------------------ kernel
-template <int BN>
+template <int BN, int BK>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, const KParams p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, BK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -287,7 +301,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               tma_load_2d(sa, &tmA, &full[s], k0, m0);
             } else {
 #pragma unroll
-              for (int j = 0; j < BM / 32; ++j) tma_load_2d(sa + j * 4096, &tmA, &full[s], m0 + 32 * j, k0);
+              for (int j = 0; j < BM / 32; ++j)
+                tma_load_2d(sa + j * C::MN_CHUNK, &tmA, &full[s], m0 + 32 * j, k0);
             }
             if (p.b_pair_off == 0) {
               const int n0 = nt * BN;
@@ -295,18 +310,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tma_load_2d(sb, &tmB, &full[s], k0, n0);
               } else {
 #pragma unroll
-                for (int j = 0; j < BN / 32; ++j) tma_load_2d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, k0);
+                for (int j = 0; j < BN / 32; ++j)
+                  tma_load_2d(sb + j * C::MN_CHUNK, &tmB, &full[s], n0 + 32 * j, k0);
               }
             } else {
               const int n0 = nt * (BN / 2);
               if (!p.b_mn) {
                 tma_load_2d(sb, &tmB, &full[s], k0, n0);
-                tma_load_2d(sb + (BN / 2) * 128, &tmB, &full[s], k0, n0 + p.b_pair_off);
+                tma_load_2d(sb + (BN / 2) * C::ROW_BYTES, &tmB, &full[s], k0, n0 + p.b_pair_off);
               } else {
 #pragma unroll
                 for (int j = 0; j < BN / 64; ++j) {
-                  tma_load_2d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, k0);
-                  tma_load_2d(sb + (j + BN / 64) * 4096, &tmB, &full[s], n0 + p.b_pair_off + 32 * j, k0);
+                  tma_load_2d(sb + j * C::MN_CHUNK, &tmB, &full[s], n0 + 32 * j, k0);
+                  tma_load_2d(sb + (j + BN / 64) * C::MN_CHUNK, &tmB, &full[s],
+                              n0 + p.b_pair_off + 32 * j, k0);
                 }
               }
             }
@@ -317,15 +334,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == MMA_WARP) {
     if (lane == 0) {
       const uint32_t idesc = make_idesc(BM, BN, 2, p.a_mn, p.b_mn);
-      // Byte advance of one 8-deep K slice and the LBO/SBO of each operand.
+      // Byte advance of one 8-deep K slice and LBO / SBO / layout per operand.
       const uint32_t a_kstep = p.a_mn ? 1024u : 32u;
       const uint32_t b_kstep = p.b_mn ? 1024u : 32u;
-      const uint32_t a_lbo = p.a_mn ? 4096u : 16u;
-      const uint32_t b_lbo = p.b_mn ? 4096u : 16u;
-      const uint32_t a_sbo = p.a_mn ? 512u : 1024u;
-      const uint32_t b_sbo = p.b_mn ? 512u : 1024u;
-      const uint32_t a_lay = p.a_mn ? 1u : 2u;
-      const uint32_t b_lay = p.b_mn ? 1u : 2u;
+      const uint32_t a_lbo = p.a_mn ? (uint32_t)C::MN_CHUNK : 16u;
+      const uint32_t b_lbo = p.b_mn ? (uint32_t)C::MN_CHUNK : 16u;
+      const uint32_t a_sbo = p.a_mn ? 512u : C::K_SBO;
+      const uint32_t b_sbo = p.b_mn ? 512u : C::K_SBO;
+      const uint32_t a_lay = p.a_mn ? 1u : C::K_LAYOUT;
+      const uint32_t b_lay = p.b_mn ? 1u : C::K_LAYOUT;
       uint32_t it = 0, tc = 0;
       bool ok = true;
       for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
@@ -379,19 +396,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           if (!mbar_wait(&full[s], ph, p.err, abort_flag)) { ok = false; break; }
-          float4* raw = reinterpret_cast<float4*>(smem + s * C::STAGE_BYTES);
+          const float4* raw = reinterpret_cast<const float4*>(smem + s * C::STAGE_BYTES);
           float4* lo = reinterpret_cast<float4*>(smem + s * C::STAGE_BYTES + C::RAW_BYTES);
+          // lo = x - (x with the low 13 mantissa bits cleared); the layout is
+          // elementwise-identical to the raw tile, so swizzling is irrelevant
 #pragma unroll 4
           for (int i = t; i < N4; i += NT) {
-            float4 x = raw[i];
-            float4 h, l;
-            uint32_t u;
-            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x.x)); h.x = __uint_as_float(u);
-            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x.y)); h.y = __uint_as_float(u);
-            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x.z)); h.z = __uint_as_float(u);
-            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x.w)); h.w = __uint_as_float(u);
-            l.x = x.x - h.x; l.y = x.y - h.y; l.z = x.z - h.z; l.w = x.w - h.w;
-            raw[i] = h;
+            const float4 x = raw[i];
+            float4 l;
+            l.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+            l.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+            l.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+            l.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
             lo[i] = l;
           }
           fence_proxy_async_smem();
@@ -444,20 +460,18 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// 2-D fp32 tensor map with a 128-byte inner box. K-major tiles use
-// SWIZZLE_128B; MN-major tiles use SWIZZLE_128B_ATOM_32B (the layout UMMA
-// requires for MN-major tf32 operands).
+// 2-D fp32 tensor map. box = {box_inner, box_outer} elements.
 static bool make_map(CUtensorMap* m, const float* base, uint64_t inner, uint64_t outer,
-                     uint64_t ld_elems, uint32_t box_outer, bool mn_major) {
+                     uint64_t ld_elems, uint32_t box_inner, uint32_t box_outer,
+                     CUtensorMapSwizzle swz) {
   auto enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {ld_elems * sizeof(float)};
-  cuuint32_t box[2] = {32, box_outer};
+  cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -473,20 +487,20 @@ int num_sms() {
   return n;
 }
 
-template <int BN>
+template <int BN, int BK>
 static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
                           const KParams& kp) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, BK>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
   const int grid = kp.num_units < num_sms() ? kp.num_units : num_sms();
-  gemm_tf32x3_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ta, tb, kp);
+  gemm_tf32x3_kernel<BN, BK><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ta, tb, kp);
   return rnet_k::launched();
 }
 
@@ -498,10 +512,14 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   if ((A.ld % 4) || (B.ld % 4) || (reinterpret_cast<uintptr_t>(A.p) & 15) ||
       (reinterpret_cast<uintptr_t>(B.p) & 15))
     return cudaErrorInvalidValue;
-  // Paired-B epilogues need BN/2 = 64 aligned feature halves -> BN = 128.
+  // Paired-B and row-owner epilogues use 128-wide tiles (64-feature halves).
   const bool paired = b_pair_off > 0;
   const bool row_owner = epi.kind == EPI_TOP2;
   const int BN = (paired || row_owner || N <= 128) ? 128 : 256;
+  // 16-deep K-blocks (4 stages at BN=256) measured 5-20% faster than 32-deep
+  // (2 stages) on every step shape; the 32-deep instantiation is kept for
+  // shapes that may prefer it.
+  constexpr int BK = 16;
   const int n_logical_tile = paired ? BN / 2 : BN;
 
   KParams kp{};
@@ -524,11 +542,13 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
       splits = k_splits;
     } else {
       const int tiles = kp.m_tiles * kp.n_tiles;
-      if (tiles < num_sms()) {
-        splits = num_sms() / tiles;
-        const int max_splits = kp.kb_total / 4 > 0 ? kp.kb_total / 4 : 1;  // >= 4 k-blocks each
-        if (splits > max_splits) splits = max_splits;
-      }
+      if (tiles < num_sms()) splits = num_sms() / tiles;
+      // keep each split's K at most 2048 so the TMEM accumulation stays
+      // fp32-accurate, and at least 4 k-blocks so a split is worth a tile
+      const int min_splits = (K + 2047) / 2048;
+      if (splits < min_splits) splits = min_splits;
+      const int max_splits = kp.kb_total / 4 > 0 ? kp.kb_total / 4 : 1;
+      if (splits > max_splits) splits = max_splits;
     }
   }
   if (splits < 1) splits = 1;
@@ -536,22 +556,28 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   kp.k_splits = (kp.kb_total + kp.kb_per_split - 1) / kp.kb_per_split;
   kp.num_units = row_owner ? kp.m_tiles : kp.m_tiles * kp.n_tiles * kp.k_splits;
 
+  const CUtensorMapSwizzle kswz = BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapSwizzle mswz = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   CUtensorMap ta, tb;
   bool ok;
   if (!A.mn_major)
-    ok = make_map(&ta, A.p, (uint64_t)K, (uint64_t)M, A.ld, BM, false);
+    ok = make_map(&ta, A.p, (uint64_t)K, (uint64_t)M, A.ld, BK, BM, kswz);
   else
-    ok = make_map(&ta, A.p, (uint64_t)M, (uint64_t)K, A.ld, 32, true);
+    ok = make_map(&ta, A.p, (uint64_t)M, (uint64_t)K, A.ld, 32, BK, mswz);
   if (!ok) return cudaErrorInvalidValue;
   const uint64_t b_rows = paired ? (uint64_t)b_pair_off + N : (uint64_t)N;
   if (!B.mn_major)
-    ok = make_map(&tb, B.p, (uint64_t)K, b_rows, B.ld, paired ? BN / 2 : BN, false);
+    ok = make_map(&tb, B.p, (uint64_t)K, b_rows, B.ld, BK, paired ? BN / 2 : BN, kswz);
   else
-    ok = make_map(&tb, B.p, b_rows, (uint64_t)K, B.ld, 32, true);
+    ok = make_map(&tb, B.p, b_rows, (uint64_t)K, B.ld, 32, BK, mswz);
   if (!ok) return cudaErrorInvalidValue;
 
-  if (BN == 128) return launch<128>(stream, ta, tb, kp);
-  return launch<256>(stream, ta, tb, kp);
+  if (BK == 32) {
+    if (BN == 128) return launch<128, 32>(stream, ta, tb, kp);
+    return launch<256, 32>(stream, ta, tb, kp);
+  }
+  if (BN == 128) return launch<128, 16>(stream, ta, tb, kp);
+  return launch<256, 16>(stream, ta, tb, kp);
 }
 
 }  // namespace rnet_gemm
