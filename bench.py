@@ -427,6 +427,24 @@ def run_op(args):
                                    p(w15), p(mix), p(cb), p(dx), *(p(a) for a in gw), B, T, D, 1,
                                    None)
         work = f"causal_conv {args.op[5:]} B={B} T={T} D={D}"
+    elif args.op in ("swiglu_fwd", "swiglu_bwd"):
+        Fd = CFG["d_ff"]
+        x = rnd(N, D)
+        gu = rnd(2 * Fd, D, scale=D ** -0.5)  # gate|up contiguous -> paired GEMM
+        down = rnd(D, Fd, scale=Fd ** -0.5)
+        y, gc, uc = z(N, D), z(N, Fd), z(N, Fd)
+        gate, up = gu[:Fd], gu[Fd:]
+        fwd = lambda: rnet.call("rnet_swiglu_forward", p(x), p(y), p(gate), p(up), p(down),
+                                p(gc), p(uc), N, D, Fd, None)
+        fwd()
+        if args.op == "swiglu_fwd":
+            fn = fwd
+        else:
+            dy, dx = rnd(N, D), z(N, D)
+            gg, gup, gd = z(Fd, D), z(Fd, D), z(D, Fd)
+            fn = lambda: rnet.call("rnet_swiglu_backward", p(dy), p(x), p(gate), p(up), p(down),
+                                   p(gc), p(uc), p(dx), p(gg), p(gup), p(gd), N, D, Fd, None)
+        work = f"swiglu {args.op[7:]} N={N} D={D} F={Fd}"
     elif args.op in ("rms_fwd", "rms_bwd"):
         x, w, y, ri = rnd(N, D), rnd(D), z(N, D), z(N)
         fwd = lambda: rnet.call("rnet_rms_norm_forward", p(x), p(w), p(y), p(ri), N, D,

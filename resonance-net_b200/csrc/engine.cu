@@ -74,6 +74,7 @@ Engine::~Engine() {
   cudaFree(VT_);
   cudaFree(dKT_);
   cudaFree(dVT_);
+  for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
   cudaFree(scratch_);
   cudaFree(arena_);
   if (stream_) cudaStreamDestroy(stream_);

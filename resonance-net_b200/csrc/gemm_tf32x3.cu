@@ -44,6 +44,8 @@ constexpr int FIRST_SPLIT_WARP = 6;
 constexpr int NUM_SPLIT_WARPS = 8;
 constexpr int NUM_THREADS = 32 * (FIRST_SPLIT_WARP + NUM_SPLIT_WARPS);
 constexpr int SMEM_BUDGET = 200 * 1024;  // pipeline stages (barriers etc. extra)
+constexpr int TILE_LD = 33;              // epilogue transpose tile: 32 x 33 floats per warp
+constexpr int EPI_TILE_FLOATS = 32 * TILE_LD;
 
 struct KParams {
   int M, N, K;
@@ -67,7 +69,8 @@ struct Cfg {
   static constexpr int STAGES_FIT = SMEM_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int EPI_BYTES = NUM_EPI_WARPS * EPI_TILE_FLOATS * 4;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
   // UMMA smem-descriptor parameters
   static constexpr uint32_t K_LAYOUT = BK == 32 ? 2u : 4u;  // SWIZZLE_128B / SWIZZLE_64B
   static constexpr uint32_t K_SBO = 8 * ROW_BYTES;          // 8-row core-matrix group
@@ -98,6 +101,86 @@ __device__ __forceinline__ void unit_range(const KParams& p, int unit, int& mt, 
 __device__ __forceinline__ float silu_fast(float g) { return g / (1.0f + __expf(-g)); }
 
 // ------------------------------------------------------------------ epilogue
+// The accumulator arrives thread-per-row (TMEM lane = tile row, 32 columns
+// per tcgen05.ld). The SwiGLU epilogues, which move three [N, F] planes per
+// tile, go through a per-warp 32x33 shared-memory tile so that a warp
+// instruction touches four full 128-byte row segments (coalesced float4)
+// instead of 32 rows; the other kinds store thread-per-row directly.
+// Thread `lane` holds row (row0 + lane) x columns [col0, col0 + 32) in v.
+// Writes the 32x32 block to dst (row stride ld) with coalesced float4 stores:
+// op 0 = store, 1 = red.add, 2 = store R + v (R row stride ldr).
+__device__ __forceinline__ void tile_out(float* st, const float (&v)[32], float* dst, int ld,
+                                         const float* R, int ldr, int row0, int col0, int M,
+                                         int N, int op) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) st[lane * TILE_LD + i] = v[i];
+  __syncwarp();
+  const int cc = (lane & 7) * 4;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int rr = j * 4 + (lane >> 3);
+    const int row = row0 + rr, col = col0 + cc;
+    if (row < M) {
+      const float* s = st + rr * TILE_LD + cc;
+      float4 x = make_float4(s[0], s[1], s[2], s[3]);
+      float* g = dst + (size_t)row * ld + col;
+      if (col + 4 <= N) {
+        if (op == 1) {
+          red_add_v4(g, x.x, x.y, x.z, x.w);
+        } else {
+          if (op == 2) {
+            const float4 r = *reinterpret_cast<const float4*>(R + (size_t)row * ldr + col);
+            x.x += r.x; x.y += r.y; x.z += r.z; x.w += r.w;
+          }
+          *reinterpret_cast<float4*>(g) = x;
+        }
+      } else {
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+        for (int q = 0; q < 4 && col + q < N; ++q) {
+          if (op == 1) atomicAdd(g + q, xs[q]);
+          else g[q] = xs[q] + (op == 2 ? R[(size_t)row * ldr + col + q] : 0.f);
+        }
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// Inverse of tile_out for loads: thread `lane` receives row (row0 + lane) x
+// columns [col0, col0 + 32) of src (row stride ld); out-of-range reads as 0.
+__device__ __forceinline__ void tile_in(float* st, float (&v)[32], const float* src, int ld,
+                                        int row0, int col0, int M, int N) {
+  const int lane = threadIdx.x & 31;
+  const int cc = (lane & 7) * 4;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int rr = j * 4 + (lane >> 3);
+    const int row = row0 + rr, col = col0 + cc;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < M) {
+      const float* g = src + (size_t)row * ld + col;
+      if (col + 4 <= N) {
+        x = *reinterpret_cast<const float4*>(g);
+      } else {
+        if (col < N) x.x = g[0];
+        if (col + 1 < N) x.y = g[1];
+        if (col + 2 < N) x.z = g[2];
+      }
+    }
+    float* s = st + rr * TILE_LD + cc;
+    s[0] = x.x; s[1] = x.y; s[2] = x.z; s[3] = x.w;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = st[lane * TILE_LD + i];
+  __syncwarp();
+}
+
+// Direct thread-per-row store of one 32-column chunk (row stride ld): eight
+// float4 per thread. For plain stores / split-K reductions / residual adds
+// this beats staging through shared memory, which competes with the
+// operand pipeline for shared-memory bandwidth.
 __device__ __forceinline__ void store_row_chunk(const KParams& p, int kind, int row, int col0,
                                                 const float (&v)[32]) {
   const Epilogue& e = p.epi;
@@ -120,13 +203,12 @@ __device__ __forceinline__ void store_row_chunk(const KParams& p, int kind, int 
       float4* dst = reinterpret_cast<float4*>(e.C + (size_t)row * e.ldc + col0);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float4 q = r[j];
+        const float4 q = r[j];
         dst[j] = make_float4(q.x + a * v[4 * j], q.y + a * v[4 * j + 1], q.z + a * v[4 * j + 2],
                              q.w + a * v[4 * j + 3]);
       }
     }
   } else {
-#pragma unroll
     for (int i = 0; i < 32; ++i) {
       const int col = col0 + i;
       if (col < p.N) {
@@ -144,10 +226,15 @@ struct Top2State {
   int i0, i1;
 };
 
+// One accumulator sub-tile (128 rows x BN columns); warp q handles rows
+// row0 = m0 + 32q .. +31, `st` is the warp's smem tile.
 template <int BN>
-__device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc, int row,
-                                                 int nt, bool last_sub, Top2State& st) {
+__device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc, int row0,
+                                                 int nt, bool last_sub, Top2State& st,
+                                                 float* tile) {
   const Epilogue& e = p.epi;
+  const int lane = threadIdx.x & 31;
+  const int row = row0 + lane;
   float v[32];
   if (e.kind == EPI_SWIGLU_FWD) {
     constexpr int HALF_CHUNKS = BN / 64;
@@ -157,18 +244,11 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
       tmem_ld_32cols(tacc + c * 32, g);
       tmem_ld_32cols(tacc + (c + HALF_CHUNKS) * 32, v);
       const int f0 = nt * (BN / 2) + c * 32;
-      if (row < p.M) {
+      tile_out(tile, g, e.G, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0);
+      tile_out(tile, v, e.U, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int f = f0 + i;
-          if (f < p.N) {
-            const size_t o = (size_t)row * e.ldf + f;
-            e.G[o] = g[i];
-            e.U[o] = v[i];
-            e.H[o] = silu_fast(g[i]) * v[i];
-          }
-        }
-      }
+      for (int i = 0; i < 32; ++i) v[i] = silu_fast(g[i]) * v[i];
+      tile_out(tile, v, e.H, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0);
     }
     return;
   }
@@ -177,22 +257,22 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
     for (int c = 0; c < BN / 32; ++c) {
       tmem_ld_32cols(tacc + c * 32, v);
       const int f0 = nt * BN + c * 32;
-      if (row < p.M) {
+      // Two 32-float arrays live at a time: dU is stored before U is read.
+      float g[32];
+      tile_in(tile, g, e.Gc, e.ldf, row0, f0, p.M, p.N);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int f = f0 + i;
-          if (f < p.N) {
-            const size_t o = (size_t)row * e.ldf + f;
-            const float g = e.Gc[o], u = e.Uc[o];
-            const float sig = 1.0f / (1.0f + __expf(-g));
-            const float dsilu = sig + g * sig * (1.0f - sig);
-            const float dh = v[i];
-            float* dgu = e.C + (size_t)row * e.ldc;
-            dgu[f] = dh * u * dsilu;
-            dgu[p.N + f] = dh * (g * sig);
-          }
-        }
+      for (int i = 0; i < 32; ++i) {
+        const float sig = 1.0f / (1.0f + __expf(-g[i]));
+        const float dsilu = sig + g[i] * sig * (1.0f - sig);
+        const float dh = v[i];
+        v[i] = dh * (g[i] * sig);  // dU
+        g[i] = dh * dsilu;         // dG / u
       }
+      tile_out(tile, v, e.C + p.N, e.ldc, nullptr, 0, row0, f0, p.M, p.N, 0);
+      tile_in(tile, v, e.Uc, e.ldf, row0, f0, p.M, p.N);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= g[i];  // dG
+      tile_out(tile, v, e.C, e.ldc, nullptr, 0, row0, f0, p.M, p.N, 0);
     }
     return;
   }
@@ -201,7 +281,7 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
     for (int c = 0; c < BN / 32; ++c) {
       tmem_ld_32cols(tacc + c * 32, v);
       const int s0 = nt * BN + c * 32;
-      if (e.C != nullptr && row < p.M) store_row_chunk(p, EPI_STORE, row, s0, v);
+      if (e.C != nullptr) store_row_chunk(p, EPI_STORE, row, s0, v);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int s = s0 + i;
@@ -233,6 +313,48 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
   }
 }
 
+// ------------------------------------------------------------------ TMA tiles
+// A tile [BM x BK] of k-block k0 / m-tile m0 into sa.
+template <int BN, int BK>
+__device__ __forceinline__ void load_a(uint8_t* sa, const void* map, uint64_t* bar,
+                                       const KParams& p, int k0, int m0) {
+  using C = Cfg<BN, BK>;
+  if (!p.a_mn) {
+    tma_load_2d(sa, map, bar, k0, m0);
+  } else {
+#pragma unroll
+    for (int j = 0; j < BM / 32; ++j) tma_load_2d(sa + j * C::MN_CHUNK, map, bar, m0 + 32 * j, k0);
+  }
+}
+
+// B tile [BN x BK] of n-tile nt (two halves for paired operands) into sb.
+template <int BN, int BK>
+__device__ __forceinline__ void load_b(uint8_t* sb, const void* map, uint64_t* bar,
+                                       const KParams& p, int k0, int nt) {
+  using C = Cfg<BN, BK>;
+  if (p.b_pair_off == 0) {
+    const int n0 = nt * BN;
+    if (!p.b_mn) {
+      tma_load_2d(sb, map, bar, k0, n0);
+    } else {
+#pragma unroll
+      for (int j = 0; j < BN / 32; ++j) tma_load_2d(sb + j * C::MN_CHUNK, map, bar, n0 + 32 * j, k0);
+    }
+  } else {
+    const int n0 = nt * (BN / 2);
+    if (!p.b_mn) {
+      tma_load_2d(sb, map, bar, k0, n0);
+      tma_load_2d(sb + (BN / 2) * C::ROW_BYTES, map, bar, k0, n0 + p.b_pair_off);
+    } else {
+#pragma unroll
+      for (int j = 0; j < BN / 64; ++j) {
+        tma_load_2d(sb + j * C::MN_CHUNK, map, bar, n0 + 32 * j, k0);
+        tma_load_2d(sb + (j + BN / 64) * C::MN_CHUNK, map, bar, n0 + p.b_pair_off + 32 * j, k0);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 template <int BN, int BK>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -242,7 +364,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  float* epi_tiles = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES);
   uint64_t* full = bars;
   uint64_t* split = bars + C::STAGES;
   uint64_t* empty = bars + 2 * C::STAGES;
@@ -297,36 +420,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_arrive_expect_tx(&full[s], C::RAW_BYTES);
             const int k0 = kb * BK;
             const int m0 = mt * BM;
-            if (!p.a_mn) {
-              tma_load_2d(sa, &tmA, &full[s], k0, m0);
-            } else {
-#pragma unroll
-              for (int j = 0; j < BM / 32; ++j)
-                tma_load_2d(sa + j * C::MN_CHUNK, &tmA, &full[s], m0 + 32 * j, k0);
-            }
-            if (p.b_pair_off == 0) {
-              const int n0 = nt * BN;
-              if (!p.b_mn) {
-                tma_load_2d(sb, &tmB, &full[s], k0, n0);
-              } else {
-#pragma unroll
-                for (int j = 0; j < BN / 32; ++j)
-                  tma_load_2d(sb + j * C::MN_CHUNK, &tmB, &full[s], n0 + 32 * j, k0);
-              }
-            } else {
-              const int n0 = nt * (BN / 2);
-              if (!p.b_mn) {
-                tma_load_2d(sb, &tmB, &full[s], k0, n0);
-                tma_load_2d(sb + (BN / 2) * C::ROW_BYTES, &tmB, &full[s], k0, n0 + p.b_pair_off);
-              } else {
-#pragma unroll
-                for (int j = 0; j < BN / 64; ++j) {
-                  tma_load_2d(sb + j * C::MN_CHUNK, &tmB, &full[s], n0 + 32 * j, k0);
-                  tma_load_2d(sb + (j + BN / 64) * C::MN_CHUNK, &tmB, &full[s],
-                              n0 + p.b_pair_off + 32 * j, k0);
-                }
-              }
-            }
+            load_a<BN, BK>(sa, &tmA, &full[s], p, k0, m0);
+            load_b<BN, BK>(sb, &tmB, &full[s], p, k0, nt);
           }
         }
       }
@@ -431,7 +526,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!mbar_wait(&accf[ab], tph, p.err, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN;
-        epilogue_subtile<BN>(p, tacc, row, nt, nt == nt1 - 1, st);
+        epilogue_subtile<BN>(p, tacc, mt * BM + q * 32, nt, nt == nt1 - 1, st,
+                             epi_tiles + q * EPI_TILE_FLOATS);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acce[ab]);
@@ -558,19 +654,18 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
 
   const CUtensorMapSwizzle kswz = BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const CUtensorMapSwizzle mswz = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-  CUtensorMap ta, tb;
-  bool ok;
-  if (!A.mn_major)
-    ok = make_map(&ta, A.p, (uint64_t)K, (uint64_t)M, A.ld, BK, BM, kswz);
-  else
-    ok = make_map(&ta, A.p, (uint64_t)M, (uint64_t)K, A.ld, 32, BK, mswz);
-  if (!ok) return cudaErrorInvalidValue;
+  auto map_a = [&](CUtensorMap* m, const float* base) {
+    return !A.mn_major ? make_map(m, base, (uint64_t)K, (uint64_t)M, A.ld, BK, BM, kswz)
+                       : make_map(m, base, (uint64_t)M, (uint64_t)K, A.ld, 32, BK, mswz);
+  };
   const uint64_t b_rows = paired ? (uint64_t)b_pair_off + N : (uint64_t)N;
-  if (!B.mn_major)
-    ok = make_map(&tb, B.p, (uint64_t)K, b_rows, B.ld, BK, paired ? BN / 2 : BN, kswz);
-  else
-    ok = make_map(&tb, B.p, b_rows, (uint64_t)K, B.ld, 32, BK, mswz);
-  if (!ok) return cudaErrorInvalidValue;
+  auto map_b = [&](CUtensorMap* m, const float* base) {
+    return !B.mn_major
+               ? make_map(m, base, (uint64_t)K, b_rows, B.ld, BK, paired ? BN / 2 : BN, kswz)
+               : make_map(m, base, b_rows, (uint64_t)K, B.ld, 32, BK, mswz);
+  };
+  CUtensorMap ta, tb;
+  if (!map_a(&ta, A.p) || !map_b(&tb, B.p)) return cudaErrorInvalidValue;
 
   if (BK == 32) {
     if (BN == 128) return launch<128, 32>(stream, ta, tb, kp);
