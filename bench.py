@@ -30,6 +30,7 @@ import subprocess
 import sys
 import tempfile
 import time
+import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -57,6 +58,7 @@ def parse():
     ap.add_argument("--n", type=int, default=512)
     ap.add_argument("--k", type=int, default=512)
     ap.add_argument("--amn", type=int, default=0)
+    ap.add_argument("--cg", type=int, default=0, help="--op: GEMM CTA group (0 auto, 1, 2)")
     ap.add_argument("--bmn", type=int, default=0)
     return ap.parse_args()
 
@@ -78,7 +80,7 @@ def measured_peaks():
 
 class ClockSampler:
     """nvidia-smi clock / throttle-reason sampling during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -86,6 +88,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
@@ -93,10 +96,22 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        # the first sample arrives only after nvidia-smi has initialised
+        t_end = time.time() + 5.0
+        while time.time() < t_end and os.path.getsize(self.path) == 0:
+            time.sleep(0.02)
+
+    def mark(self, begin: bool):
+        """Wall-clock bounds of the timed region; samples outside are dropped."""
+        if begin:
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
 
     def stop(self):
         if self.proc is None:
@@ -110,9 +125,20 @@ class ClockSampler:
         with open(self.path) as f:
             for line in f:
                 parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
+                if len(parts) >= 10:
+                    rows.append(parts[1:])
+                    try:
+                        ts = parts[0].replace("/", "-")
+                        rows[-1].insert(0, time.mktime(time.strptime(ts[:19], "%Y-%m-%d %H:%M:%S"))
+                                        + float("0" + ts[19:]))
+                    except ValueError:
+                        rows[-1].insert(0, None)
         os.unlink(self.path)
+        if self.t0 is not None and self.t1 is not None:
+            inside = [r for r in rows if r[0] is not None and self.t0 - 0.05 <= r[0] <= self.t1 + 0.05]
+            if inside:
+                rows = inside
+        rows = [r[1:] for r in rows]
         if not rows:
             return None
         def num(x):
@@ -212,11 +238,13 @@ def run_ours(args, rank, world, local):
     clocks.start()
     n0 = rnet.kernel_launches()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark(True)
     ev0.record(stream)
     for i in range(args.steps):
         model.train_step(d_in[i % POOL], d_tg[i % POOL], B, T, LR, CLIP, d_loss)
     ev1.record(stream)
     ev1.synchronize()
+    clocks.mark(False)
     launches = rnet.kernel_launches() - n0
     barrier()
     ck = clocks.stop()
@@ -336,12 +364,14 @@ def run_reference(args, rank, world, local):
         clocks = ClockSampler(local)
         clocks.start()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.mark(True)
         e0.record()
         for i in range(args.steps):
             R.ref_train_step_device(h, d_in[i % POOL].data_ptr(), d_tg[i % POOL].data_ptr(), B, T,
                                     ctypes.c_float(LR), ctypes.c_float(CLIP))
         e1.record()
         torch.cuda.synchronize()
+        clocks.mark(False)
         ck = clocks.stop()
         ms = e0.elapsed_time(e1)
         R.ref_model_destroy(h)
@@ -378,6 +408,7 @@ def run_op(args):
     B, T, D = args.batch, args.seq, CFG["d_model"]
     N = B * T
     g = torch.Generator(device="cuda").manual_seed(0)
+    rnet.call("rnet_gemm_set_cta_group", args.cg)
 
     def rnd(*shape, scale=1.0):
         return torch.randn(*shape, device="cuda", generator=g) * scale
@@ -393,7 +424,7 @@ def run_op(args):
         lda, ldb = (M if args.amn else K), (Nn if args.bmn else K)
         fn = lambda: rnet.call("rnet_gemm_f32", M, Nn, K, p(A), lda, args.amn, p(Bm), ldb,
                                args.bmn, p(C), Nn, p(C), Nn, 0, F32(1.0), None)
-        work = f"gemm M={M} N={Nn} K={K} a_mn={args.amn} b_mn={args.bmn}"
+        work = f"gemm M={M} N={Nn} K={K} a_mn={args.amn} b_mn={args.bmn} cg={args.cg}"
     elif args.op in ("scan_fwd", "scan_bwd"):
         x = rnd(N, D)
         Wz, Wh = rnd(D, D, scale=D ** -0.5), rnd(D, D, scale=D ** -0.5)
@@ -444,7 +475,7 @@ def run_op(args):
             gg, gup, gd = z(Fd, D), z(Fd, D), z(D, Fd)
             fn = lambda: rnet.call("rnet_swiglu_backward", p(dy), p(x), p(gate), p(up), p(down),
                                    p(gc), p(uc), p(dx), p(gg), p(gup), p(gd), N, D, Fd, None)
-        work = f"swiglu {args.op[7:]} N={N} D={D} F={Fd}"
+        work = f"swiglu {args.op[7:]} N={N} D={D} F={Fd} cg={args.cg}"
     elif args.op in ("rms_fwd", "rms_bwd"):
         x, w, y, ri = rnd(N, D), rnd(D), z(N, D), z(N)
         fwd = lambda: rnet.call("rnet_rms_norm_forward", p(x), p(w), p(y), p(ri), N, D,

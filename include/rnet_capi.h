@@ -53,6 +53,13 @@ int rnet_gemm_f32(int M, int N, int K, const float* A, int lda, int a_mn_major, 
                   int ldb, int b_mn_major, float* C, int ldc, const float* R, int ldr, int op,
                   float alpha, void* stream);
 
+/* Tile shape selection of the GEMM engine for every later call in this
+ * process: 0 = automatic (CTA pairs, one 256-row MMA over two SMs, whenever
+ * M > 128; single-CTA 128-row tiles otherwise), 1 = always single-CTA,
+ * 2 = always CTA pairs. Results are identical up to fp32 summation order.
+ * No counterpart in the reference (its GEMMs are cuBLAS calls). */
+int rnet_gemm_set_cta_group(int cta_group);
+
 /* ------------------------------------------------------------------ layer ops
  * One entry per function of the reference's include/layers.h:28-153, same
  * argument meaning, same accumulate/overwrite contract:

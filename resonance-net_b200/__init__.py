@@ -46,6 +46,7 @@ _SIGS = {
     "rnet_abi_version": [],
     "rnet_device_error": [ctypes.POINTER(ctypes.c_uint), _I],
     "rnet_gemm_f32": [_I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _I, _P, _I, _I, _F, _P],
+    "rnet_gemm_set_cta_group": [_I],
     "rnet_rms_norm_forward": [_P, _P, _P, _P, _I, _I, _F, _P],
     "rnet_rms_norm_backward": [_P, _P, _P, _P, _P, _P, _I, _I, _P],
     "rnet_embed_forward": [_P, _P, _P, _I, _I, _I, _P],

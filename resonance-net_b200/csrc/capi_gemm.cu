@@ -1,5 +1,7 @@
 // C-ABI entry of the GEMM engine (used by parity tests and by callers that
 // want the engine directly).
+#include <string>
+
 #include "gemm.cuh"
 #include "status.h"
 
@@ -20,6 +22,16 @@ extern "C" int rnet_gemm_f32(int M, int N, int K, const float* A, int lda, int a
   e.ldr = ldr;
   cudaError_t err = gemm_tf32x3((cudaStream_t)stream, M, N, K, a, b, e, 0, 0,
                                 rnet_status::device_error_word());
-  if (err != cudaSuccess) return rnet_status::fail_cuda(err, "rnet_gemm_f32");
+  if (err != cudaSuccess) {
+    const std::string what = std::string("rnet_gemm_f32 (") + gemm_last_reason() + ")";
+    return rnet_status::fail_cuda(err, what.c_str());
+  }
+  return RNET_OK;
+}
+
+extern "C" int rnet_gemm_set_cta_group(int cta_group) {
+  if (cta_group < 0 || cta_group > 2)
+    return rnet_status::fail(RNET_ERR_ARG, "rnet_gemm_set_cta_group: expected 0, 1 or 2");
+  rnet_gemm::set_force_cta_group(cta_group);
   return RNET_OK;
 }

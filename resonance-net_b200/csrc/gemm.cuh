@@ -56,4 +56,10 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
 // Number of SMs of the current device (cached).
 int num_sms();
 
+// Reason of the last failed gemm_tf32x3 call on this thread ("" if none).
+const char* gemm_last_reason();
+
+// 0 = automatic CTA group choice, 1 / 2 = force single CTAs / CTA pairs.
+void set_force_cta_group(int cg);
+
 }  // namespace rnet_gemm

@@ -58,12 +58,15 @@ struct KParams {
   unsigned* err;
 };
 
-template <int BN, int BK>
+// BN = MMA N (accumulator columns per tile). CG = 2: one MMA covers the
+// 2*BM rows of a CTA pair; each CTA stages its BM rows of A and BN/2 rows of B.
+template <int BN, int BK, int CG>
 struct Cfg {
   static constexpr int ROW_BYTES = BK * 4;            // K-major row (64 or 128 B)
   static constexpr int MN_CHUNK = 128 * BK;           // MN-major box: 32 elems x BK rows
+  static constexpr int B_ROWS = BN / CG;              // B rows staged by this CTA
   static constexpr int A_BYTES = BM * BK * 4;
-  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int B_BYTES = B_ROWS * BK * 4;
   static constexpr int RAW_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGE_BYTES = 2 * RAW_BYTES;  // raw (= hi) + lo
   static constexpr int STAGES_FIT = SMEM_BUDGET / STAGE_BYTES;
@@ -75,7 +78,9 @@ struct Cfg {
   static constexpr uint32_t K_LAYOUT = BK == 32 ? 2u : 4u;  // SWIZZLE_128B / SWIZZLE_64B
   static constexpr uint32_t K_SBO = 8 * ROW_BYTES;          // 8-row core-matrix group
   static_assert(BK == 16 || BK == 32, "BK");
+  static_assert(CG == 1 || CG == 2, "CG");
   static_assert(STAGES >= 2, "stages");
+  static_assert(B_ROWS % 32 == 0, "B rows");
 };
 
 __device__ __forceinline__ void unit_range(const KParams& p, int unit, int& mt, int& nt0,
@@ -314,11 +319,11 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
 }
 
 // ------------------------------------------------------------------ TMA tiles
-// A tile [BM x BK] of k-block k0 / m-tile m0 into sa.
-template <int BN, int BK>
+// A tile [BM x BK] of k-block k0 starting at row m0 into sa.
+template <int BN, int BK, int CG>
 __device__ __forceinline__ void load_a(uint8_t* sa, const void* map, uint64_t* bar,
                                        const KParams& p, int k0, int m0) {
-  using C = Cfg<BN, BK>;
+  using C = Cfg<BN, BK, CG>;
   if (!p.a_mn) {
     tma_load_2d(sa, map, bar, k0, m0);
   } else {
@@ -327,18 +332,23 @@ __device__ __forceinline__ void load_a(uint8_t* sa, const void* map, uint64_t* b
   }
 }
 
-// B tile [BN x BK] of n-tile nt (two halves for paired operands) into sb.
-template <int BN, int BK>
+// This CTA's B rows of n-tile nt into sb. CG = 1: the whole [BN x BK] tile,
+// two BN/2 halves (rows n0 and n0 + pair offset) for paired operands.
+// CG = 2: CTA `rank` stages MMA columns [rank*BN/2, (rank+1)*BN/2), which
+// for paired operands is the first (rank 0) or the paired (rank 1) half.
+template <int BN, int BK, int CG>
 __device__ __forceinline__ void load_b(uint8_t* sb, const void* map, uint64_t* bar,
-                                       const KParams& p, int k0, int nt) {
-  using C = Cfg<BN, BK>;
-  if (p.b_pair_off == 0) {
-    const int n0 = nt * BN;
+                                       const KParams& p, int k0, int nt, int rank) {
+  using C = Cfg<BN, BK, CG>;
+  if (CG == 2 || p.b_pair_off == 0) {
+    const int n0 = p.b_pair_off == 0 ? nt * BN + rank * C::B_ROWS
+                                     : nt * (BN / 2) + rank * p.b_pair_off;
     if (!p.b_mn) {
       tma_load_2d(sb, map, bar, k0, n0);
     } else {
 #pragma unroll
-      for (int j = 0; j < BN / 32; ++j) tma_load_2d(sb + j * C::MN_CHUNK, map, bar, n0 + 32 * j, k0);
+      for (int j = 0; j < C::B_ROWS / 32; ++j)
+        tma_load_2d(sb + j * C::MN_CHUNK, map, bar, n0 + 32 * j, k0);
     }
   } else {
     const int n0 = nt * (BN / 2);
@@ -356,11 +366,24 @@ __device__ __forceinline__ void load_b(uint8_t* sb, const void* map, uint64_t* b
 }
 
 // ------------------------------------------------------------------ kernel
-template <int BN, int BK>
+// Persistent, warp-specialised. Units (tile, k-split) are strided over the
+// CTAs (CG = 1) or over the CTA pairs of a 2-CTA cluster (CG = 2).
+//
+// CG = 2 hand-offs (even CTA = leader, the only one issuing MMAs):
+//   producer (each CTA)  -> full[s]   own CTA   (TMA transaction bytes)
+//   split warps (each)   -> split[s]  leader    (remote arrive, 2 x 8 warps)
+//   leader MMA commit    -> empty[s]  both CTAs (tcgen05.commit multicast)
+//   leader MMA commit    -> accf[b]   both CTAs (tcgen05.commit multicast)
+//   epilogue warps (each)-> acce[b]   leader    (remote arrive, 2 x 4 warps)
+// A cluster barrier after set-up (barrier init, TMEM alloc) and before
+// teardown (TMEM dealloc, exit) keeps either CTA from touching the other's
+// barriers or TMEM outside their lifetime.
+template <int BN, int BK, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, const KParams p) {
-  using C = Cfg<BN, BK>;
+  using C = Cfg<BN, BK, CG>;
+  constexpr bool PAIR = CG == 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -371,35 +394,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* empty = bars + 2 * C::STAGES;
   uint64_t* accf = bars + 3 * C::STAGES;
   uint64_t* acce = accf + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+  uint64_t* drain = acce + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int rank = PAIR ? (int)cluster_ctarank() : 0;
+  const int group = PAIR ? blockIdx.x >> 1 : blockIdx.x;
+  const int n_groups = PAIR ? gridDim.x >> 1 : gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&split[s], NUM_SPLIT_WARPS);
+      mbar_init(&split[s], NUM_SPLIT_WARPS * CG);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], NUM_EPI_WARPS);
+      mbar_init(&acce[b], NUM_EPI_WARPS * CG);
     }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == MMA_WARP) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc<CG>(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish<CG>();
   }
   if (warp == PRODUCER_WARP && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -407,9 +435,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+      for (int unit = group; unit < p.num_units && ok; unit += n_groups) {
         int mt, nt0, nt1, kb0, kb1;
         unit_range(p, unit, mt, nt0, nt1, kb0, kb1);
+        const int m0 = mt * BM * CG + rank * BM;
         for (int nt = nt0; nt < nt1 && ok; ++nt) {
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s = it % C::STAGES;
@@ -419,16 +448,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint8_t* sb = sa + C::A_BYTES;
             mbar_arrive_expect_tx(&full[s], C::RAW_BYTES);
             const int k0 = kb * BK;
-            const int m0 = mt * BM;
-            load_a<BN, BK>(sa, &tmA, &full[s], p, k0, m0);
-            load_b<BN, BK>(sb, &tmB, &full[s], p, k0, nt);
+            load_a<BN, BK, CG>(sa, &tmA, &full[s], p, k0, m0);
+            load_b<BN, BK, CG>(sb, &tmB, &full[s], p, k0, nt, rank);
           }
         }
       }
     }
   } else if (warp == MMA_WARP) {
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc(BM, BN, 2, p.a_mn, p.b_mn);
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = make_idesc(BM * CG, BN, 2, p.a_mn, p.b_mn);
       // Byte advance of one 8-deep K slice and LBO / SBO / layout per operand.
       const uint32_t a_kstep = p.a_mn ? 1024u : 32u;
       const uint32_t b_kstep = p.b_mn ? 1024u : 32u;
@@ -440,7 +468,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t b_lay = p.b_mn ? 1u : C::K_LAYOUT;
       uint32_t it = 0, tc = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+      for (int unit = group; unit < p.num_units && ok; unit += n_groups) {
         int mt, nt0, nt1, kb0, kb1;
         unit_range(p, unit, mt, nt0, nt1, kb0, kb1);
         for (int nt = nt0; nt < nt1 && ok; ++nt, ++tc) {
@@ -465,17 +493,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               const uint64_t dal = make_sdesc(a_lo + kk * a_kstep, a_lbo, a_sbo, a_lay);
               const uint64_t dbh = make_sdesc(b_hi + kk * b_kstep, b_lbo, b_sbo, b_lay);
               const uint64_t dbl = make_sdesc(b_lo + kk * b_kstep, b_lbo, b_sbo, b_lay);
-              umma_tf32(tacc, dah, dbl, idesc, accumulate);
-              umma_tf32(tacc, dal, dbh, idesc, 1);
-              umma_tf32(tacc, dah, dbh, idesc, 1);
+              umma_tf32<CG>(tacc, dah, dbl, idesc, accumulate);
+              umma_tf32<CG>(tacc, dal, dbh, idesc, 1);
+              umma_tf32<CG>(tacc, dah, dbh, idesc, 1);
               accumulate = 1;
             }
-            umma_commit(&empty[s]);
+            if constexpr (PAIR) umma_commit_pair(&empty[s]); else umma_commit<CG>(&empty[s]);
           }
           if (!ok) break;
-          umma_commit(&accf[ab]);
+          if constexpr (PAIR) umma_commit_pair(&accf[ab]); else umma_commit<CG>(&accf[ab]);
         }
       }
+      // Every issued MMA has finished before teardown releases TMEM (also on
+      // the abort path, where no epilogue waited for the last ones).
+      umma_commit<CG>(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, p.err, &no_abort);
     }
   } else if (warp >= FIRST_SPLIT_WARP) {
     const int t = threadIdx.x - FIRST_SPLIT_WARP * 32;
@@ -483,7 +516,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     constexpr int N4 = C::RAW_BYTES / 16;
     uint32_t it = 0;
     bool ok = true;
-    for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+    for (int unit = group; unit < p.num_units && ok; unit += n_groups) {
       int mt, nt0, nt1, kb0, kb1;
       unit_range(p, unit, mt, nt0, nt1, kb0, kb1);
       for (int nt = nt0; nt < nt1 && ok; ++nt) {
@@ -507,7 +540,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&split[s]);
+          if (lane == 0) {
+            if constexpr (PAIR) mbar_arrive_cluster(&split[s], 0); else mbar_arrive(&split[s]);
+          }
         }
       }
     }
@@ -515,10 +550,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int q = warp;  // TMEM lane quadrant
     uint32_t tc = 0;
     bool ok = true;
-    for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+    for (int unit = group; unit < p.num_units && ok; unit += n_groups) {
       int mt, nt0, nt1, kb0, kb1;
       unit_range(p, unit, mt, nt0, nt1, kb0, kb1);
-      const int row = mt * BM + q * 32 + lane;
+      const int row0 = mt * BM * CG + rank * BM + q * 32;
       Top2State st{-1e30f, -1e30f, 0, 0};
       for (int nt = nt0; nt < nt1; ++nt, ++tc) {
         const int ab = tc & 1;
@@ -526,19 +561,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!mbar_wait(&accf[ab], tph, p.err, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN;
-        epilogue_subtile<BN>(p, tacc, mt * BM + q * 32, nt, nt == nt1 - 1, st,
+        epilogue_subtile<BN>(p, tacc, row0, nt, nt == nt1 - 1, st,
                              epi_tiles + q * EPI_TILE_FLOATS);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acce[ab]);
+        if (lane == 0) {
+          if constexpr (PAIR) mbar_arrive_cluster(&acce[ab], 0); else mbar_arrive(&acce[ab]);
+        }
       }
     }
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync(); else __syncthreads();
   tc_fence_after();
-  if (warp == MMA_WARP) tmem_dealloc(tmem_base, C::TMEM_COLS);
+  if (warp == MMA_WARP) tmem_dealloc<CG>(tmem_base, C::TMEM_COLS);
 }
 
 // ------------------------------------------------------------------ host
@@ -572,6 +609,18 @@ static bool make_map(CUtensorMap* m, const float* base, uint64_t inner, uint64_t
   return r == CUDA_SUCCESS;
 }
 
+// Which argument check or launch step failed last (thread-local).
+static thread_local const char* g_reason = "";
+const char* gemm_last_reason() { return g_reason; }
+static cudaError_t reject(const char* why) {
+  g_reason = why;
+  return cudaErrorInvalidValue;
+}
+
+// Test hook: force the CTA group (0 = automatic).
+static int g_force_cg = 0;
+void set_force_cta_group(int cg) { g_force_cg = (cg == 1 || cg == 2) ? cg : 0; }
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -583,20 +632,56 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int BK>
+template <int BN, int BK, int CG>
 static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
                           const KParams& kp) {
-  using C = Cfg<BN, BK>;
+  using C = Cfg<BN, BK, CG>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK, CG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) {
+      g_reason = "shared-memory attribute";
+      return e;
+    }
     configured = true;
   }
-  const int grid = kp.num_units < num_sms() ? kp.num_units : num_sms();
-  gemm_tf32x3_kernel<BN, BK><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ta, tb, kp);
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = CG > 1 ? 1 : 0;
+  // Persistent grid: one CTA (pair) per SM (pair) that can be co-resident.
+  static int max_groups = 0;
+  if (max_groups == 0) {
+    max_groups = num_sms() / CG;
+    if (CG > 1) {
+      int n = 0;
+      cfg.gridDim = dim3(max_groups * CG);
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_tf32x3_kernel<BN, BK, CG>, &cfg) ==
+              cudaSuccess &&
+          n > 0 && n < max_groups)
+        max_groups = n;
+      cudaGetLastError();
+    }
+    if (getenv("RNET_GEMM_VERBOSE"))
+      fprintf(stderr, "gemm_tf32x3<BN=%d, CG=%d>: %d co-resident CTA groups, %d stages, %d B smem\n",
+              BN, CG, max_groups, C::STAGES, C::SMEM_BYTES);
+  }
+  const int groups = kp.num_units < max_groups ? kp.num_units : max_groups;
+  cfg.gridDim = dim3(groups * CG);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, BK, CG>, ta, tb, kp);
+  if (e != cudaSuccess) {
+    g_reason = "kernel launch";
+    return e;
+  }
   return rnet_k::launched();
 }
 
@@ -604,17 +689,23 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
                         const Operand& B, const Epilogue& epi, int b_pair_off, int k_splits,
                         unsigned* err_word) {
   if (M <= 0 || N <= 0) return cudaSuccess;
-  if (K <= 0 || A.p == nullptr || B.p == nullptr) return cudaErrorInvalidValue;
+  g_reason = "";
+  if (K <= 0 || A.p == nullptr || B.p == nullptr) return reject("K <= 0 or null operand");
   if ((A.ld % 4) || (B.ld % 4) || (reinterpret_cast<uintptr_t>(A.p) & 15) ||
       (reinterpret_cast<uintptr_t>(B.p) & 15))
-    return cudaErrorInvalidValue;
-  // Paired-B and row-owner epilogues use 128-wide tiles (64-feature halves).
+    return reject("operand ld not a multiple of 4 or operand not 16-byte aligned");
   const bool paired = b_pair_off > 0;
   const bool row_owner = epi.kind == EPI_TOP2;
-  const int BN = (paired || row_owner || N <= 128) ? 128 : 256;
-  // 16-deep K-blocks (4 stages at BN=256) measured 5-20% faster than 32-deep
-  // (2 stages) on every step shape; the 32-deep instantiation is kept for
-  // shapes that may prefer it.
+  // CTA pairs (one 256-row MMA over two SMs, each staging half of B) cut
+  // shared-memory and L2->SM traffic per FLOP by a third; single CTAs are kept
+  // for short M, where pairs would leave SMs idle.
+  const int CG = g_force_cg > 0 ? g_force_cg : (M > BM ? 2 : 1);
+  // CG = 1: paired-B and row-owner epilogues use 128-wide tiles (64-feature
+  // halves). CG = 2: 256-wide tiles (each CTA stages one 128-row half).
+  const int BN = CG == 2 ? (N <= 128 && !paired ? 128 : 256)
+                         : ((paired || row_owner || N <= 128) ? 128 : 256);
+  // 16-deep K-blocks (4-6 stages) measured 5-20% faster than 32-deep (2-3
+  // stages) on every step shape.
   constexpr int BK = 16;
   const int n_logical_tile = paired ? BN / 2 : BN;
 
@@ -622,7 +713,7 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   kp.M = M;
   kp.N = N;
   kp.K = K;
-  kp.m_tiles = (M + BM - 1) / BM;
+  kp.m_tiles = (M + BM * CG - 1) / (BM * CG);
   kp.n_tiles = (N + n_logical_tile - 1) / n_logical_tile;
   kp.kb_total = (K + BK - 1) / BK;
   kp.row_owner = row_owner ? 1 : 0;
@@ -638,7 +729,8 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
       splits = k_splits;
     } else {
       const int tiles = kp.m_tiles * kp.n_tiles;
-      if (tiles < num_sms()) splits = num_sms() / tiles;
+      const int groups = num_sms() / CG;
+      if (tiles < groups) splits = groups / tiles;
       // keep each split's K at most 2048 so the TMEM accumulation stays
       // fp32-accurate, and at least 4 k-blocks so a split is worth a tile
       const int min_splits = (K + 2047) / 2048;
@@ -659,20 +751,23 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
                        : make_map(m, base, (uint64_t)M, (uint64_t)K, A.ld, 32, BK, mswz);
   };
   const uint64_t b_rows = paired ? (uint64_t)b_pair_off + N : (uint64_t)N;
+  // K-major box rows = the rows one TMA copy stages (a half tile when paired
+  // or when a CTA pair splits B).
+  const uint32_t b_box = (paired || CG == 2) ? BN / 2 : BN;
   auto map_b = [&](CUtensorMap* m, const float* base) {
-    return !B.mn_major
-               ? make_map(m, base, (uint64_t)K, b_rows, B.ld, BK, paired ? BN / 2 : BN, kswz)
-               : make_map(m, base, b_rows, (uint64_t)K, B.ld, 32, BK, mswz);
+    return !B.mn_major ? make_map(m, base, (uint64_t)K, b_rows, B.ld, BK, b_box, kswz)
+                       : make_map(m, base, b_rows, (uint64_t)K, B.ld, 32, BK, mswz);
   };
   CUtensorMap ta, tb;
-  if (!map_a(&ta, A.p) || !map_b(&tb, B.p)) return cudaErrorInvalidValue;
+  if (!map_a(&ta, A.p)) return reject("tensor map of A rejected");
+  if (!map_b(&tb, B.p)) return reject("tensor map of B rejected");
 
-  if (BK == 32) {
-    if (BN == 128) return launch<128, 32>(stream, ta, tb, kp);
-    return launch<256, 32>(stream, ta, tb, kp);
+  if (CG == 2) {
+    if (BN == 128) return launch<128, BK, 2>(stream, ta, tb, kp);
+    return launch<256, BK, 2>(stream, ta, tb, kp);
   }
-  if (BN == 128) return launch<128, 16>(stream, ta, tb, kp);
-  return launch<256, 16>(stream, ta, tb, kp);
+  if (BN == 128) return launch<128, BK, 1>(stream, ta, tb, kp);
+  return launch<256, BK, 1>(stream, ta, tb, kp);
 }
 
 }  // namespace rnet_gemm

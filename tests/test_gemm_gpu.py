@@ -3,6 +3,9 @@ through the C ABI (rnet_gemm_f32): all four operand majors, ragged shapes
 (M, N, K not multiples of the tile), store / accumulate (split-K) / residual
 epilogues, and long K (weight-gradient shape).
 
+Every case runs on both tile shapes of the engine: single-CTA 128-row tiles
+(cta_group 1) and CTA-pair 256-row tiles over two SMs (cta_group 2).
+
 Tolerance: max |err| / max |ref| <= 2e-5 (fp32-class; plain TF32 would give
 ~1e-3), tighter than the 1e-4 the layer parity tests use.
 """
@@ -13,6 +16,13 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 TOL = 2e-5
+
+
+@pytest.fixture(params=[1, 2], ids=["cg1", "cg2"])
+def cta_group(request, rnet):
+    rnet.call("rnet_gemm_set_cta_group", request.param)
+    yield request.param
+    rnet.call("rnet_gemm_set_cta_group", 0)
 
 
 def _run(rnet, torch, M, N, K, amn, bmn, op):
@@ -35,16 +45,16 @@ def _run(rnet, torch, M, N, K, amn, bmn, op):
 @pytest.mark.parametrize("amn", [0, 1])
 @pytest.mark.parametrize("bmn", [0, 1])
 @pytest.mark.parametrize("M,N,K", [(128, 128, 32), (200, 300, 96), (64, 64, 64), (256, 512, 512),
-                                   (1000, 1024, 520)])
-def test_layouts_store(rnet, cuda, M, N, K, amn, bmn):
+                                   (1000, 1024, 520), (384, 640, 48), (132, 96, 40)])
+def test_layouts_store(rnet, cuda, cta_group, M, N, K, amn, bmn):
     assert _run(rnet, cuda, M, N, K, amn, bmn, 0) <= TOL
 
 
 @pytest.mark.parametrize("op", [1, 2])
-def test_accumulate_and_residual(rnet, cuda, op):
+def test_accumulate_and_residual(rnet, cuda, cta_group, op):
     assert _run(rnet, cuda, 512, 512, 1024, 0, 0, op) <= TOL
 
 
-def test_long_k_split(rnet, cuda):
+def test_long_k_split(rnet, cuda, cta_group):
     # weight-gradient shape: K = tokens, both operands MN-major, split-K red.add
     assert _run(rnet, cuda, 512, 1024, 16384, 1, 1, 1) <= TOL

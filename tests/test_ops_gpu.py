@@ -34,6 +34,14 @@ def _p(a):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
+@pytest.fixture(params=[0, 1], ids=["auto", "cg1"])
+def cta_group(request, rnet):
+    """GEMM tile shape: automatic (CTA pairs once M > 128) or single-CTA."""
+    rnet.call("rnet_gemm_set_cta_group", request.param)
+    yield request.param
+    rnet.call("rnet_gemm_set_cta_group", 0)
+
+
 @pytest.mark.parametrize("N,D", [(64, 64), (1000, 512), (7, 2048)])
 def test_rms_norm(rnet, orc, cuda, N, D):
     torch = cuda
@@ -131,7 +139,7 @@ def test_min_gru(rnet, orc, cuda, B, T, D):
 
 
 @pytest.mark.parametrize("B,T,D,S", [(2, 32, 64, 64), (3, 100, 64, 160), (4, 128, 512, 1024)])
-def test_slot_memory(rnet, orc, cuda, B, T, D, S):
+def test_slot_memory(rnet, orc, cuda, cta_group, B, T, D, S):
     torch = cuda
     r = _rng(B * T + S)
     N, k = B * T, 2
@@ -185,7 +193,7 @@ def test_slot_memory(rnet, orc, cuda, B, T, D, S):
 
 @pytest.mark.parametrize("N,D,F", [(64, 64, 128), (300, 64, 192), (2048, 512, 1024)])
 @pytest.mark.parametrize("contiguous", [True, False])
-def test_swiglu(rnet, orc, cuda, N, D, F, contiguous):
+def test_swiglu(rnet, orc, cuda, cta_group, N, D, F, contiguous):
     torch = cuda
     r = _rng(N + D + F + contiguous)
     x = r.normal(size=(N, D)).astype(np.float32)
