@@ -303,14 +303,9 @@ int rnet_swiglu_backward(const float* dy, const float* x, const float* gate_w,
   float* dGU = t.get<float>((size_t)N * 2 * F);
   CK(t.err);
   CK(rnet_k::silu_mul(gate_cache, up_cache, H, (size_t)N * F, s));
-  Epilogue e;
-  e.kind = EPI_SWIGLU_BWD;
-  e.C = dGU;
-  e.ldc = 2 * F;
-  e.Gc = gate_cache;
-  e.Uc = up_cache;
-  e.ldf = F;
-  CK(gemm_tf32x3(s, N, F, dim, kmaj(dy, dim), mnmaj(down_w, F), e, 0, 0, ew()));
+  CK(gemm_tf32x3(s, N, F, dim, kmaj(dy, dim), mnmaj(down_w, F), mk(EPI_STORE, dGU, 2 * F), 0, 0,
+                 ew()));
+  CK(rnet_k::swiglu_bwd_pointwise(dGU, 2 * F, gate_cache, up_cache, N, F, s));
   CK(gemm_tf32x3(s, dim, F, N, mnmaj(dy, dim), mnmaj(H, F), mk(EPI_ACCUM, d_down_w, F), 0, 0,
                  ew()));
   CK(gemm_tf32x3(s, N, dim, F, kmaj(dGU, 2 * F), mnmaj(gate_w, dim), mk(EPI_ACCUM, dx, dim), 0, 0,

@@ -145,6 +145,56 @@ __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __rest
   }
 }
 
+// SwiGLU backward pointwise step, in place over dgu = [dG | dU] ([N, 2F],
+// row stride ld): on entry dG holds dH = dY W_down; on exit
+//   dG = dH * u * silu'(g),  dU = dH * silu(g),
+// silu'(g) = s + g s (1 - s), s = sigmoid(g) (reference src/swiglu_ffn.cu:23-40).
+__device__ __forceinline__ void swiglu_grad1(float dh, float g, float u, float& dg, float& du) {
+  const float sig = 1.0f / (1.0f + __expf(-g));
+  const float dsilu = sig + g * sig * (1.0f - sig);
+  dg = dh * u * dsilu;
+  du = dh * (g * sig);
+}
+
+__global__ void swiglu_bwd_pointwise_v4(float* __restrict__ dgu, int ld,
+                                        const float* __restrict__ G, const float* __restrict__ U,
+                                        int N, int F) {
+  const int F4 = F >> 2;
+  const size_t n4 = (size_t)N * F4;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / F4;
+    const int c = (int)(i - r * F4) * 4;
+    float4* pg = reinterpret_cast<float4*>(dgu + r * ld + c);
+    float4* pu = reinterpret_cast<float4*>(dgu + r * ld + F + c);
+    const float4 dh = *pg;
+    const float4 g = *reinterpret_cast<const float4*>(G + r * F + c);
+    const float4 u = *reinterpret_cast<const float4*>(U + r * F + c);
+    float4 dg, du;
+    swiglu_grad1(dh.x, g.x, u.x, dg.x, du.x);
+    swiglu_grad1(dh.y, g.y, u.y, dg.y, du.y);
+    swiglu_grad1(dh.z, g.z, u.z, dg.z, du.z);
+    swiglu_grad1(dh.w, g.w, u.w, dg.w, du.w);
+    *pg = dg;
+    *pu = du;
+  }
+}
+
+__global__ void swiglu_bwd_pointwise_1(float* __restrict__ dgu, int ld,
+                                       const float* __restrict__ G, const float* __restrict__ U,
+                                       int N, int F) {
+  const size_t n = (size_t)N * F;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / F;
+    const int c = (int)(i - r * F);
+    float dg, du;
+    swiglu_grad1(dgu[r * ld + c], G[i], U[i], dg, du);
+    dgu[r * ld + c] = dg;
+    dgu[r * ld + F + c] = du;
+  }
+}
+
 int ew_grid(size_t n) {
   size_t g = (n + 255) / 256;
   if (g > 148 * 16) g = 148 * 16;
@@ -212,6 +262,19 @@ cudaError_t add3(const float* a, const float* b, const float* c, float* out, siz
                  cudaStream_t s) {
   if (!n) return cudaSuccess;
   add3_kernel<<<ew_grid(n), 256, 0, s>>>(a, b, c, out, n);
+  return launched();
+}
+
+cudaError_t swiglu_bwd_pointwise(float* dgu, int ld, const float* G, const float* U, int N, int F,
+                                 cudaStream_t s) {
+  if (N <= 0 || F <= 0) return cudaSuccess;
+  const bool v4 = (F % 4 == 0) && (ld % 4 == 0) &&
+                  ((reinterpret_cast<uintptr_t>(dgu) | reinterpret_cast<uintptr_t>(G) |
+                    reinterpret_cast<uintptr_t>(U)) & 15) == 0;
+  if (v4)
+    swiglu_bwd_pointwise_v4<<<ew_grid((size_t)N * F / 4), 256, 0, s>>>(dgu, ld, G, U, N, F);
+  else
+    swiglu_bwd_pointwise_1<<<ew_grid((size_t)N * F), 256, 0, s>>>(dgu, ld, G, U, N, F);
   return launched();
 }
 

@@ -429,16 +429,12 @@ int Engine::layer_backward(int l, int B, int T) {
   float* dVT = dVT_ + (size_t)l * S * D;
   const double ND4 = 4.0 * N * D;
   // 4. SwiGLU (src/resonance_net.cpp:468-490, src/swiglu_ffn.cu:88-152)
-  {
-    Epilogue e;
-    e.kind = EPI_SWIGLU_BWD;
-    e.C = dGU_;
-    e.ldc = 2 * F;
-    e.Gc = a.G;
-    e.Uc = a.U;
-    e.ldf = F;
-    MM(N, F, D, kmaj(dX_, D), mnmaj(w.down, F), e, 0);
-  }
+  // dH = dY W_down into the dG half of dGU, then the pointwise SwiGLU
+  // gradient in place (a fused epilogue measured 4x slower: its cache reads
+  // have too little memory-level parallelism in four epilogue warps)
+  MM(N, F, D, kmaj(dX_, D), mnmaj(w.down, F), epi_store(dGU_, 2 * F), 0);
+  PROF(PK_OTHER, 0, 5.0 * 4 * N * F,
+       rnet_k::swiglu_bwd_pointwise(dGU_, 2 * F, a.G, a.U, N, F, s));
   MM(D, F, N, mnmaj(dX_, D), mnmaj(a.H, F), epi_accum(g.down, F), 0);
   MM(N, D, 2 * F, kmaj(dGU_, 2 * F), mnmaj(w.gate, D), epi_store(dsub_, D), 0);
   MM(2 * F, D, N, mnmaj(dGU_, 2 * F), mnmaj(a.n4, D), epi_accum(g.gate, D), 0);

@@ -22,7 +22,6 @@ enum EpiKind : int {
   EPI_ACCUM = 1,       // C += alpha*acc        (vector red.add; split-K safe)
   EPI_RESID = 2,       // C = R + alpha*acc
   EPI_SWIGLU_FWD = 3,  // paired B: G = acc[gate], U = acc[up], H = silu(G)*U
-  EPI_SWIGLU_BWD = 4,  // acc = dH; DGU[:, f] = dG, DGU[:, F+f] = dU
   EPI_TOP2 = 5,        // row-owner: running top-2 over N, softmax, idx/w (+optional C)
 };
 
@@ -33,12 +32,10 @@ struct Epilogue {
   int ldc = 0;
   const float* R = nullptr;  // residual (EPI_RESID)
   int ldr = 0;
-  // SwiGLU: gate/up caches and hidden output, all [M, ldf]
+  // SwiGLU forward: gate / up pre-activations and hidden output, all [M, ldf]
   float* G = nullptr;
   float* U = nullptr;
   float* H = nullptr;
-  const float* Gc = nullptr;
-  const float* Uc = nullptr;
   int ldf = 0;
   // top-2
   int* topk_idx = nullptr;

@@ -107,8 +107,8 @@ __device__ __forceinline__ float silu_fast(float g) { return g / (1.0f + __expf(
 
 // ------------------------------------------------------------------ epilogue
 // The accumulator arrives thread-per-row (TMEM lane = tile row, 32 columns
-// per tcgen05.ld). The SwiGLU epilogues, which move three [N, F] planes per
-// tile, go through a per-warp 32x33 shared-memory tile so that a warp
+// per tcgen05.ld). The SwiGLU forward epilogue, which writes three [N, F]
+// planes per tile, goes through a per-warp 32x33 shared-memory tile so that a warp
 // instruction touches four full 128-byte row segments (coalesced float4)
 // instead of 32 rows; the other kinds store thread-per-row directly.
 // Thread `lane` holds row (row0 + lane) x columns [col0, col0 + 32) in v.
@@ -149,36 +149,6 @@ __device__ __forceinline__ void tile_out(float* st, const float (&v)[32], float*
       }
     }
   }
-  __syncwarp();
-}
-
-// Inverse of tile_out for loads: thread `lane` receives row (row0 + lane) x
-// columns [col0, col0 + 32) of src (row stride ld); out-of-range reads as 0.
-__device__ __forceinline__ void tile_in(float* st, float (&v)[32], const float* src, int ld,
-                                        int row0, int col0, int M, int N) {
-  const int lane = threadIdx.x & 31;
-  const int cc = (lane & 7) * 4;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int rr = j * 4 + (lane >> 3);
-    const int row = row0 + rr, col = col0 + cc;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (row < M) {
-      const float* g = src + (size_t)row * ld + col;
-      if (col + 4 <= N) {
-        x = *reinterpret_cast<const float4*>(g);
-      } else {
-        if (col < N) x.x = g[0];
-        if (col + 1 < N) x.y = g[1];
-        if (col + 2 < N) x.z = g[2];
-      }
-    }
-    float* s = st + rr * TILE_LD + cc;
-    s[0] = x.x; s[1] = x.y; s[2] = x.z; s[3] = x.w;
-  }
-  __syncwarp();
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = st[lane * TILE_LD + i];
   __syncwarp();
 }
 
@@ -226,6 +196,21 @@ __device__ __forceinline__ void store_row_chunk(const KParams& p, int kind, int 
   }
 }
 
+// The residual rows the epilogue reads for the warp's 32 rows x BN columns of
+// tile nt, prefetched into L2 while the tile's MMAs still run, so the
+// epilogue's loads hit L2 instead of DRAM.
+template <int BN>
+__device__ __forceinline__ void prefetch_epilogue_inputs(const KParams& p, int row, int nt) {
+  const Epilogue& e = p.epi;
+  if (row >= p.M) return;
+  if (e.kind == EPI_RESID) {
+    const int c0 = nt * BN;
+#pragma unroll
+    for (int c = 0; c < BN; c += 32)
+      if (c0 + c < p.N) prefetch_l2(e.R + (size_t)row * e.ldr + c0 + c);
+  }
+}
+
 struct Top2State {
   float h0, h1;
   int i0, i1;
@@ -254,30 +239,6 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = silu_fast(g[i]) * v[i];
       tile_out(tile, v, e.H, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0);
-    }
-    return;
-  }
-  if (e.kind == EPI_SWIGLU_BWD) {
-#pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      tmem_ld_32cols(tacc + c * 32, v);
-      const int f0 = nt * BN + c * 32;
-      // Two 32-float arrays live at a time: dU is stored before U is read.
-      float g[32];
-      tile_in(tile, g, e.Gc, e.ldf, row0, f0, p.M, p.N);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float sig = 1.0f / (1.0f + __expf(-g[i]));
-        const float dsilu = sig + g[i] * sig * (1.0f - sig);
-        const float dh = v[i];
-        v[i] = dh * (g[i] * sig);  // dU
-        g[i] = dh * dsilu;         // dG / u
-      }
-      tile_out(tile, v, e.C + p.N, e.ldc, nullptr, 0, row0, f0, p.M, p.N, 0);
-      tile_in(tile, v, e.Uc, e.ldf, row0, f0, p.M, p.N);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= g[i];  // dG
-      tile_out(tile, v, e.C, e.ldc, nullptr, 0, row0, f0, p.M, p.N, 0);
     }
     return;
   }
@@ -558,6 +519,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int nt = nt0; nt < nt1; ++nt, ++tc) {
         const int ab = tc & 1;
         const uint32_t tph = (tc >> 1) & 1;
+        prefetch_epilogue_inputs<BN>(p, row0 + lane, nt);
         if (!mbar_wait(&accf[ab], tph, p.err, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN;

@@ -82,6 +82,10 @@ cudaError_t add3(const float* a, const float* b, const float* c, float* out, siz
                  cudaStream_t s);
 // h = g * sigmoid(g) * u   (reference silu_mul_kernel, src/swiglu_ffn.cu:11-21)
 cudaError_t silu_mul(const float* g, const float* u, float* h, size_t n, cudaStream_t s);
+// In place over dgu = [dG | dU] ([N, 2F], row stride ld) holding dH in its
+// dG half: dG = dH * u * silu'(g), dU = dH * silu(g) (G, U: [N, F] caches).
+cudaError_t swiglu_bwd_pointwise(float* dgu, int ld, const float* G, const float* U, int N, int F,
+                                 cudaStream_t s);
 
 // ---- recurrent decode (decode.cu) -----------------------------------------
 // ring: [M][14][D] last conv inputs indexed by position mod 14; *pos = index
