@@ -312,7 +312,8 @@ def run_ours(args, rank, world, local):
                      "peak_src": f"{peaks['src']} bf16 dense, sustained",
                      "ceiling_3xtf32": round(peaks["bf16_sust"] / 6, 1),
                      "frac_of_3xtf32_ceiling": round(gemm_tflops / (peaks["bf16_sust"] / 6), 4),
-                     "ms_per_launch": round(per_launch_ms, 4), "traffic": traffic},
+                     "ms_per_launch": round(per_launch_ms, 4), "traffic": traffic,
+                     "algorithmic_bytes_per_launch": round(g["bytes"] / max(1, g["launches"]))},
         "kernels": kernels, "loss": round(loss, 4),
         "clocks": ck,
     }
