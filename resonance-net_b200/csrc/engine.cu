@@ -324,7 +324,8 @@ int Engine::profile_read(ProfStats* out, bool reset) {
        gemm_tf32x3(stream_, (M), (N), (K), (A), (B), (E), (PAIR), 0, err))
 
 // ------------------------------------------------------------------ forward
-int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B, int T) {
+int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B, int T,
+                          bool train) {
   const int N = B * T, D = cfg_.d_model, F = cfg_.d_ff, S = cfg_.n_slots, k = cfg_.slot_top_k;
   const float eps = cfg_.rms_eps;
   const LayerParams& w = W_[l];
@@ -342,9 +343,10 @@ int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B,
   // 2. MinGRU (:301-313): P = n2 [Wz;Wh]^T, fused gate + scan + residual
   PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(a.r1, w.n2, a.n2, a.rinv2, N, D, eps, s));
   MM(N, 2 * D, D, kmaj(a.n2, D), kmaj(w.Wz, D), epi_store(a.P, 2 * D), 0);
+  // training keeps e = h~ - h_prev (all the backward needs), prefill keeps h
   PROF(PK_SCAN_FWD, 0, 6 * ND4,
        rnet_k::gru_scan_fwd(a.P, a.P + D, 2 * D, w.bz, w.bh, a.z, a.h, nullptr, a.r1, a.r2, B, T,
-                            D, s));
+                            D, s, train));
   // 3. slot memory (:315-330)
   PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(a.r2, w.n3, a.n3, a.rinv3, N, D, eps, s));
   MM(N, D, D, kmaj(a.n3, D), kmaj(w.pq, D), epi_store(a.q, D), 0);
@@ -391,7 +393,7 @@ int Engine::forward(const int* d_tokens, float* d_logits, int B, int T) {
   for (int l = 0; l < cfg_.n_layers; ++l) {
     const float* Xl = caches ? X_ + (size_t)l * ND : X_ + (size_t)(l & 1) * ND;
     float* Xn = caches ? X_ + (size_t)(l + 1) * ND : X_ + (size_t)((l + 1) & 1) * ND;
-    rc = layer_forward(l, Xl, Xn, caches ? act_[l] : act_[0], B, T);
+    rc = layer_forward(l, Xl, Xn, caches ? act_[l] : act_[0], B, T, caches);
     if (rc) return rc;
   }
   const float* XL = caches ? X_ + (size_t)cfg_.n_layers * ND : X_ + (size_t)(cfg_.n_layers & 1) * ND;
@@ -453,8 +455,8 @@ int Engine::layer_backward(int l, int B, int T) {
   MM(D, D, N, mnmaj(dq_, D), mnmaj(a.n3, D), epi_accum(g.pq, D), 0);
   PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, a.r2, w.n3, a.rinv3, dX_, g.n3, N, D, 1, s));
   // 2. MinGRU (:512-528, src/min_gru.cu:128-191)
-  PROF(PK_SCAN_BWD, 0, 6 * ND4,
-       rnet_k::gru_scan_bwd(dX_, a.z, a.h, a.P + D, 2 * D, w.bh, dPZH_, dPZH_ + D, 2 * D, g.bz,
+  PROF(PK_SCAN_BWD, 0, 5 * ND4,
+       rnet_k::gru_scan_bwd(dX_, a.z, a.h, nullptr, 0, nullptr, dPZH_, dPZH_ + D, 2 * D, g.bz,
                             g.bh, B, T, D, s));
   MM(N, D, 2 * D, kmaj(dPZH_, 2 * D), mnmaj(w.Wz, D), epi_store(dsub_, D), 0);
   MM(2 * D, D, N, mnmaj(dPZH_, 2 * D), mnmaj(a.n2, D), epi_accum(g.Wz, D), 0);
@@ -585,7 +587,7 @@ int Engine::prefill(Decoder* d, const int* d_tokens, int T) {
   for (int l = 0; l < cfg_.n_layers; ++l) {
     const float* Xl = X_ + (size_t)(l & 1) * ND;
     float* Xn = X_ + (size_t)((l + 1) & 1) * ND;
-    rc = layer_forward(l, Xl, Xn, act_[0], M, T);
+    rc = layer_forward(l, Xl, Xn, act_[0], M, T, false);
     if (rc) return rc;
     float* st = d->state + (size_t)l * d->floats_per_layer;
     CK(rnet_k::decode_extract_state(act_[0].n1, act_[0].h, st, st + (size_t)M * 14 * D, M, T, D,

@@ -148,7 +148,9 @@ class Engine {
   void prof_end(cudaEvent_t a, int kind, double flops, double bytes);
 
   int gemm_err(cudaError_t e, const char* what);
-  int layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B, int T);
+  // train: keep the activation caches the backward reads (scan keeps e = h~ -
+  // h_prev in LayerAct::h); otherwise LayerAct::h holds h (prefill)
+  int layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B, int T, bool train);
   int layer_backward(int l, int B, int T);
   int head_backward(const float* d_dlogits, int N);
 

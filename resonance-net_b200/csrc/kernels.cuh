@@ -36,12 +36,15 @@ cudaError_t conv_bwd(const float* dS, const float* x, const float* w3, const flo
 // ---- MinGRU scan (min_gru_scan.cu) ----------------------------------------
 // z = sigmoid(pz + bz), h~ = ph + bh, h_t = (1-z) h_{t-1} + z h~ (h_{-1} = 0).
 // pz/ph rows have stride ldp. Writes z, h; optional y = h (copy) and optional
-// residual out = res + h.
+// residual out = res + h. h_as_diff: the `h` output receives e_t = h~_t -
+// h_{t-1} instead (all the backward needs of h~ and h; exact in fp32).
 cudaError_t gru_scan_fwd(const float* pz, const float* ph, int ldp, const float* bz,
                          const float* bh, float* z, float* h, float* y, const float* res,
-                         float* out, int B, int T, int D, cudaStream_t s);
+                         float* out, int B, int T, int D, cudaStream_t s, bool h_as_diff = false);
 // Reverse scan: dh_t = dy_t + (1 - z_{t+1}) dh_{t+1};
 // dz = dh (h~ - h_{t-1}) z (1-z), dh~ = dh z. h~ = ph + bh (ph stride ldp).
+// ph == nullptr: `h` holds e = h~ - h_{t-1} from gru_scan_fwd(h_as_diff) and
+// bh is not read.
 // Writes dz/dh~ with row stride ldd (dh~ at column offset `dht_off`),
 // dbz += sum dz, dbh += sum dh~.
 cudaError_t gru_scan_bwd(const float* dy, const float* z, const float* h, const float* ph,

@@ -56,7 +56,8 @@ __global__ void __launch_bounds__(W * 32)
     scan_fwd_kernel(const float* __restrict__ pz, const float* __restrict__ ph, int ldp,
                     const float* __restrict__ bz, const float* __restrict__ bh,
                     float* __restrict__ zo, float* __restrict__ ho, float* __restrict__ yo,
-                    const float* __restrict__ res, float* __restrict__ out, int T, int D) {
+                    const float* __restrict__ res, float* __restrict__ out, int T, int D,
+                    int diff) {
   extern __shared__ float smem[];
   float* sZ = smem;             // pz, then z
   float* sT = smem + TILE;      // ph, then h~
@@ -102,11 +103,13 @@ __global__ void __launch_bounds__(W * 32)
       const int row = r0 + i;
       const int t = seg0 + row;
       const float z = sZ[row * CW + lane];
-      h = (1.f - z) * h + z * sT[row * CW + lane];
+      const float ht = sT[row * CW + lane];
+      const float hp = h;
+      h = (1.f - z) * h + z * ht;
       if (act && t < T) {
         const size_t o = ((size_t)b * T + t) * D + d;
         zo[o] = z;
-        ho[o] = h;
+        ho[o] = diff ? ht - hp : h;
         if (yo) yo[o] = h;
         if (out) out[o] = sR[row * CW + lane] + h;
       }
@@ -136,7 +139,7 @@ __global__ void __launch_bounds__(W * 32)
   const int c0 = (blockIdx.x % groups) * CW;
   const int d = c0 + lane;
   const bool act = d < D;
-  const float bhd = act ? bh[d] : 0.f;
+  const float bhd = act && ph ? bh[d] : 0.f;
   if (warp == 0) carry[lane] = 0.f;
   float accz = 0.f, acch = 0.f;
   const int nseg = (T + SEG - 1) / SEG;
@@ -144,7 +147,8 @@ __global__ void __launch_bounds__(W * 32)
     const int seg0 = sg * SEG;
     stage(sZ, z, D, b, T, D, seg0, c0);
     stage(sG, dy, D, b, T, D, seg0, c0);
-    stage(sP, ph, ldp, b, T, D, seg0, c0);
+    if (ph) stage(sP, ph, ldp, b, T, D, seg0, c0);
+    else stage(sP, h, D, b, T, D, seg0, c0);  // h holds e = h~ - h_prev
     cp_async_wait_all();
     __syncthreads();
     // warp 0 owns the LAST chunk of the segment (reverse time order)
@@ -171,9 +175,15 @@ __global__ void __launch_bounds__(W * 32)
       if (act && t < T) {
         const size_t o = ((size_t)b * T + t) * D + d;
         const size_t od = ((size_t)b * T + t) * ldd + d;
-        const float htv = sP[row * CW + lane] + bhd;
-        const float hp = t > 0 ? h[o - D] : 0.f;
-        const float vz = dh * (htv - hp) * zv * (1.f - zv);
+        float e;
+        if (ph) {
+          const float htv = sP[row * CW + lane] + bhd;
+          const float hp = t > 0 ? h[o - D] : 0.f;
+          e = htv - hp;
+        } else {
+          e = sP[row * CW + lane];
+        }
+        const float vz = dh * e * zv * (1.f - zv);
         const float vh = dh * zv;
         dz[od] = vz;
         dht[od] = vh;
@@ -210,13 +220,14 @@ void allow_smem(K kernel, size_t bytes) {
 
 cudaError_t gru_scan_fwd(const float* pz, const float* ph, int ldp, const float* bz,
                          const float* bh, float* z, float* h, float* y, const float* res,
-                         float* out, int B, int T, int D, cudaStream_t s) {
+                         float* out, int B, int T, int D, cudaStream_t s, bool h_as_diff) {
   if (B <= 0 || T <= 0) return cudaSuccess;
   if (D % 4 || ldp % 4) return cudaErrorInvalidValue;
   const size_t smem = (size_t)(out ? 3 : 2) * TILE * sizeof(float);
   allow_smem(scan_fwd_kernel, 3 * TILE * sizeof(float));
   const int grid = B * ((D + CW - 1) / CW);
-  scan_fwd_kernel<<<grid, W * 32, smem, s>>>(pz, ph, ldp, bz, bh, z, h, y, res, out, T, D);
+  scan_fwd_kernel<<<grid, W * 32, smem, s>>>(pz, ph, ldp, bz, bh, z, h, y, res, out, T, D,
+                                             h_as_diff ? 1 : 0);
   return launched();
 }
 
