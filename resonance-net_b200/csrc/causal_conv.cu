@@ -2,10 +2,15 @@
 //
 // Reference: src/causal_conv.cu:9-30 (one depthwise kernel launched per scale),
 // :33-39 + :61-71 (sum3 into the c3 slot), :85-130 and :150-187 (data and
-// weight gradients, the weight gradient on only K blocks). Here one thread
-// owns one channel over a 32-step time chunk, holds the 46-sample window
-// (14-step causal halo) in registers and produces all three scales; the weight
-// gradient is a two-level deterministic reduction over (batch, chunk).
+// weight gradients, the weight gradient on only K blocks).
+//
+// Layout: a persistent CTA owns 32 channels (lane = channel) and walks the
+// 128-step tiles of the sequences. A tile plus its 14-step halo ([142 rows x
+// 32 channels]) is copied global -> shared with cp.async (16 B per copy), three
+// tiles in flight per CTA; warp w runs steps [16w, 16w+16) of a tile from shared memory
+// with a 30-sample register window and writes each output row (128 B per
+// warp) coalesced. The weight gradient is a deterministic two-level
+// reduction: warps of a CTA in fixed order, then CTA partials in fixed order.
 //
 // Per-scale accumulation order matches the reference (sum += x*w over taps in
 // increasing k, zero left padding), and S = (c3 + c7) + c15 as its sum3.
@@ -13,43 +18,54 @@
 #include "kernels.cuh"
 
 namespace rnet_k {
+using namespace rnet_dev;
 
 namespace {
 
-constexpr int TC = 32;    // time steps per thread
-constexpr int HALO = 14;  // max kernel size - 1
-constexpr int CPB = 128;  // channels per block
-constexpr int MAX_PARTS = 192;
+constexpr int HALO = 14;             // max kernel size - 1
+constexpr int CW = 32;               // channels per CTA (lane = channel)
+constexpr int NW = 8;                // warps per CTA
+constexpr int STEPS = 16;            // steps per warp
+constexpr int TS = NW * STEPS;       // steps per tile
+constexpr int ROWS = TS + HALO;      // staged rows per tile
+constexpr int WIN = STEPS + HALO;    // register window per warp
+constexpr int MAX_PARTS = 64;        // weight-gradient partials per channel group
+constexpr int PIPE = 3;              // tiles in flight per CTA (cp.async groups)
 
-__global__ void __launch_bounds__(CPB)
-    conv_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w3,
-                    const float* __restrict__ w7, const float* __restrict__ w15,
-                    float* __restrict__ S, float* __restrict__ Sq, float* __restrict__ c7o,
-                    float* __restrict__ c15o, int T, int D, int nchunks) {
-  const int d = blockIdx.x * CPB + threadIdx.x;
-  if (d >= D) return;
-  const int b = blockIdx.y / nchunks;
-  const int t0 = (blockIdx.y % nchunks) * TC;
-  const float* xb = x + (size_t)b * T * D + d;
-  float win[TC + HALO];
-#pragma unroll
-  for (int i = 0; i < TC + HALO; ++i) {
-    const int t = t0 - HALO + i;
-    win[i] = (t >= 0 && t < T) ? xb[(size_t)t * D] : 0.0f;
+__device__ __forceinline__ void cp_async16(float* smem, const float* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)),
+               "l"(gmem), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Stage rows t = t_first .. t_first + ROWS - 1 of sequence b, channels
+// [c0, c0 + 32) of a [B, T, D] array into tile[ROWS][CW]; zero outside [0, T)
+// and past D.
+__device__ __forceinline__ void stage(float (*tile)[CW], const float* src, int b, int T, int D,
+                                      int t_first, int c0) {
+  for (int q = threadIdx.x; q < ROWS * (CW / 4); q += NW * 32) {
+    const int row = q / (CW / 4), part = q % (CW / 4);
+    const int t = t_first + row, ch = c0 + part * 4;
+    const bool valid = t >= 0 && t < T && ch < D;
+    const float* g = valid ? src + ((size_t)b * T + t) * D + ch : src;
+    cp_async16(&tile[row][part * 4], g, valid);
   }
-  float a3[3], a7[7], a15[15];
+}
+
+// Outputs of one warp's STEPS steps from its register window (output step i
+// uses x[t-(K-1)+k] = win[i + HALO - (K-1) + k]). WQ: also Sq = S + c7 + c15
+// (the reference's dmix operand); WC: also c7, c15. FULL: all STEPS steps
+// exist (no bounds test in the unrolled loop).
+template <bool WQ, bool WC, bool FULL>
+__device__ __forceinline__ void fwd_steps(const float (&win)[WIN], const float (&a3)[3],
+                                          const float (&a7)[7], const float (&a15)[15], float* pS,
+                                          float* pQ, float* p7, float* p15, int n, int D) {
 #pragma unroll
-  for (int k = 0; k < 3; ++k) a3[k] = w3[k * D + d];
-#pragma unroll
-  for (int k = 0; k < 7; ++k) a7[k] = w7[k * D + d];
-#pragma unroll
-  for (int k = 0; k < 15; ++k) a15[k] = w15[k * D + d];
-  const size_t base = (size_t)b * T * D + d;
-#pragma unroll
-  for (int i = 0; i < TC; ++i) {
-    const int t = t0 + i;
-    if (t >= T) break;
-    // output t uses x[t-(K-1)+k] = win[i + HALO - (K-1) + k]
+  for (int i = 0; i < STEPS; ++i) {
+    if (!FULL && i >= n) break;
     float s3 = 0.f, s7 = 0.f, s15 = 0.f;
 #pragma unroll
     for (int k = 0; k < 3; ++k) s3 += win[i + HALO - 2 + k] * a3[k];
@@ -58,81 +74,204 @@ __global__ void __launch_bounds__(CPB)
 #pragma unroll
     for (int k = 0; k < 15; ++k) s15 += win[i + k] * a15[k];
     const float sum = s3 + s7 + s15;
-    const size_t o = base + (size_t)t * D;
-    S[o] = sum;
-    if (Sq) Sq[o] = sum + s7 + s15;
-    if (c7o) c7o[o] = s7;
-    if (c15o) c15o[o] = s15;
+    *pS = sum;
+    pS += D;
+    if (WQ) {
+      *pQ = sum + s7 + s15;
+      pQ += D;
+    }
+    if (WC) {
+      *p7 = s7;
+      *p15 = s15;
+      p7 += D;
+      p15 += D;
+    }
   }
 }
 
-// Data + weight gradient. Block (channel group, part p) loops over work
-// items (b, chunk) = p, p + nparts, ...
-__global__ void __launch_bounds__(CPB)
+template <bool WQ, bool WC>
+__global__ void __launch_bounds__(NW * 32, 3)
+    conv_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w3,
+                    const float* __restrict__ w7, const float* __restrict__ w15,
+                    float* __restrict__ S, float* __restrict__ Sq, float* __restrict__ c7o,
+                    float* __restrict__ c15o, int B, int T, int D, int nseg, int nparts) {
+  // persistent over tiles (b, segment) = p, p + nparts, ... of one channel
+  // group, PIPE tiles in flight
+  extern __shared__ __align__(16) float smem[];
+  typedef float Tile[ROWS][CW];
+  Tile* sx = reinterpret_cast<Tile*>(smem);  // [PIPE]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = blockIdx.x * CW;
+  const int d = c0 + lane;
+  const bool act = d < D;
+  float a3[3], a7[7], a15[15];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) a3[k] = act ? w3[k * D + d] : 0.f;
+#pragma unroll
+  for (int k = 0; k < 7; ++k) a7[k] = act ? w7[k * D + d] : 0.f;
+#pragma unroll
+  for (int k = 0; k < 15; ++k) a15[k] = act ? w15[k * D + d] : 0.f;
+  const int r0 = warp * STEPS;  // window row j = x[t0 + r0 - HALO + j]
+  const int items = B * nseg;
+  auto stage_item = [&](int it, int buf) {
+    if (it < items)
+      stage(sx[buf], x, it / nseg, T, D, (it % nseg) * TS - HALO, c0);
+    asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty
+  };
+#pragma unroll
+  for (int q = 0; q < PIPE - 1; ++q) stage_item(blockIdx.y + q * nparts, q);
+  int buf = 0;
+  for (int it = blockIdx.y; it < items; it += nparts) {
+    stage_item(it + (PIPE - 1) * nparts, (buf + PIPE - 1) % PIPE);
+    asm volatile("cp.async.wait_group %0;" ::"n"(PIPE - 1) : "memory");
+    __syncthreads();
+    const int b = it / nseg;
+    const int t0 = (it % nseg) * TS;
+    if (act) {
+      float win[WIN];
+#pragma unroll
+      for (int j = 0; j < WIN; ++j) win[j] = sx[buf][r0 + j][lane];
+      const int tb = t0 + r0;
+      const size_t o = ((size_t)b * T + tb) * D + d;
+      const int n = T - tb < STEPS ? T - tb : STEPS;
+      if (n == STEPS)
+        fwd_steps<WQ, WC, true>(win, a3, a7, a15, S + o, Sq + o, c7o + o, c15o + o, STEPS, D);
+      else if (n > 0)
+        fwd_steps<WQ, WC, false>(win, a3, a7, a15, S + o, Sq + o, c7o + o, c15o + o, n, D);
+    }
+    __syncthreads();  // buffer `buf` is restaged PIPE - 1 iterations on
+    buf = (buf + 1) % PIPE;
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+// Data + weight gradient. CTA (channel group, part p) loops over tiles
+// (b, segment) = p, p + nparts, ...; dx rows of a tile need dS rows up to 14
+// steps AFTER it (anti-causal), the weight gradient x rows 14 steps before.
+// dx[t] = sum_K sum_k w_K[k] dS[t + (K-1) - k] for one warp's steps from its
+// dS window (gs[j] = dS[tb + j]); ACC: dx += instead of =.
+template <bool ACC, bool FULL>
+__device__ __forceinline__ void dx_steps(const float (&gs)[WIN], const float (&a3)[3],
+                                         const float (&a7)[7], const float (&a15)[15], float* px,
+                                         int n, int D) {
+#pragma unroll
+  for (int i = 0; i < STEPS; ++i) {
+    if (!FULL && i >= n) break;
+    float s3 = 0.f, s7 = 0.f, s15 = 0.f;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) s3 += a3[k] * gs[i + 2 - k];
+#pragma unroll
+    for (int k = 0; k < 7; ++k) s7 += a7[k] * gs[i + 6 - k];
+#pragma unroll
+    for (int k = 0; k < 15; ++k) s15 += a15[k] * gs[i + 14 - k];
+    const float v = s3 + s7 + s15;
+    *px = ACC ? *px + v : v;
+    px += D;
+  }
+}
+
+template <bool ACC>
+__global__ void __launch_bounds__(NW * 32, 2)
     conv_bwd_kernel(const float* __restrict__ dS, const float* __restrict__ x,
                     const float* __restrict__ w3, const float* __restrict__ w7,
                     const float* __restrict__ w15, float* __restrict__ dx,
-                    float* __restrict__ parts, int B, int T, int D, int nchunks, int nparts,
-                    int accumulate) {
-  const int d = blockIdx.x * CPB + threadIdx.x;
-  if (d >= D) return;
+                    float* __restrict__ parts, int B, int T, int D, int nseg, int nparts) {
+  // two buffers of {x tile, dS tile}: the next tile is staged while this one
+  // is consumed
+  extern __shared__ __align__(16) float smem[];
+  typedef float Tile[ROWS][CW];
+  Tile* sx = reinterpret_cast<Tile*>(smem);                     // [PIPE]
+  Tile* sg = reinterpret_cast<Tile*>(smem + PIPE * ROWS * CW);  // [PIPE]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = blockIdx.x * CW;
+  const int d = c0 + lane;
+  const bool act = d < D;
   float a3[3], a7[7], a15[15];
 #pragma unroll
-  for (int k = 0; k < 3; ++k) a3[k] = w3[k * D + d];
+  for (int k = 0; k < 3; ++k) a3[k] = act ? w3[k * D + d] : 0.f;
 #pragma unroll
-  for (int k = 0; k < 7; ++k) a7[k] = w7[k * D + d];
+  for (int k = 0; k < 7; ++k) a7[k] = act ? w7[k * D + d] : 0.f;
 #pragma unroll
-  for (int k = 0; k < 15; ++k) a15[k] = w15[k * D + d];
+  for (int k = 0; k < 15; ++k) a15[k] = act ? w15[k * D + d] : 0.f;
   float g3[3] = {0, 0, 0}, g7[7] = {0, 0, 0, 0, 0, 0, 0};
   float g15[15];
 #pragma unroll
   for (int k = 0; k < 15; ++k) g15[k] = 0.f;
-  const int items = B * nchunks;
+  const int r0 = warp * STEPS;
+  const int items = B * nseg;
+  auto stage_item = [&](int it, int buf) {
+    if (it < items) {
+      const int b = it / nseg;
+      const int t0 = (it % nseg) * TS;
+      stage(sx[buf], x, b, T, D, t0 - HALO, c0);  // row j = x[t0 - 14 + j]
+      stage(sg[buf], dS, b, T, D, t0, c0);        // row j = dS[t0 + j]
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty
+  };
+#pragma unroll
+  for (int q = 0; q < PIPE - 1; ++q) stage_item(blockIdx.y + q * nparts, q);
+  int buf = 0;
   for (int it = blockIdx.y; it < items; it += nparts) {
-    const int b = it / nchunks;
-    const int t0 = (it % nchunks) * TC;
-    const size_t base = (size_t)b * T * D + d;
-    float xs[TC + HALO];  // x[t0-14 .. t0+31]
-    float gs[TC + HALO];  // dS[t0 .. t0+45]
+    stage_item(it + (PIPE - 1) * nparts, (buf + PIPE - 1) % PIPE);
+    asm volatile("cp.async.wait_group %0;" ::"n"(PIPE - 1) : "memory");
+    __syncthreads();
+    const int b = it / nseg;
+    const int t0 = (it % nseg) * TS;
+    if (act) {
+      float gs[WIN];  // dS[t0 + r0 + j]
 #pragma unroll
-    for (int i = 0; i < TC + HALO; ++i) {
-      const int tx = t0 - HALO + i;
-      xs[i] = (tx >= 0 && tx < T) ? x[base + (size_t)tx * D] : 0.f;
-      const int tg = t0 + i;
-      gs[i] = (tg < T) ? dS[base + (size_t)tg * D] : 0.f;
+      for (int j = 0; j < WIN; ++j) gs[j] = sg[buf][r0 + j][lane];
+      const int tb = t0 + r0;
+      const int n = T - tb < STEPS ? T - tb : STEPS;
+      float* px = dx + ((size_t)b * T + tb) * D + d;
+      if (n == STEPS)
+        dx_steps<ACC, true>(gs, a3, a7, a15, px, STEPS, D);
+      else if (n > 0)
+        dx_steps<ACC, false>(gs, a3, a7, a15, px, n, D);
+      // weight grads: g_K[k] += x[t-(K-1)+k] * dS[t] (dS zero past T). Window
+      // row j = x[t0 + r0 - 14 + j] is read once and feeds every (k, i) with
+      // i + 14 - (K-1) + k = j; per k the sum still runs over i ascending.
+#pragma unroll
+      for (int j = 0; j < WIN; ++j) {
+        const float xv = sx[buf][r0 + j][lane];
+#pragma unroll
+        for (int k = 0; k < 15; ++k) {
+          const int i = j - k;
+          if (i >= 0 && i < STEPS) g15[k] += xv * gs[i];
+        }
+#pragma unroll
+        for (int k = 0; k < 7; ++k) {
+          const int i = j - 8 - k;
+          if (i >= 0 && i < STEPS) g7[k] += xv * gs[i];
+        }
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          const int i = j - 12 - k;
+          if (i >= 0 && i < STEPS) g3[k] += xv * gs[i];
+        }
+      }
     }
-#pragma unroll
-    for (int i = 0; i < TC; ++i) {
-      const int t = t0 + i;
-      if (t >= T) break;
-      // dx[t] = sum_K sum_k w_K[k] dS[t + (K-1) - k]  (dS index i + K-1-k in gs)
-      float s3 = 0.f, s7 = 0.f, s15 = 0.f;
-#pragma unroll
-      for (int k = 0; k < 3; ++k) s3 += a3[k] * gs[i + 2 - k];
-#pragma unroll
-      for (int k = 0; k < 7; ++k) s7 += a7[k] * gs[i + 6 - k];
-#pragma unroll
-      for (int k = 0; k < 15; ++k) s15 += a15[k] * gs[i + 14 - k];
-      const size_t o = base + (size_t)t * D;
-      const float v = s3 + s7 + s15;
-      dx[o] = accumulate ? dx[o] + v : v;
-      // weight grads: x[t-(K-1)+k] * dS[t]
-      const float g = gs[i];
-#pragma unroll
-      for (int k = 0; k < 3; ++k) g3[k] += xs[i + HALO - 2 + k] * g;
-#pragma unroll
-      for (int k = 0; k < 7; ++k) g7[k] += xs[i + HALO - 6 + k] * g;
-#pragma unroll
-      for (int k = 0; k < 15; ++k) g15[k] += xs[i + k] * g;
-    }
+    __syncthreads();  // buffer `buf` is restaged PIPE - 1 iterations on
+    buf = (buf + 1) % PIPE;
   }
-  float* pp = parts + (size_t)blockIdx.y * 25 * D + d;
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  // CTA partial: sum the 8 warps' accumulators in warp order
+  float(*red)[NW][CW] = reinterpret_cast<float(*)[NW][CW]>(smem);  // [25][8][32]
+  static_assert(25 * NW * CW <= 2 * PIPE * ROWS * CW, "reduction scratch");
 #pragma unroll
-  for (int k = 0; k < 3; ++k) pp[(size_t)k * D] = g3[k];
+  for (int k = 0; k < 3; ++k) red[k][warp][lane] = g3[k];
 #pragma unroll
-  for (int k = 0; k < 7; ++k) pp[(size_t)(3 + k) * D] = g7[k];
+  for (int k = 0; k < 7; ++k) red[3 + k][warp][lane] = g7[k];
 #pragma unroll
-  for (int k = 0; k < 15; ++k) pp[(size_t)(10 + k) * D] = g15[k];
+  for (int k = 0; k < 15; ++k) red[10 + k][warp][lane] = g15[k];
+  __syncthreads();
+  for (int j = warp; j < 25; j += NW) {
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) sum += red[j][w][lane];
+    if (act) parts[((size_t)blockIdx.y * 25 + j) * D + d] = sum;
+  }
 }
 
 __global__ void conv_wgrad_reduce(const float* __restrict__ parts, int nparts, int D,
@@ -149,11 +288,11 @@ __global__ void conv_wgrad_reduce(const float* __restrict__ parts, int nparts, i
 }
 
 int nparts_for(int B, int T, int D) {
-  const int nchunks = (T + TC - 1) / TC;
-  const int groups = (D + CPB - 1) / CPB;
-  int p = (148 * 6) / groups;
+  const int nseg = (T + TS - 1) / TS;
+  const int groups = (D + CW - 1) / CW;
+  int p = (148 * 2) / groups;  // every CTA resident (two per SM)
   if (p > MAX_PARTS) p = MAX_PARTS;
-  if (p > B * nchunks) p = B * nchunks;
+  if (p > B * nseg) p = B * nseg;
   return p < 1 ? 1 : p;
 }
 
@@ -162,9 +301,21 @@ int nparts_for(int B, int T, int D) {
 cudaError_t conv_fwd(const float* x, const float* w3, const float* w7, const float* w15, float* S,
                      float* Sq, float* c7, float* c15, int B, int T, int D, cudaStream_t s) {
   if (B <= 0 || T <= 0) return cudaSuccess;
-  const int nchunks = (T + TC - 1) / TC;
-  dim3 grid((D + CPB - 1) / CPB, B * nchunks);
-  conv_fwd_kernel<<<grid, CPB, 0, s>>>(x, w3, w7, w15, S, Sq, c7, c15, T, D, nchunks);
+  if (D % 4) return cudaErrorInvalidValue;
+  const int nseg = (T + TS - 1) / TS;
+  const int groups = (D + CW - 1) / CW;
+  // persistent: three CTAs per SM (<= 85 registers x 256 threads, 55 KB each)
+  int np = (148 * 3) / groups;
+  if (np > B * nseg) np = B * nseg;
+  if (np < 1) np = 1;
+  // Sq (model path) and c7/c15 (layer-op caches) are never asked for together
+  if ((c7 == nullptr) != (c15 == nullptr) || (Sq && c7)) return cudaErrorInvalidValue;
+  constexpr size_t smem = PIPE * ROWS * CW * sizeof(float);
+  auto kern = Sq ? conv_fwd_kernel<true, false>
+                 : (c7 ? conv_fwd_kernel<false, true> : conv_fwd_kernel<false, false>);
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(groups, np);
+  kern<<<grid, NW * 32, smem, s>>>(x, w3, w7, w15, S, Sq, c7, c15, B, T, D, nseg, np);
   return launched();
 }
 
@@ -176,11 +327,14 @@ cudaError_t conv_bwd(const float* dS, const float* x, const float* w3, const flo
                      const float* w15, float* dx, float* dw3, float* dw7, float* dw15,
                      float* partials, int B, int T, int D, int accumulate, cudaStream_t s) {
   if (B <= 0 || T <= 0) return cudaSuccess;
-  const int nchunks = (T + TC - 1) / TC;
+  if (D % 4) return cudaErrorInvalidValue;
+  const int nseg = (T + TS - 1) / TS;
   const int np = nparts_for(B, T, D);
-  dim3 grid((D + CPB - 1) / CPB, np);
-  conv_bwd_kernel<<<grid, CPB, 0, s>>>(dS, x, w3, w7, w15, dx, partials, B, T, D, nchunks, np,
-                                       accumulate);
+  dim3 grid((D + CW - 1) / CW, np);
+  constexpr size_t smem = 2 * PIPE * ROWS * CW * sizeof(float);
+  auto kern = accumulate ? conv_bwd_kernel<true> : conv_bwd_kernel<false>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<grid, NW * 32, smem, s>>>(dS, x, w3, w7, w15, dx, partials, B, T, D, nseg, np);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   conv_wgrad_reduce<<<(25 * D + 255) / 256, 256, 0, s>>>(partials, np, D, dw3, dw7, dw15);

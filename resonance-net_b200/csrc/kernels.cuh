@@ -20,8 +20,8 @@ cudaError_t rms_norm_bwd(const float* dy, const float* x, const float* w, const 
 
 // ---- depthwise causal convolution (causal_conv.cu) -------------------------
 // c3/c7/c15 of x over each length-T sequence, S = c3 + c7 + c15.
-// Writes S; optionally Sq = S + c7 + c15 (reference dmix operand) and/or c7,
-// c15 individually (reference conv_buf layout).
+// Writes S; optionally Sq = S + c7 + c15 (reference dmix operand) or c7, c15
+// individually (reference conv_buf layout), not both. D % 4 == 0.
 cudaError_t conv_fwd(const float* x, const float* w3, const float* w7, const float* w15,
                      float* S, float* Sq, float* c7, float* c15, int B, int T, int D,
                      cudaStream_t s);
