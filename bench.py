@@ -59,6 +59,7 @@ def parse():
     ap.add_argument("--k", type=int, default=512)
     ap.add_argument("--amn", type=int, default=0)
     ap.add_argument("--cg", type=int, default=0, help="--op: GEMM CTA group (0 auto, 1, 2)")
+    ap.add_argument("--epi", type=int, default=0, help="--op gemm: 0 store, 1 accumulate, 2 residual")
     ap.add_argument("--bmn", type=int, default=0)
     return ap.parse_args()
 
@@ -423,9 +424,11 @@ def run_op(args):
         Bm = rnd(K, Nn) if args.bmn else rnd(Nn, K)
         C = z(M, Nn)
         lda, ldb = (M if args.amn else K), (Nn if args.bmn else K)
+        R = rnd(M, Nn)
         fn = lambda: rnet.call("rnet_gemm_f32", M, Nn, K, p(A), lda, args.amn, p(Bm), ldb,
-                               args.bmn, p(C), Nn, p(C), Nn, 0, F32(1.0), None)
-        work = f"gemm M={M} N={Nn} K={K} a_mn={args.amn} b_mn={args.bmn} cg={args.cg}"
+                               args.bmn, p(C), Nn, p(R), Nn, args.epi, F32(1.0), None)
+        work = (f"gemm M={M} N={Nn} K={K} a_mn={args.amn} b_mn={args.bmn} cg={args.cg} "
+                f"epi={args.epi}")
     elif args.op in ("scan_fwd", "scan_bwd"):
         x = rnd(N, D)
         Wz, Wh = rnd(D, D, scale=D ** -0.5), rnd(D, D, scale=D ** -0.5)

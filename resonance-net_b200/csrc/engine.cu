@@ -40,15 +40,6 @@ Epilogue epi_accum(float* C, int ldc) {
   e.ldc = ldc;
   return e;
 }
-Epilogue epi_resid(float* C, const float* R, int ld) {
-  Epilogue e;
-  e.kind = EPI_RESID;
-  e.C = C;
-  e.ldc = ld;
-  e.R = R;
-  e.ldr = ld;
-  return e;
-}
 
 size_t layer_count(const rnet_model_config& c) {
   const size_t D = c.d_model, F = c.d_ff, S = c.n_slots;
@@ -317,11 +308,14 @@ int Engine::profile_read(ProfStats* out, bool reset) {
 
 // GEMM through the engine: algorithmic FLOPs 2MNK, bytes = operands + output
 // (+ output read for residual / accumulate epilogues).
-#define MM(M, N, K, A, B, E, PAIR)                                                        \
+#define MMS(M, N, K, A, B, E, PAIR, SPLITS)                                               \
   PROF(PK_GEMM, 2.0 * (M) * (N) * (K),                                                    \
        4.0 * ((double)(M) * (K) + (double)(N) * (K) +                                     \
               (double)(M) * (N) * (((E).kind == EPI_RESID || (E).kind == EPI_ACCUM) ? 2 : 1)), \
-       gemm_tf32x3(stream_, (M), (N), (K), (A), (B), (E), (PAIR), 0, err))
+       gemm_tf32x3(stream_, (M), (N), (K), (A), (B), (E), (PAIR), (SPLITS), err))
+#define MM(M, N, K, A, B, E, PAIR) MMS(M, N, K, A, B, E, PAIR, 0)
+// residual accumulation: one K pass (deterministic, one rounding per element)
+#define MM_RES(M, N, K, A, B, C) MMS(M, N, K, A, B, epi_accum(C, N), 0, 1)
 
 // ------------------------------------------------------------------ forward
 int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B, int T,
@@ -335,18 +329,22 @@ int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B,
   const float* VT = VT_ + (size_t)l * S * D;
   const double ND4 = 4.0 * N * D;
   // 1. multi-scale causal conv (reference layer_forward :287-299)
-  PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(Xl, w.n1, a.n1, a.rinv1, N, D, eps, s));
+  // Residual sums are seeded by the kernel that already holds the residual
+  // row (RMSNorm input copy, scan second output) and the GEMM accumulates
+  // into them (red.add: the same single rounding as R + acc, without the
+  // epilogue's dependent residual loads).
+  PROF(PK_RMS_FWD, 0, 3 * ND4, rnet_k::rms_norm_fwd(Xl, w.n1, a.n1, a.rinv1, N, D, eps, s, a.r1));
   PROF(PK_CONV_FWD, 50.0 * N * D, (conv_quirk ? 3 : 2) * ND4,
        rnet_k::conv_fwd(a.n1, w.c3, w.c7, w.c15, a.S, conv_quirk ? a.Sq : nullptr, nullptr,
                         nullptr, B, T, D, s));
-  MM(N, D, D, kmaj(a.S, D), kmaj(w.mix, D), epi_resid(a.r1, Xl, D), 0);
+  MM_RES(N, D, D, kmaj(a.S, D), kmaj(w.mix, D), a.r1);
   // 2. MinGRU (:301-313): P = n2 [Wz;Wh]^T, fused gate + scan + residual
   PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(a.r1, w.n2, a.n2, a.rinv2, N, D, eps, s));
   MM(N, 2 * D, D, kmaj(a.n2, D), kmaj(w.Wz, D), epi_store(a.P, 2 * D), 0);
   // training keeps e = h~ - h_prev (all the backward needs), prefill keeps h
-  PROF(PK_SCAN_FWD, 0, 6 * ND4,
+  PROF(PK_SCAN_FWD, 0, 7 * ND4,
        rnet_k::gru_scan_fwd(a.P, a.P + D, 2 * D, w.bz, w.bh, a.z, a.h, nullptr, a.r1, a.r2, B, T,
-                            D, s, train));
+                            D, s, train, a.r3));
   // 3. slot memory (:315-330)
   PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(a.r2, w.n3, a.n3, a.rinv3, N, D, eps, s));
   MM(N, D, D, kmaj(a.n3, D), kmaj(w.pq, D), epi_store(a.q, D), 0);
@@ -362,9 +360,9 @@ int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B,
   }
   PROF(PK_SLOT_GATHER, 2.0 * k * N * D, (1 + k) * ND4,
        rnet_k::slot_gather(a.idx, a.w, VT, a.r, N, D, S, k, err, s));
-  MM(N, D, D, kmaj(a.r, D), kmaj(w.pout, D), epi_resid(a.r3, a.r2, D), 0);
+  MM_RES(N, D, D, kmaj(a.r, D), kmaj(w.pout, D), a.r3);
   // 4. SwiGLU FFN (:332-342): paired gate|up tiles, SiLU*up in the epilogue
-  PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(a.r3, w.n4, a.n4, a.rinv4, N, D, eps, s));
+  PROF(PK_RMS_FWD, 0, 3 * ND4, rnet_k::rms_norm_fwd(a.r3, w.n4, a.n4, a.rinv4, N, D, eps, s, Xn));
   {
     Epilogue e;
     e.kind = EPI_SWIGLU_FWD;
@@ -375,7 +373,7 @@ int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B,
     MM(N, F, D, kmaj(a.n4, D), kmaj(w.gate, D), e, F);  // 2*N*F*D each for gate and up
     if (prof_on_) prof_.back().flops *= 2.0;
   }
-  MM(N, D, F, kmaj(a.H, F), kmaj(w.down, F), epi_resid(Xn, a.r3, D), 0);
+  MM_RES(N, D, F, kmaj(a.H, F), kmaj(w.down, F), Xn);
   return RNET_OK;
 }
 
@@ -617,7 +615,7 @@ int Engine::decode_step(Decoder* d, const int* d_tokens) {
     float* h = ring + (size_t)M * 14 * D;
     CK(rnet_k::rms_norm_fwd(d->x, w.n1, d->n, nullptr, M, D, eps, s));
     CK(rnet_k::decode_conv(d->n, ring, d->pos, w.c3, w.c7, w.c15, d->S, M, D, s));
-    MM(M, D, D, kmaj(d->S, D), kmaj(w.mix, D), epi_resid(d->x, d->x, D), 0);
+    MM_RES(M, D, D, kmaj(d->S, D), kmaj(w.mix, D), d->x);
     CK(rnet_k::rms_norm_fwd(d->x, w.n2, d->n, nullptr, M, D, eps, s));
     MM(M, 2 * D, D, kmaj(d->n, D), kmaj(w.Wz, D), epi_store(d->P, 2 * D), 0);
     CK(rnet_k::decode_gru(d->P, w.bz, w.bh, h, d->x, M, D, s));
@@ -631,7 +629,7 @@ int Engine::decode_step(Decoder* d, const int* d_tokens) {
       MM(M, S, D, kmaj(d->q, D), kmaj(KT_ + (size_t)l * S * D, D), e, 0);
     }
     CK(rnet_k::slot_gather(d->idx, d->w, VT_ + (size_t)l * S * D, d->r, M, D, S, 2, err, s));
-    MM(M, D, D, kmaj(d->r, D), kmaj(w.pout, D), epi_resid(d->x, d->x, D), 0);
+    MM_RES(M, D, D, kmaj(d->r, D), kmaj(w.pout, D), d->x);
     CK(rnet_k::rms_norm_fwd(d->x, w.n4, d->n, nullptr, M, D, eps, s));
     {
       Epilogue e;
@@ -642,7 +640,7 @@ int Engine::decode_step(Decoder* d, const int* d_tokens) {
       e.ldf = F;
       MM(M, F, D, kmaj(d->n, D), kmaj(w.gate, D), e, F);
     }
-    MM(M, D, F, kmaj(d->H, F), kmaj(w.down, F), epi_resid(d->x, d->x, D), 0);
+    MM_RES(M, D, F, kmaj(d->H, F), kmaj(w.down, F), d->x);
   }
   CK(rnet_k::rms_norm_fwd(d->x, fnorm_, d->n, nullptr, M, D, eps, s));
   MM(M, V, D, kmaj(d->n, D), kmaj(outw_, D), epi_store(d->logits, V), 0);

@@ -272,8 +272,14 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
     }
     return;
   }
+  // residual: this thread's 32-column slice of row `row` is one 128-byte
+  // line; the next chunk's line is pulled into L1 while this one is stored
+  const bool resid = e.kind == EPI_RESID && row < p.M;
+  const float* rrow = e.R + (size_t)row * e.ldr + nt * BN;
+  if (resid && nt * BN < p.N) prefetch_l1(rrow);
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
+    if (resid && c + 1 < BN / 32 && nt * BN + (c + 1) * 32 < p.N) prefetch_l1(rrow + (c + 1) * 32);
     tmem_ld_32cols(tacc + c * 32, v);
     store_row_chunk(p, e.kind, row, nt * BN + c * 32, v);
   }

@@ -11,8 +11,10 @@ cudaError_t launched(unsigned n = 1);
 
 // ---- RMSNorm (rms_norm.cu) ------------------------------------------------
 // y = x * rinv * w, rinv = rsqrt(mean(x^2) + eps)        (y may be null)
+// xcopy (optional): also store x there (seeds a residual sum that a GEMM then
+// accumulates into).
 cudaError_t rms_norm_fwd(const float* x, const float* w, float* y, float* rinv, int rows,
-                         int D, float eps, cudaStream_t s);
+                         int D, float eps, cudaStream_t s, float* xcopy = nullptr);
 // dx_norm = rinv*(dy*w - xhat*mean(dy*w*xhat)); dw += sum_rows dy*xhat.
 // mode 0: dx = dx_norm (overwrite); mode 1: dx += dx_norm (residual stream).
 cudaError_t rms_norm_bwd(const float* dy, const float* x, const float* w, const float* rinv,
@@ -38,9 +40,11 @@ cudaError_t conv_bwd(const float* dS, const float* x, const float* w3, const flo
 // pz/ph rows have stride ldp. Writes z, h; optional y = h (copy) and optional
 // residual out = res + h. h_as_diff: the `h` output receives e_t = h~_t -
 // h_{t-1} instead (all the backward needs of h~ and h; exact in fp32).
+// out2 (optional): a second copy of out.
 cudaError_t gru_scan_fwd(const float* pz, const float* ph, int ldp, const float* bz,
                          const float* bh, float* z, float* h, float* y, const float* res,
-                         float* out, int B, int T, int D, cudaStream_t s, bool h_as_diff = false);
+                         float* out, int B, int T, int D, cudaStream_t s, bool h_as_diff = false,
+                         float* out2 = nullptr);
 // Reverse scan: dh_t = dy_t + (1 - z_{t+1}) dh_{t+1};
 // dz = dh (h~ - h_{t-1}) z (1-z), dh~ = dh z. h~ = ph + bh (ph stride ldp).
 // ph == nullptr: `h` holds e = h~ - h_{t-1} from gru_scan_fwd(h_as_diff) and

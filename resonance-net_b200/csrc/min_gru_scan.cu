@@ -56,8 +56,8 @@ __global__ void __launch_bounds__(W * 32)
     scan_fwd_kernel(const float* __restrict__ pz, const float* __restrict__ ph, int ldp,
                     const float* __restrict__ bz, const float* __restrict__ bh,
                     float* __restrict__ zo, float* __restrict__ ho, float* __restrict__ yo,
-                    const float* __restrict__ res, float* __restrict__ out, int T, int D,
-                    int diff) {
+                    const float* __restrict__ res, float* __restrict__ out,
+                    float* __restrict__ out2, int T, int D, int diff) {
   extern __shared__ float smem[];
   float* sZ = smem;             // pz, then z
   float* sT = smem + TILE;      // ph, then h~
@@ -111,7 +111,11 @@ __global__ void __launch_bounds__(W * 32)
         zo[o] = z;
         ho[o] = diff ? ht - hp : h;
         if (yo) yo[o] = h;
-        if (out) out[o] = sR[row * CW + lane] + h;
+        if (out) {
+          const float r = sR[row * CW + lane] + h;
+          out[o] = r;
+          if (out2) out2[o] = r;
+        }
       }
     }
     __syncthreads();
@@ -220,13 +224,14 @@ void allow_smem(K kernel, size_t bytes) {
 
 cudaError_t gru_scan_fwd(const float* pz, const float* ph, int ldp, const float* bz,
                          const float* bh, float* z, float* h, float* y, const float* res,
-                         float* out, int B, int T, int D, cudaStream_t s, bool h_as_diff) {
+                         float* out, int B, int T, int D, cudaStream_t s, bool h_as_diff,
+                         float* out2) {
   if (B <= 0 || T <= 0) return cudaSuccess;
   if (D % 4 || ldp % 4) return cudaErrorInvalidValue;
   const size_t smem = (size_t)(out ? 3 : 2) * TILE * sizeof(float);
   allow_smem(scan_fwd_kernel, 3 * TILE * sizeof(float));
   const int grid = B * ((D + CW - 1) / CW);
-  scan_fwd_kernel<<<grid, W * 32, smem, s>>>(pz, ph, ldp, bz, bh, z, h, y, res, out, T, D,
+  scan_fwd_kernel<<<grid, W * 32, smem, s>>>(pz, ph, ldp, bz, bh, z, h, y, res, out, out2, T, D,
                                              h_as_diff ? 1 : 0);
   return launched();
 }

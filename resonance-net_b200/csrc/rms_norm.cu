@@ -22,7 +22,8 @@ constexpr int WARPS = 8;
 template <int VPL>
 __global__ void __launch_bounds__(WARPS * 32)
     rms_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                   float* __restrict__ y, float* __restrict__ rinv, int rows, int D, float eps) {
+                   float* __restrict__ y, float* __restrict__ rinv, int rows, int D, float eps,
+                   float* __restrict__ xcopy) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = D >> 2;
   const float4* w4 = reinterpret_cast<const float4*>(w);
@@ -35,6 +36,14 @@ __global__ void __launch_bounds__(WARPS * 32)
       const int c = lane + 32 * j;
       v[j] = c < nv ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
       ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+    }
+    if (xcopy) {
+      float4* cr = reinterpret_cast<float4*>(xcopy + (size_t)row * D);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nv) cr[c] = v[j];
+      }
     }
     ss = warp_sum(ss);
     const float ri = rsqrtf(ss / (float)D + eps);
@@ -119,6 +128,129 @@ __global__ void __launch_bounds__(WARPS * 32)
   }
 }
 
+// Backward for D <= STAGED_MAX_D: persistent CTAs walk groups of WARPS rows
+// (one row per warp); the dy / x (/ dx when accumulating) rows of the next
+// group are copied global -> shared with cp.async while the current group is
+// computed, so loads stay in flight through the reductions and stores.
+constexpr int STAGED_MAX_D = 512;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(WARPS * 32, 2)
+    rms_bwd_staged_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                          const float* __restrict__ w, const float* __restrict__ rinv,
+                          float* __restrict__ dx, float* __restrict__ dw, int rows, int D,
+                          int mode) {
+  // [2 stages][3 arrays][WARPS rows][D]
+  extern __shared__ __align__(16) float sbuf[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nv = D >> 2;
+  const int narr = mode == 1 ? 3 : 2;
+  auto slot = [&](int st, int arr, int wr) {
+    return sbuf + ((size_t)(st * 3 + arr) * WARPS + wr) * D;
+  };
+  const int ngroups = (rows + WARPS - 1) / WARPS;
+  // stage group g into stage st: every thread copies 16 B pieces of the rows
+  auto stage = [&](int g, int st) {
+    if (g < ngroups) {
+      const int r0 = g * WARPS;
+      const int pieces = narr * WARPS * nv;
+      for (int q = threadIdx.x; q < pieces; q += WARPS * 32) {
+        const int arr = q / (WARPS * nv);
+        const int rem = q - arr * WARPS * nv;
+        const int wr = rem / nv, c = rem - wr * nv;
+        const int row = r0 + wr;
+        if (row < rows) {
+          const float* src = arr == 0 ? dy : (arr == 1 ? x : dx);
+          cp_async16(slot(st, arr, wr) + 4 * c, src + (size_t)row * D + 4 * c);
+        }
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float4 acc[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4 wv[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int c = lane + 32 * j;
+    wv[j] = c < nv ? w4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const float invD = 1.0f / (float)D;
+  int st = 0;
+  stage(blockIdx.x, 0);
+  for (int g = blockIdx.x; g < ngroups; g += gridDim.x) {
+    stage(g + gridDim.x, st ^ 1);
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();
+    const int row = g * WARPS + warp;
+    if (row < rows) {
+      const float4* dyr = reinterpret_cast<const float4*>(slot(st, 0, warp));
+      const float4* xr = reinterpret_cast<const float4*>(slot(st, 1, warp));
+      const float4* pr = reinterpret_cast<const float4*>(slot(st, 2, warp));
+      const float ri = rinv[row];
+      float4 gv[VPL], xh[VPL];
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nv) {
+          const float4 a = dyr[c], b = xr[c], ww = wv[j];
+          gv[j] = a;
+          xh[j] = make_float4(b.x * ri, b.y * ri, b.z * ri, b.w * ri);
+          dot += a.x * ww.x * xh[j].x + a.y * ww.y * xh[j].y + a.z * ww.z * xh[j].z +
+                 a.w * ww.w * xh[j].w;
+        }
+      }
+      dot = warp_sum(dot) * invD;
+      float4* dxr = reinterpret_cast<float4*>(dx + (size_t)row * D);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nv) {
+          const float4 ww = wv[j];
+          float4 o = make_float4(ri * (gv[j].x * ww.x - xh[j].x * dot),
+                                 ri * (gv[j].y * ww.y - xh[j].y * dot),
+                                 ri * (gv[j].z * ww.z - xh[j].z * dot),
+                                 ri * (gv[j].w * ww.w - xh[j].w * dot));
+          if (mode == 1) {
+            const float4 p = pr[c];
+            o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+          }
+          dxr[c] = o;
+          acc[j].x += gv[j].x * xh[j].x;
+          acc[j].y += gv[j].y * xh[j].y;
+          acc[j].z += gv[j].z * xh[j].z;
+          acc[j].w += gv[j].w * xh[j].w;
+        }
+      }
+    }
+    __syncthreads();  // stage `st` is refilled next iteration
+    st ^= 1;
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  // per-warp partials (reusing the staging buffer), fixed-order sum over warps
+  float* sdw = sbuf;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nv) reinterpret_cast<float4*>(sdw + (size_t)warp * D)[c] = acc[j];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float sum = 0.f;
+    for (int k = 0; k < WARPS; ++k) sum += sdw[(size_t)k * D + i];
+    atomicAdd(&dw[i], sum);
+  }
+}
+
 int sm_count() {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -128,16 +260,33 @@ int sm_count() {
 
 template <int VPL>
 cudaError_t fwd_t(const float* x, const float* w, float* y, float* rinv, int rows, int D,
-                  float eps, cudaStream_t s) {
+                  float eps, cudaStream_t s, float* xcopy) {
   const int need = (rows + WARPS - 1) / WARPS;
   const int cap = sm_count() * 8;
-  rms_fwd_kernel<VPL><<<need < cap ? need : cap, WARPS * 32, 0, s>>>(x, w, y, rinv, rows, D, eps);
+  rms_fwd_kernel<VPL><<<need < cap ? need : cap, WARPS * 32, 0, s>>>(x, w, y, rinv, rows, D, eps,
+                                                                          xcopy);
   return launched();
 }
 
 template <int VPL>
 cudaError_t bwd_t(const float* dy, const float* x, const float* w, const float* rinv, float* dx,
                   float* dw, int rows, int D, int mode, cudaStream_t s) {
+  if constexpr (VPL * 128 <= STAGED_MAX_D) {
+    const size_t smem = (size_t)2 * 3 * WARPS * D * sizeof(float);
+    static bool set = false;
+    if (!set) {
+      cudaFuncSetAttribute(rms_bwd_staged_kernel<VPL>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)((size_t)2 * 3 * WARPS * STAGED_MAX_D * sizeof(float)));
+      set = true;
+    }
+    const int ngroups = (rows + WARPS - 1) / WARPS;
+    int grid = sm_count() * 2;  // two CTAs per SM (2 x 96 KB at D = 512)
+    if (grid > ngroups) grid = ngroups;
+    rms_bwd_staged_kernel<VPL><<<grid, WARPS * 32, smem, s>>>(dy, x, w, rinv, dx, dw, rows, D,
+                                                              mode);
+    return launched();
+  }
   // >= 4 rows per warp so the dw partial flush is amortised
   int grid = (rows + WARPS * 4 - 1) / (WARPS * 4);
   const int cap = sm_count() * 6;
@@ -159,15 +308,15 @@ cudaError_t bwd_t(const float* dy, const float* x, const float* w, const float* 
 }  // namespace
 
 cudaError_t rms_norm_fwd(const float* x, const float* w, float* y, float* rinv, int rows, int D,
-                         float eps, cudaStream_t s) {
+                         float eps, cudaStream_t s, float* xcopy) {
   if (rows <= 0) return cudaSuccess;
   if (D % 4 != 0 || D > 2048) return cudaErrorInvalidValue;
   const int vpl = (D + 127) / 128;
-  if (vpl <= 1) return fwd_t<1>(x, w, y, rinv, rows, D, eps, s);
-  if (vpl <= 2) return fwd_t<2>(x, w, y, rinv, rows, D, eps, s);
-  if (vpl <= 4) return fwd_t<4>(x, w, y, rinv, rows, D, eps, s);
-  if (vpl <= 8) return fwd_t<8>(x, w, y, rinv, rows, D, eps, s);
-  return fwd_t<16>(x, w, y, rinv, rows, D, eps, s);
+  if (vpl <= 1) return fwd_t<1>(x, w, y, rinv, rows, D, eps, s, xcopy);
+  if (vpl <= 2) return fwd_t<2>(x, w, y, rinv, rows, D, eps, s, xcopy);
+  if (vpl <= 4) return fwd_t<4>(x, w, y, rinv, rows, D, eps, s, xcopy);
+  if (vpl <= 8) return fwd_t<8>(x, w, y, rinv, rows, D, eps, s, xcopy);
+  return fwd_t<16>(x, w, y, rinv, rows, D, eps, s, xcopy);
 }
 
 cudaError_t rms_norm_bwd(const float* dy, const float* x, const float* w, const float* rinv,
