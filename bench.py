@@ -92,12 +92,14 @@ class ClockSampler:
         self.t0 = self.t1 = None
 
     def start(self):
+        if self.gpu is None:
+            return
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -234,18 +236,29 @@ def run_ours(args, rank, world, local):
     model.synchronize()
 
     # ---- device-resident timed region (value) ------------------------------
-    clocks = ClockSampler(local)
+    # one sampler (rank 0, its own GPU): NVML polling from every rank at once
+    # measurably slows the other ranks' steps
+    clocks = ClockSampler(local) if rank == 0 else ClockSampler(None)
+    clocks.start()  # returns after its first sample, before the ranks align
     barrier()
-    clocks.start()
     n0 = rnet.kernel_launches()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    per_step = os.environ.get("RNET_BENCH_PER_STEP") == "1"
+    step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)] if per_step else []
     clocks.mark(True)
     ev0.record(stream)
     for i in range(args.steps):
+        if per_step:
+            step_ev[i].record(stream)
         model.train_step(d_in[i % POOL], d_tg[i % POOL], B, T, LR, CLIP, d_loss)
+    if per_step:
+        step_ev[args.steps].record(stream)
     ev1.record(stream)
     ev1.synchronize()
     clocks.mark(False)
+    if per_step:
+        print(f"rank {rank} step ms: " + " ".join(f"{step_ev[i].elapsed_time(step_ev[i + 1]):.2f}"
+                                                  for i in range(args.steps)), file=sys.stderr)
     launches = rnet.kernel_launches() - n0
     barrier()
     ck = clocks.stop()
