@@ -59,6 +59,11 @@ def parse():
     ap.add_argument("--k", type=int, default=512)
     ap.add_argument("--amn", type=int, default=0)
     ap.add_argument("--cg", type=int, default=0, help="--op: GEMM CTA group (0 auto, 1, 2)")
+    ap.add_argument("--decode", action="store_true",
+                    help="config 4: prefill + batched greedy decode instead of training")
+    ap.add_argument("--streams", type=int, default=256, help="--decode: streams over all GPUs")
+    ap.add_argument("--prompt", type=int, default=4096, help="--decode: prefill length")
+    ap.add_argument("--gen", type=int, default=1024, help="--decode: decode steps")
     ap.add_argument("--epi", type=int, default=0, help="--op gemm: 0 store, 1 accumulate, 2 residual")
     ap.add_argument("--bmn", type=int, default=0)
     return ap.parse_args()
@@ -520,11 +525,126 @@ def run_op(args):
                       "ms_per_call": round(e0.elapsed_time(e1) / args.steps, 4)}), flush=True)
 
 
+def run_decode(args, rank, world, local):
+    """Config 4: prefill of `streams` Zipf-byte prompts of length `prompt` through
+    the chunked scan, then `gen` greedy decode steps carrying the O(1) recurrent
+    state (graph-replayed step). Streams are split over the ranks with no
+    collective (strong scaling of a fixed stream count)."""
+    import numpy as np
+    import torch
+    rnet = importlib.import_module("resonance-net_b200")
+    rdata = importlib.import_module("resonance-net_b200.data")
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        pg = dist
+    M = args.streams // world
+    T, G = args.prompt, args.gen
+    cfg = rnet.ModelConfig.make(d_model=CFG["d_model"], n_layers=CFG["n_layers"],
+                                d_ff=CFG["d_ff"], n_slots=CFG["n_slots"], top_k=CFG["top_k"],
+                                vocab=CFG["vocab"], seq_len=T)
+    model = rnet.Model(cfg, device=local, reference_init=False)
+    model.set_params(rdata.init_params_normal(cfg, seed=1234))
+    dec = rnet.Decoder(model, M)
+    tok, _ = rdata.zipf_tokens(M, T, seed=11 + rank)
+    h_tok = torch.from_numpy(np.ascontiguousarray(tok.reshape(-1))).pin_memory()
+    d_tok = h_tok.cuda()
+    d_out = torch.zeros(G, M, dtype=torch.int32, device="cuda")
+    h_out = torch.zeros(G, M, dtype=torch.int32).pin_memory()
+    stream = torch.cuda.ExternalStream(model.stream())
+
+    def barrier():
+        torch.cuda.synchronize()
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if not pg:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, reps):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1)) / reps
+
+    reps = max(1, min(args.steps, 3))
+    for _ in range(max(1, args.warmup)):
+        dec.prefill(d_tok, T)
+    dec.generate(8, d_out, True)  # captures the decode-step graph
+    n0 = rnet.kernel_launches()
+    clocks = ClockSampler(local) if rank == 0 else ClockSampler(None)
+    clocks.start()
+    clocks.mark(True)
+    ms_prefill = timed(lambda: dec.prefill(d_tok, T), reps)
+    ms_decode = timed(lambda: dec.generate(G, d_out, True), 1)
+    clocks.mark(False)
+    ck = clocks.stop()
+    launches = rnet.kernel_launches() - n0
+
+    # end to end: prompt from pinned host memory, generated tokens back to host
+    def e2e():
+        d_tok.copy_(h_tok, non_blocking=True)
+        dec.prefill(d_tok, T)
+        dec.generate(G, d_out, True)
+        h_out.copy_(d_out, non_blocking=True)
+    ms_e2e = timed(e2e, 1)
+    if rank != 0:
+        if pg:
+            pg.destroy_process_group()
+        return
+    peaks = measured_peaks()
+    # one decode step streams every weight once and reads + writes each
+    # stream's state (14 conv rows + h per layer)
+    weight_bytes = 4.0 * model.num_params
+    state_bytes = 2 * 4.0 * M * CFG["n_layers"] * 15 * CFG["d_model"]
+    step_ms = ms_decode / G
+    achieved = (weight_bytes + state_bytes) / (step_ms * 1e-3) / 1e9
+    out = {
+        "metric": "decode tok/s (d512 L8, 256 streams x 1024 greedy steps after a 4096-token prefill)",
+        "value": round(args.streams * G / (ms_decode * 1e-3), 1), "unit": "tok/s",
+        "n_gpus": world, "steps": 1, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp32 (3xTF32 tcgen05)", "data": "synthetic Zipf(1.1) byte prompts, N(0,0.02) weights",
+        "config": {"workload": "config 4: prefill + greedy decode", "model": "ResonanceNet d512 L8",
+                   "streams": args.streams, "streams_per_gpu": M, "prompt": T, "decode_steps": G,
+                   "parallelism": f"streams sharded over {world} GPU(s), no collective"},
+        "prefill": {"value": round(args.streams * T / (ms_prefill * 1e-3), 1), "unit": "tok/s",
+                    "ms": round(ms_prefill, 3)},
+        "e2e": {"value": round(args.streams * G / (ms_e2e * 1e-3), 1), "unit": "generated tok/s",
+                "note": "prompt H2D + prefill + decode + tokens D2H",
+                "h2d_bytes_per_step": int(4 * M * T), "d2h_bytes_per_step": int(4 * M * G)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "kernel": "decode step (all kernels of one graph replay)",
+                     "achieved": round(achieved, 1), "peak": peaks["hbm"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm"], 4),
+                     "bytes_per_step": weight_bytes + state_bytes},
+        "clocks": ck,
+    }
+    print(json.dumps(out), flush=True)
+    if pg:
+        pg.destroy_process_group()
+
+
 def main():
     args = parse()
     rank, world, local = env_rank()
     if args.op:
         run_op(args)
+        return
+    if args.decode:
+        run_decode(args, rank, world, local)
         return
     if args.impl == "reference":
         run_reference(args, rank, world, local)

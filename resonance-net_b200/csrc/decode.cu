@@ -117,7 +117,83 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int M, int V,
   if (pos_ptr && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(pos_ptr, 1);
 }
 
+// h[r, f] = silu(gu[r, f]) * gu[r, F + f]  (gate | up rows of width 2F)
+__global__ void silu_mul_rows_kernel(const float* __restrict__ gu, float* __restrict__ h, int M,
+                                     int F) {
+  const size_t n = (size_t)M * F;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / F;
+    const int f = (int)(i - r * F);
+    const float g = gu[r * 2 * F + f];
+    h[i] = g / (1.0f + __expf(-g)) * gu[r * 2 * F + F + f];
+  }
+}
+
+// Top-2 of each score row by the reference's sequential rule (walk the slots
+// in order; a score strictly above the smaller held score replaces the first
+// such minimum), then softmax over the pair (src/slot_memory.cu:40-51). One
+// warp per row: lane l holds slots [32l, 32l+32) and the held pair is passed
+// from lane to lane, so the walk stays in slot order.
+__global__ void topk2_rows_kernel(const float* __restrict__ scores, int* __restrict__ idx,
+                                  float* __restrict__ w, int M, int S) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float* sr = scores + (size_t)row * S;
+  float h0 = -1e30f, h1 = -1e30f;
+  int i0 = 0, i1 = 0;
+  for (int base = 0; base < S; base += 32 * 32) {
+    float v[32];
+    const int s0 = base + lane * 32;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = s0 + j < S ? sr[s0 + j] : -3e38f;
+    for (int src = 0; src < 32; ++src) {
+      if (lane == src) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (s0 + j >= S) break;
+          const float x = v[j];
+          const bool m1 = h1 < h0;
+          const float hm = m1 ? h1 : h0;
+          if (x > hm) {
+            if (m1) { h1 = x; i1 = s0 + j; } else { h0 = x; i0 = s0 + j; }
+          }
+        }
+      }
+      h0 = __shfl_sync(0xffffffffu, h0, src);
+      h1 = __shfl_sync(0xffffffffu, h1, src);
+      i0 = __shfl_sync(0xffffffffu, i0, src);
+      i1 = __shfl_sync(0xffffffffu, i1, src);
+    }
+  }
+  if (lane == 0) {
+    const float mx = fmaxf(h0, h1);
+    const float e0 = __expf(h0 - mx), e1 = __expf(h1 - mx);
+    const float sum = e0 + e1;
+    idx[2 * (size_t)row] = i0;
+    idx[2 * (size_t)row + 1] = i1;
+    w[2 * (size_t)row] = e0 / sum;
+    w[2 * (size_t)row + 1] = e1 / sum;
+  }
+}
+
 }  // namespace
+
+cudaError_t silu_mul_rows(const float* gu, float* h, int M, int F, cudaStream_t s) {
+  if (M <= 0 || F <= 0) return cudaSuccess;
+  const size_t n = (size_t)M * F;
+  size_t grid = (n + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  silu_mul_rows_kernel<<<(unsigned)grid, 256, 0, s>>>(gu, h, M, F);
+  return launched();
+}
+
+cudaError_t topk2_rows(const float* scores, int* idx, float* w, int M, int S, cudaStream_t s) {
+  if (M <= 0) return cudaSuccess;
+  topk2_rows_kernel<<<(M + 7) / 8, 256, 0, s>>>(scores, idx, w, M, S);
+  return launched();
+}
 
 cudaError_t decode_conv(const float* n, float* ring, const int* pos, const float* w3,
                         const float* w7, const float* w15, float* S, int M, int D,

@@ -5,6 +5,7 @@
 // (backward), :551-697 (step, zero_grad), :743-824 (checkpoint).
 #include <cmath>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <random>
 #include <string>
@@ -547,6 +548,7 @@ int Engine::decoder_init(Decoder* d, int M) {
   f(&d->state, L * d->floats_per_layer);
   f(&d->x, m * D); f(&d->n, m * D); f(&d->S, m * D); f(&d->P, 2 * m * D); f(&d->q, m * D);
   f(&d->r, m * D); f(&d->G, m * F); f(&d->U, m * F); f(&d->H, m * F); f(&d->logits, m * V);
+  f(&d->GU, m * 2 * F); f(&d->scores, m * (size_t)cfg_.n_slots);
   f(&d->w, m * k);
   plan.push_back({(void**)&d->idx, m * k * sizeof(int)});
   plan.push_back({(void**)&d->tok, m * sizeof(int)});
@@ -555,6 +557,10 @@ int Engine::decoder_init(Decoder* d, int M) {
   for (auto& e : plan) total += (e.second + 255) & ~size_t(255);
   CK(cudaMalloc(&d->arena, total));
   CK(cudaMemsetAsync(d->arena, 0, total, stream_));
+  // split-K workspace of the decode step's short-M GEMMs (the step is
+  // captured into a graph, which cannot allocate). splits <= SMs / tiles and a
+  // tile covers 128 x 128 outputs, so splits * M * N <= SMs * 128 * 128.
+  CK(rnet_gemm::reserve_workspace(stream_, (size_t)rnet_gemm::num_sms() * 128 * 128));
   char* p = (char*)d->arena;
   for (auto& e : plan) {
     *e.first = p;
@@ -621,25 +627,16 @@ int Engine::decode_step(Decoder* d, const int* d_tokens) {
     CK(rnet_k::decode_gru(d->P, w.bz, w.bh, h, d->x, M, D, s));
     CK(rnet_k::rms_norm_fwd(d->x, w.n3, d->n, nullptr, M, D, eps, s));
     MM(M, D, D, kmaj(d->n, D), kmaj(w.pq, D), epi_store(d->q, D), 0);
-    {
-      Epilogue e;
-      e.kind = EPI_TOP2;
-      e.topk_idx = d->idx;
-      e.topk_w = d->w;
-      MM(M, S, D, kmaj(d->q, D), kmaj(KT_ + (size_t)l * S * D, D), e, 0);
-    }
+    // short M: scores through the split-K GEMM, then a warp-per-row top-2
+    // (the row-owner top-2 epilogue would run on M / 128 CTAs)
+    MM(M, S, D, kmaj(d->q, D), kmaj(KT_ + (size_t)l * S * D, D), epi_store(d->scores, S), 0);
+    CK(rnet_k::topk2_rows(d->scores, d->idx, d->w, M, S, s));
     CK(rnet_k::slot_gather(d->idx, d->w, VT_ + (size_t)l * S * D, d->r, M, D, S, 2, err, s));
     MM_RES(M, D, D, kmaj(d->r, D), kmaj(w.pout, D), d->x);
     CK(rnet_k::rms_norm_fwd(d->x, w.n4, d->n, nullptr, M, D, eps, s));
-    {
-      Epilogue e;
-      e.kind = EPI_SWIGLU_FWD;
-      e.G = d->G;
-      e.U = d->U;
-      e.H = d->H;
-      e.ldf = F;
-      MM(M, F, D, kmaj(d->n, D), kmaj(w.gate, D), e, F);
-    }
+    // gate|up as one [2F, D] operand (adjacent in the parameter buffer)
+    MM(M, 2 * F, D, kmaj(d->n, D), kmaj(w.gate, D), epi_store(d->GU, 2 * F), 0);
+    CK(rnet_k::silu_mul_rows(d->GU, d->H, M, F, s));
     MM_RES(M, D, F, kmaj(d->H, F), kmaj(w.down, F), d->x);
   }
   CK(rnet_k::rms_norm_fwd(d->x, fnorm_, d->n, nullptr, M, D, eps, s));

@@ -70,6 +70,7 @@ struct Decoder {
   float* state = nullptr;  // per layer: ring [M][14][D] then h [M][D]
   size_t floats_per_layer = 0;
   float *x, *n, *S, *P, *q, *r, *G, *U, *H, *logits;
+  float *GU, *scores;  // [M, 2F] gate|up pre-activations, [M, S] slot scores
   int* idx;
   float* w;
   int* tok;  // current / next token per stream

@@ -53,6 +53,11 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
 // Number of SMs of the current device (cached).
 int num_sms();
 
+// Grow the split-K workspace of `stream` on the current device to at least
+// `floats` (call before capturing short-M GEMMs into a CUDA graph; calls made
+// while capturing never allocate and run unsplit when the workspace is short).
+cudaError_t reserve_workspace(cudaStream_t stream, size_t floats);
+
 // Reason of the last failed gemm_tf32x3 call on this thread ("" if none).
 const char* gemm_last_reason();
 

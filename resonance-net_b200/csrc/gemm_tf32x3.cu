@@ -28,6 +28,8 @@
 #include <cudaTypedefs.h>
 #include <cstdio>
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "gemm.cuh"
@@ -54,6 +56,9 @@ struct KParams {
   int row_owner;   // 1: a unit is one m-tile swept over all n-tiles
   int b_pair_off;  // rows
   int a_mn, b_mn;
+  // split-K into a workspace: split ks stores its partial at epi.C + ks *
+  // split_stride (0: no workspace split)
+  long long split_stride;
   Epilogue epi;
   unsigned* err;
 };
@@ -157,8 +162,9 @@ __device__ __forceinline__ void tile_out(float* st, const float (&v)[32], float*
 // this beats staging through shared memory, which competes with the
 // operand pipeline for shared-memory bandwidth.
 __device__ __forceinline__ void store_row_chunk(const KParams& p, int kind, int row, int col0,
-                                                const float (&v)[32]) {
-  const Epilogue& e = p.epi;
+                                                const float (&v)[32], size_t c_off = 0) {
+  Epilogue e = p.epi;
+  e.C += c_off;
   if (row >= p.M) return;
   const float a = e.alpha;
   if (col0 + 32 <= p.N) {
@@ -221,7 +227,7 @@ struct Top2State {
 template <int BN>
 __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc, int row0,
                                                  int nt, bool last_sub, Top2State& st,
-                                                 float* tile) {
+                                                 float* tile, size_t c_off) {
   const Epilogue& e = p.epi;
   const int lane = threadIdx.x & 31;
   const int row = row0 + lane;
@@ -281,7 +287,7 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
   for (int c = 0; c < BN / 32; ++c) {
     if (resid && c + 1 < BN / 32 && nt * BN + (c + 1) * 32 < p.N) prefetch_l1(rrow + (c + 1) * 32);
     tmem_ld_32cols(tacc + c * 32, v);
-    store_row_chunk(p, e.kind, row, nt * BN + c * 32, v);
+    store_row_chunk(p, e.kind, row, nt * BN + c * 32, v, c_off);
   }
 }
 
@@ -529,8 +535,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!mbar_wait(&accf[ab], tph, p.err, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN;
+        const size_t c_off =
+            p.split_stride ? (size_t)p.split_stride * (size_t)(kb0 / p.kb_per_split) : 0;
         epilogue_subtile<BN>(p, tacc, row0, nt, nt == nt1 - 1, st,
-                             epi_tiles + q * EPI_TILE_FLOATS);
+                             epi_tiles + q * EPI_TILE_FLOATS, c_off);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -653,6 +661,89 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
   return rnet_k::launched();
 }
 
+// ------------------------------------------------------------------ split-K workspace
+// Short-M GEMMs (decode steps, small batches) have too few output tiles to
+// fill the GPU. Their K range is split over extra CTAs that store partial
+// tiles into a workspace; splitk_reduce sums the partials in split order (so
+// results do not depend on scheduling) and applies the epilogue.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int S, int M, int N,
+                                     Epilogue e) {
+  const size_t plane = (size_t)M * N;
+  if ((N & 3) == 0) {
+    const int N4 = N >> 2;
+    const size_t n4 = (size_t)M * N4;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+         i += (size_t)gridDim.x * blockDim.x) {
+      const size_t r = i / N4;
+      const int c = (int)(i - r * N4) * 4;
+      const float* src = ws + r * N + c;
+      float4 a = *reinterpret_cast<const float4*>(src);
+      for (int k = 1; k < S; ++k) {
+        const float4 b = *reinterpret_cast<const float4*>(src + k * plane);
+        a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+      }
+      float* dst = e.C + r * e.ldc + c;
+      const float al = e.alpha;
+      float4 o = make_float4(al * a.x, al * a.y, al * a.z, al * a.w);
+      if (e.kind == EPI_ACCUM || e.kind == EPI_RESID) {
+        const float* base = e.kind == EPI_ACCUM ? dst : e.R + r * e.ldr + c;
+        o.x += base[0]; o.y += base[1]; o.z += base[2]; o.w += base[3];
+      }
+      dst[0] = o.x; dst[1] = o.y; dst[2] = o.z; dst[3] = o.w;
+    }
+  } else {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < plane;
+         i += (size_t)gridDim.x * blockDim.x) {
+      const size_t r = i / N;
+      const int c = (int)(i - r * N);
+      float a = ws[i];
+      for (int k = 1; k < S; ++k) a += ws[i + k * plane];
+      float* dst = e.C + r * e.ldc + c;
+      float o = e.alpha * a;
+      if (e.kind == EPI_ACCUM) o += *dst;
+      if (e.kind == EPI_RESID) o += e.R[r * e.ldr + c];
+      *dst = o;
+    }
+  }
+}
+
+struct Workspace {
+  float* p = nullptr;
+  size_t floats = 0;
+};
+static std::mutex g_ws_mu;
+// one workspace per (device, stream): GEMMs on one stream are ordered
+static std::vector<std::pair<std::pair<int, cudaStream_t>, Workspace>> g_ws;
+
+static Workspace* workspace_for(cudaStream_t s) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  for (auto& e : g_ws)
+    if (e.first.first == dev && e.first.second == s) return &e.second;
+  g_ws.push_back({{dev, s}, Workspace{}});
+  return &g_ws.back().second;
+}
+
+cudaError_t reserve_workspace(cudaStream_t stream, size_t floats) {
+  Workspace* w = workspace_for(stream);
+  if (w->floats >= floats) return cudaSuccess;
+  if (w->p) {
+    cudaError_t e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return e;
+    cudaFree(w->p);
+    w->p = nullptr;
+    w->floats = 0;
+  }
+  cudaError_t e = cudaMalloc(&w->p, floats * sizeof(float));
+  if (e != cudaSuccess) {
+    w->p = nullptr;
+    return e;
+  }
+  w->floats = floats;
+  return cudaSuccess;
+}
+
 cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand& A,
                         const Operand& B, const Epilogue& epi, int b_pair_off, int k_splits,
                         unsigned* err_word) {
@@ -664,17 +755,37 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
     return reject("operand ld not a multiple of 4 or operand not 16-byte aligned");
   const bool paired = b_pair_off > 0;
   const bool row_owner = epi.kind == EPI_TOP2;
+  constexpr int BK = 16;
+  // Short M: split K over a workspace when the output tiles cannot fill the
+  // SMs (store / residual epilogues, and accumulation asked for in one pass).
+  int ws_splits = 1;
+  if (!paired && !row_owner && g_force_cg == 0 && M <= 1024 &&
+      (epi.kind == EPI_STORE || epi.kind == EPI_RESID ||
+       (epi.kind == EPI_ACCUM && k_splits == 1))) {
+    const int tiles = ((M + BM - 1) / BM) * ((N + 127) / 128);
+    const int kb = (K + BK - 1) / BK;
+    int sp = num_sms() / tiles;
+    if (sp > kb / 2) sp = kb / 2;  // >= 2 k-blocks per split
+    if (sp > 32) sp = 32;
+    if (sp >= 2) {
+      const size_t need = (size_t)sp * M * N;
+      Workspace* w = workspace_for(stream);
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      cudaStreamIsCapturing(stream, &cs);
+      if (w->floats < need && cs == cudaStreamCaptureStatusNone)
+        reserve_workspace(stream, need);  // on failure: no split
+      if (w->floats >= need) ws_splits = sp;
+    }
+  }
   // CTA pairs (one 256-row MMA over two SMs, each staging half of B) cut
   // shared-memory and L2->SM traffic per FLOP by a third; single CTAs are kept
   // for short M, where pairs would leave SMs idle.
-  const int CG = g_force_cg > 0 ? g_force_cg : (M > BM ? 2 : 1);
+  const int CG = g_force_cg > 0 ? g_force_cg : (M > BM && ws_splits == 1 ? 2 : 1);
   // CG = 1: paired-B and row-owner epilogues use 128-wide tiles (64-feature
   // halves). CG = 2: 256-wide tiles (each CTA stages one 128-row half).
+  // (16-deep K-blocks, 4-6 stages, measured 5-20% faster than 32-deep.)
   const int BN = CG == 2 ? (N <= 128 && !paired ? 128 : 256)
-                         : ((paired || row_owner || N <= 128) ? 128 : 256);
-  // 16-deep K-blocks (4-6 stages) measured 5-20% faster than 32-deep (2-3
-  // stages) on every step shape.
-  constexpr int BK = 16;
+                         : ((paired || row_owner || N <= 128 || ws_splits > 1) ? 128 : 256);
   const int n_logical_tile = paired ? BN / 2 : BN;
 
   KParams kp{};
@@ -692,7 +803,15 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   kp.err = err_word;
 
   int splits = 1;
-  if (epi.kind == EPI_ACCUM) {
+  if (ws_splits > 1) {
+    splits = ws_splits;
+    Epilogue part;  // partial tiles: plain stores into the workspace
+    part.kind = EPI_STORE;
+    part.C = workspace_for(stream)->p;
+    part.ldc = N;
+    kp.epi = part;
+    kp.split_stride = (long long)M * N;
+  } else if (epi.kind == EPI_ACCUM) {
     if (k_splits > 0) {
       splits = k_splits;
     } else {
@@ -730,12 +849,18 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   if (!map_a(&ta, A.p)) return reject("tensor map of A rejected");
   if (!map_b(&tb, B.p)) return reject("tensor map of B rejected");
 
-  if (CG == 2) {
-    if (BN == 128) return launch<128, BK, 2>(stream, ta, tb, kp);
-    return launch<256, BK, 2>(stream, ta, tb, kp);
-  }
-  if (BN == 128) return launch<128, BK, 1>(stream, ta, tb, kp);
-  return launch<256, BK, 1>(stream, ta, tb, kp);
+  cudaError_t e;
+  if (CG == 2)
+    e = BN == 128 ? launch<128, BK, 2>(stream, ta, tb, kp) : launch<256, BK, 2>(stream, ta, tb, kp);
+  else
+    e = BN == 128 ? launch<128, BK, 1>(stream, ta, tb, kp) : launch<256, BK, 1>(stream, ta, tb, kp);
+  if (e != cudaSuccess || kp.split_stride == 0) return e;
+  // fixed-order sum of the partials + the caller's epilogue
+  const size_t work = (N % 4 == 0) ? (size_t)M * N / 4 : (size_t)M * N;
+  size_t grid = (work + 255) / 256;
+  if (grid > (size_t)num_sms() * 8) grid = (size_t)num_sms() * 8;
+  splitk_reduce_kernel<<<(unsigned)grid, 256, 0, stream>>>(kp.epi.C, kp.k_splits, M, N, epi);
+  return rnet_k::launched();
 }
 
 }  // namespace rnet_gemm

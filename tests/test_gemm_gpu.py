@@ -4,7 +4,8 @@ through the C ABI (rnet_gemm_f32): all four operand majors, ragged shapes
 epilogues, and long K (weight-gradient shape).
 
 Every case runs on both tile shapes of the engine: single-CTA 128-row tiles
-(cta_group 1) and CTA-pair 256-row tiles over two SMs (cta_group 2).
+(cta_group 1) and CTA-pair 256-row tiles over two SMs (cta_group 2), and with
+the automatic choice, which splits K over a workspace for short M.
 
 Tolerance: max |err| / max |ref| <= 2e-5 (fp32-class; plain TF32 would give
 ~1e-3), tighter than the 1e-4 the layer parity tests use.
@@ -18,7 +19,7 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-5
 
 
-@pytest.fixture(params=[1, 2], ids=["cg1", "cg2"])
+@pytest.fixture(params=[0, 1, 2], ids=["auto", "cg1", "cg2"])
 def cta_group(request, rnet):
     rnet.call("rnet_gemm_set_cta_group", request.param)
     yield request.param
