@@ -610,7 +610,11 @@ def run_decode(args, rank, world, local):
     weight_bytes = 4.0 * model.num_params
     state_bytes = 2 * 4.0 * M * CFG["n_layers"] * 15 * CFG["d_model"]
     step_ms = ms_decode / G
-    achieved = (weight_bytes + state_bytes) / (step_ms * 1e-3) / 1e9
+    hbm_gbs = (weight_bytes + state_bytes) / (step_ms * 1e-3) / 1e9
+    # forward FLOPs per token: 10 D^2 + 2 D S + 6 D F per layer + 2 D V (head)
+    D_, F_, S_, V_ = CFG["d_model"], CFG["d_ff"], CFG["n_slots"], CFG["vocab"]
+    flops_tok = CFG["n_layers"] * (10 * D_ * D_ + 2 * D_ * S_ + 6 * D_ * F_) + 2 * D_ * V_
+    tflops = M * flops_tok / (step_ms * 1e-3) / 1e12
     out = {
         "metric": "decode tok/s (d512 L8, 256 streams x 1024 greedy steps after a 4096-token prefill)",
         "value": round(args.streams * G / (ms_decode * 1e-3), 1), "unit": "tok/s",
@@ -626,10 +630,16 @@ def run_decode(args, rank, world, local):
                 "note": "prompt H2D + prefill + decode + tokens D2H",
                 "h2d_bytes_per_step": int(4 * M * T), "d2h_bytes_per_step": int(4 * M * G)},
         "gpu_launches": int(launches),
-        "roofline": {"bound": "hbm", "kernel": "decode step (all kernels of one graph replay)",
-                     "achieved": round(achieved, 1), "peak": peaks["hbm"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm"], 4),
-                     "bytes_per_step": weight_bytes + state_bytes},
+        # at 256 streams a step is compute-bound in fp32 (3xTF32 ceiling =
+        # bf16 peak / 6); the weight + state stream is reported beside it
+        "roofline": {"bound": "tensor", "kernel": "decode step (all kernels of one graph replay)",
+                     "achieved": round(tflops, 2), "peak": peaks["bf16"], "unit": "TFLOP/s",
+                     "frac": round(tflops / peaks["bf16"], 4),
+                     "ceiling_3xtf32": round(peaks["bf16"] / 6, 1),
+                     "frac_of_3xtf32_ceiling": round(tflops / (peaks["bf16"] / 6), 4),
+                     "flops_per_step": M * flops_tok,
+                     "hbm": {"achieved_GBps": round(hbm_gbs, 1), "frac": round(hbm_gbs / peaks["hbm"], 4),
+                             "bytes_per_step": weight_bytes + state_bytes}},
         "clocks": ck,
     }
     print(json.dumps(out), flush=True)

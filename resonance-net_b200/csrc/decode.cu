@@ -132,27 +132,69 @@ __global__ void silu_mul_rows_kernel(const float* __restrict__ gu, float* __rest
 
 // Top-2 of each score row by the reference's sequential rule (walk the slots
 // in order; a score strictly above the smaller held score replaces the first
-// such minimum), then softmax over the pair (src/slot_memory.cu:40-51). One
-// warp per row: lane l holds slots [32l, 32l+32) and the held pair is passed
-// from lane to lane, so the walk stays in slot order.
+// such minimum), then softmax over the pair (src/slot_memory.cu:40-51).
+// The held pair always holds the two largest scores seen so far, so slot i
+// changes the state only if its score exceeds the second largest of slots
+// [0, i). One warp per row, lane l owning slots [32l, 32l+32): a warp scan of
+// (largest, second largest) gives every lane the values held when its chunk
+// starts; each lane flags the slots that would enter; only those are then
+// replayed in slot order, the held pair (with positions) passed lane to lane.
+__device__ __forceinline__ void top2_merge(float& a1, float& a2, float b1, float b2) {
+  // multiset top-2 of {a1, a2, b1, b2} (a1 >= a2, b1 >= b2)
+  const float m1 = fmaxf(a1, b1);
+  const float m2 = fmaxf(fminf(a1, b1), fmaxf(a2, b2));
+  a1 = m1;
+  a2 = m2;
+}
+
 __global__ void topk2_rows_kernel(const float* __restrict__ scores, int* __restrict__ idx,
                                   float* __restrict__ w, int M, int S) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
   const float* sr = scores + (size_t)row * S;
-  float h0 = -1e30f, h1 = -1e30f;
+  const float NEG = -1e30f;  // the reference's initial held value
+  float h0 = NEG, h1 = NEG;  // held pair (positions 0, 1), uniform across the warp
   int i0 = 0, i1 = 0;
   for (int base = 0; base < S; base += 32 * 32) {
-    float v[32];
     const int s0 = base + lane * 32;
+    float v[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = s0 + j < S ? sr[s0 + j] : -3e38f;
-    for (int src = 0; src < 32; ++src) {
+    for (int j = 0; j < 32; ++j) v[j] = s0 + j < S ? sr[s0 + j] : NEG;
+    // chunk top-2 (values)
+    float c1 = NEG, c2 = NEG;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) top2_merge(c1, c2, v[j], NEG);
+    // inclusive warp scan, then the values held when this lane's chunk starts
+    float p1 = c1, p2 = c2;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float q1 = __shfl_up_sync(0xffffffffu, p1, o);
+      const float q2 = __shfl_up_sync(0xffffffffu, p2, o);
+      if (lane >= o) top2_merge(p1, p2, q1, q2);
+    }
+    float e1 = __shfl_up_sync(0xffffffffu, p1, 1), e2 = __shfl_up_sync(0xffffffffu, p2, 1);
+    if (lane == 0) { e1 = NEG; e2 = NEG; }
+    top2_merge(e1, e2, fmaxf(h0, h1), fminf(h0, h1));  // state carried from earlier blocks
+    // flag the slots that enter: strictly above the running second largest
+    unsigned flags = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (s0 + j < S && v[j] > e2) {
+        flags |= 1u << j;
+        top2_merge(e1, e2, v[j], NEG);
+      }
+    }
+    // replay the flagged slots in order with positions, lane by lane
+    unsigned busy = __ballot_sync(0xffffffffu, flags != 0);
+    while (busy) {
+      const int src = __ffs(busy) - 1;
+      busy &= busy - 1;
       if (lane == src) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (s0 + j >= S) break;
+        unsigned f = flags;
+        while (f) {
+          const int j = __ffs(f) - 1;
+          f &= f - 1;
           const float x = v[j];
           const bool m1 = h1 < h0;
           const float hm = m1 ? h1 : h0;

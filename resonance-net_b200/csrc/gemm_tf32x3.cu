@@ -666,8 +666,8 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
 // fill the GPU. Their K range is split over extra CTAs that store partial
 // tiles into a workspace; splitk_reduce sums the partials in split order (so
 // results do not depend on scheduling) and applies the epilogue.
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int S, int M, int N,
-                                     Epilogue e) {
+__global__ void __launch_bounds__(256)
+    splitk_reduce_kernel(const float* __restrict__ ws, int S, int M, int N, Epilogue e) {
   const size_t plane = (size_t)M * N;
   if ((N & 3) == 0) {
     const int N4 = N >> 2;
@@ -678,9 +678,15 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int S, int M,
       const int c = (int)(i - r * N4) * 4;
       const float* src = ws + r * N + c;
       float4 a = *reinterpret_cast<const float4*>(src);
-      for (int k = 1; k < S; ++k) {
-        const float4 b = *reinterpret_cast<const float4*>(src + k * plane);
-        a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+      // loads in batches of 8 (independent), additions in split order
+      for (int k0 = 1; k0 < S; k0 += 8) {
+        float4 b[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (k0 + j < S) b[j] = *reinterpret_cast<const float4*>(src + (k0 + j) * plane);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (k0 + j < S) { a.x += b[j].x; a.y += b[j].y; a.z += b[j].z; a.w += b[j].w; }
       }
       float* dst = e.C + r * e.ldc + c;
       const float al = e.alpha;
