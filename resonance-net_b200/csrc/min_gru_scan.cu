@@ -28,7 +28,6 @@ constexpr int SEG = W * CL;
 constexpr int CW = 32;  // channels per CTA
 constexpr int TILE = SEG * CW;  // floats per staged tile
 
-__device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + __expf(-v)); }
 
 __device__ __forceinline__ void cp_async16(float* smem, const float* gmem, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)),
@@ -52,16 +51,51 @@ __device__ __forceinline__ void stage(float* tile, const float* src, int ld, int
   }
 }
 
+// Output set of the forward scan (compile-time, so the step loops carry no
+// per-step tests): DIFF: `ho` receives e = h~ - h_prev instead of h; Y: y = h;
+// OUT: out = res + h; OUT2: a second copy of out.
+enum : int { F_DIFF = 1, F_Y = 2, F_OUT = 4, F_OUT2 = 8 };
+
+// Pass 2 of one warp's chunk: re-run the chunk from its exact carry-in and
+// write the outputs. FULL: every step of the chunk is inside [0, T).
+template <int FL, bool FULL>
+__device__ __forceinline__ float scan_fwd_emit(const float* sZ, const float* sT, const float* sR,
+                                               int r0, int lane, float h, int n, size_t o0, int D,
+                                               float* zo, float* ho, float* yo, float* out,
+                                               float* out2) {
+  size_t o = o0;
+#pragma unroll 8
+  for (int i = 0; i < CL; ++i) {
+    if (!FULL && i >= n) break;
+    const int row = r0 + i;
+    const float z = sZ[row * CW + lane];
+    const float ht = sT[row * CW + lane];
+    const float hp = h;
+    h = (1.f - z) * h + z * ht;
+    zo[o] = z;
+    ho[o] = (FL & F_DIFF) ? ht - hp : h;
+    if (FL & F_Y) yo[o] = h;
+    if (FL & F_OUT) {
+      const float r = sR[row * CW + lane] + h;
+      out[o] = r;
+      if (FL & F_OUT2) out2[o] = r;
+    }
+    o += D;
+  }
+  return h;
+}
+
+template <int FL>
 __global__ void __launch_bounds__(W * 32)
     scan_fwd_kernel(const float* __restrict__ pz, const float* __restrict__ ph, int ldp,
                     const float* __restrict__ bz, const float* __restrict__ bh,
                     float* __restrict__ zo, float* __restrict__ ho, float* __restrict__ yo,
                     const float* __restrict__ res, float* __restrict__ out,
-                    float* __restrict__ out2, int T, int D, int diff) {
+                    float* __restrict__ out2, int T, int D) {
   extern __shared__ float smem[];
   float* sZ = smem;             // pz, then z
   float* sT = smem + TILE;      // ph, then h~
-  float* sR = smem + 2 * TILE;  // residual input (only when out != null)
+  float* sR = smem + 2 * TILE;  // residual input (OUT only)
   __shared__ float sA[W][32], sH[W][32];
   __shared__ float carry[32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -75,17 +109,19 @@ __global__ void __launch_bounds__(W * 32)
   for (int seg0 = 0; seg0 < T; seg0 += SEG) {
     stage(sZ, pz, ldp, b, T, D, seg0, c0);
     stage(sT, ph, ldp, b, T, D, seg0, c0);
-    if (out) stage(sR, res, D, b, T, D, seg0, c0);
+    if (FL & F_OUT) stage(sR, res, D, b, T, D, seg0, c0);
     cp_async_wait_all();
     __syncthreads();
     const int r0 = warp * CL;
+    const int n = T - (seg0 + r0) < CL ? T - (seg0 + r0) : CL;  // live steps of the chunk
     float A = 1.f, H = 0.f;
 #pragma unroll 8
     for (int i = 0; i < CL; ++i) {
       const int row = r0 + i;
-      const bool live = act && seg0 + row < T;
-      // steps past T are identity steps (z = 0: h unchanged)
-      const float z = live ? sigmoidf_(sZ[row * CW + lane] + bzd) : 0.f;
+      const bool live = act && i < n;
+      // steps past T (and lanes past D) are identity steps (z = 0: h unchanged);
+      // z = 1 / (1 + exp(-(pz + bz))) with the fast divide (a few ulp)
+      const float z = live ? __fdividef(1.0f, 1.0f + __expf(-(sZ[row * CW + lane] + bzd))) : 0.f;
       const float ht = live ? sT[row * CW + lane] + bhd : 0.f;
       sZ[row * CW + lane] = z;
       sT[row * CW + lane] = ht;
@@ -98,25 +134,12 @@ __global__ void __launch_bounds__(W * 32)
     __syncthreads();
     float h = carry[lane];
     for (int j = 0; j < warp; ++j) h = sA[j][lane] * h + sH[j][lane];
-#pragma unroll 8
-    for (int i = 0; i < CL; ++i) {
-      const int row = r0 + i;
-      const int t = seg0 + row;
-      const float z = sZ[row * CW + lane];
-      const float ht = sT[row * CW + lane];
-      const float hp = h;
-      h = (1.f - z) * h + z * ht;
-      if (act && t < T) {
-        const size_t o = ((size_t)b * T + t) * D + d;
-        zo[o] = z;
-        ho[o] = diff ? ht - hp : h;
-        if (yo) yo[o] = h;
-        if (out) {
-          const float r = sR[row * CW + lane] + h;
-          out[o] = r;
-          if (out2) out2[o] = r;
-        }
-      }
+    if (act && n > 0) {
+      const size_t o0 = ((size_t)b * T + seg0 + r0) * D + d;
+      if (n == CL)
+        h = scan_fwd_emit<FL, true>(sZ, sT, sR, r0, lane, h, n, o0, D, zo, ho, yo, out, out2);
+      else
+        h = scan_fwd_emit<FL, false>(sZ, sT, sR, r0, lane, h, n, o0, D, zo, ho, yo, out, out2);
     }
     __syncthreads();
     if (warp == W - 1) carry[lane] = h;
@@ -222,17 +245,41 @@ void allow_smem(K kernel, size_t bytes) {
 
 }  // namespace
 
+template <int FL>
+void launch_fwd(int grid, size_t smem, cudaStream_t s, const float* pz, const float* ph, int ldp,
+                const float* bz, const float* bh, float* z, float* h, float* y, const float* res,
+                float* out, float* out2, int T, int D) {
+  static bool done = false;
+  if (!done) {
+    cudaFuncSetAttribute(scan_fwd_kernel<FL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)(3 * TILE * sizeof(float)));
+    done = true;
+  }
+  scan_fwd_kernel<FL><<<grid, W * 32, smem, s>>>(pz, ph, ldp, bz, bh, z, h, y, res, out, out2, T,
+                                                 D);
+}
+
 cudaError_t gru_scan_fwd(const float* pz, const float* ph, int ldp, const float* bz,
                          const float* bh, float* z, float* h, float* y, const float* res,
                          float* out, int B, int T, int D, cudaStream_t s, bool h_as_diff,
                          float* out2) {
   if (B <= 0 || T <= 0) return cudaSuccess;
   if (D % 4 || ldp % 4) return cudaErrorInvalidValue;
+  if (out2 && !out) return cudaErrorInvalidValue;
   const size_t smem = (size_t)(out ? 3 : 2) * TILE * sizeof(float);
-  allow_smem(scan_fwd_kernel, 3 * TILE * sizeof(float));
   const int grid = B * ((D + CW - 1) / CW);
-  scan_fwd_kernel<<<grid, W * 32, smem, s>>>(pz, ph, ldp, bz, bh, z, h, y, res, out, out2, T, D,
-                                             h_as_diff ? 1 : 0);
+  const int fl = (h_as_diff ? F_DIFF : 0) | (y ? F_Y : 0) | (out ? F_OUT : 0) | (out2 ? F_OUT2 : 0);
+#define RNET_SCAN_CASE(F)                                                                 \
+  case F:                                                                                 \
+    launch_fwd<F>(grid, smem, s, pz, ph, ldp, bz, bh, z, h, y, res, out, out2, T, D);     \
+    break;
+  switch (fl) {
+    RNET_SCAN_CASE(0) RNET_SCAN_CASE(1) RNET_SCAN_CASE(2) RNET_SCAN_CASE(3)
+    RNET_SCAN_CASE(4) RNET_SCAN_CASE(5) RNET_SCAN_CASE(6) RNET_SCAN_CASE(7)
+    RNET_SCAN_CASE(12) RNET_SCAN_CASE(13) RNET_SCAN_CASE(14) RNET_SCAN_CASE(15)
+    default: return cudaErrorInvalidValue;
+  }
+#undef RNET_SCAN_CASE
   return launched();
 }
 
