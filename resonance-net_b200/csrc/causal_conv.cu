@@ -7,13 +7,16 @@
 // Layout: a persistent CTA owns 32 channels (lane = channel) and walks the
 // 128-step tiles of the sequences. A tile plus its 14-step halo ([142 rows x
 // 32 channels]) is copied global -> shared with cp.async (16 B per copy), three
-// tiles in flight per CTA; warp w runs steps [16w, 16w+16) of a tile from shared memory
-// with a 30-sample register window and writes each output row (128 B per
-// warp) coalesced. The weight gradient is a deterministic two-level
+// tiles in flight per CTA; warp w runs steps [16w, 16w+16) of a tile from
+// shared memory with a 30-sample register window and writes each output row
+// (128 B per warp) coalesced. The weight gradient is a deterministic two-level
 // reduction: warps of a CTA in fixed order, then CTA partials in fixed order.
+// Taps are merged by lag (see fwd_steps_merged / conv_bwd_kernel): fp32 sums
+// in a different association than the reference's per-scale sums.
 //
-// Per-scale accumulation order matches the reference (sum += x*w over taps in
-// increasing k, zero left padding), and S = (c3 + c7) + c15 as its sum3.
+// The C-ABI forward (which returns c7 and c15) sums per scale in the
+// reference's order (sum += x*w over taps in increasing k, zero left padding;
+// S = (c3 + c7) + c15 as its sum3); the model path merges taps by lag.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -30,7 +33,8 @@ constexpr int TS = NW * STEPS;       // steps per tile
 constexpr int ROWS = TS + HALO;      // staged rows per tile
 constexpr int WIN = STEPS + HALO;    // register window per warp
 constexpr int MAX_PARTS = 64;        // weight-gradient partials per channel group
-constexpr int PIPE = 3;              // tiles in flight per CTA (cp.async groups)
+constexpr int PIPE = 3;              // forward: tiles in flight per CTA (cp.async groups)
+constexpr int PIPE_B = 2;            // backward: {x, dS} tile pairs in flight per CTA
 
 __device__ __forceinline__ void cp_async16(float* smem, const float* gmem, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)),
@@ -89,6 +93,32 @@ __device__ __forceinline__ void fwd_steps(const float (&win)[WIN], const float (
   }
 }
 
+// Model-path outputs (S, optionally Sq) with the taps merged by lag: tap k of
+// kernel K reads x[t - l] with l = K-1-k, so c7 + c15 = sum_l u[l] x[t - l],
+// u[l] = w15[14-l] + w7[6-l] (l <= 6): 15 multiply-adds instead of 22; then
+// S = c3 + u and Sq = S + u (= S + c7 + c15). Window row j = x[t0 + r0 - 14 + j].
+template <bool WQ, bool FULL>
+__device__ __forceinline__ void fwd_steps_merged(const float (&win)[WIN], const float (&b3)[3],
+                                                 const float (&u)[15], float* pS, float* pQ,
+                                                 int n, int D) {
+#pragma unroll
+  for (int i = 0; i < STEPS; ++i) {
+    if (!FULL && i >= n) break;
+    float s3 = 0.f, su = 0.f;
+#pragma unroll
+    for (int l = 2; l >= 0; --l) s3 += win[i + HALO - l] * b3[l];
+#pragma unroll
+    for (int l = 14; l >= 0; --l) su += win[i + HALO - l] * u[l];
+    const float sum = s3 + su;
+    *pS = sum;
+    pS += D;
+    if (WQ) {
+      *pQ = sum + su;
+      pQ += D;
+    }
+  }
+}
+
 template <bool WQ, bool WC>
 __global__ void __launch_bounds__(NW * 32, 3)
     conv_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w3,
@@ -111,6 +141,11 @@ __global__ void __launch_bounds__(NW * 32, 3)
   for (int k = 0; k < 7; ++k) a7[k] = act ? w7[k * D + d] : 0.f;
 #pragma unroll
   for (int k = 0; k < 15; ++k) a15[k] = act ? w15[k * D + d] : 0.f;
+  float b3[3], u[15];  // per-lag taps of the merged path
+#pragma unroll
+  for (int l = 0; l < 3; ++l) b3[l] = a3[2 - l];
+#pragma unroll
+  for (int l = 0; l < 15; ++l) u[l] = a15[14 - l] + (l <= 6 ? a7[6 - l] : 0.f);
   const int r0 = warp * STEPS;  // window row j = x[t0 + r0 - HALO + j]
   const int items = B * nseg;
   auto stage_item = [&](int it, int buf) {
@@ -134,10 +169,17 @@ __global__ void __launch_bounds__(NW * 32, 3)
       const int tb = t0 + r0;
       const size_t o = ((size_t)b * T + tb) * D + d;
       const int n = T - tb < STEPS ? T - tb : STEPS;
-      if (n == STEPS)
-        fwd_steps<WQ, WC, true>(win, a3, a7, a15, S + o, Sq + o, c7o + o, c15o + o, STEPS, D);
-      else if (n > 0)
-        fwd_steps<WQ, WC, false>(win, a3, a7, a15, S + o, Sq + o, c7o + o, c15o + o, n, D);
+      if (WC) {  // layer-op caches need c7 and c15 separately
+        if (n == STEPS)
+          fwd_steps<WQ, WC, true>(win, a3, a7, a15, S + o, Sq + o, c7o + o, c15o + o, STEPS, D);
+        else if (n > 0)
+          fwd_steps<WQ, WC, false>(win, a3, a7, a15, S + o, Sq + o, c7o + o, c15o + o, n, D);
+      } else {
+        if (n == STEPS)
+          fwd_steps_merged<WQ, true>(win, b3, u, S + o, Sq + o, STEPS, D);
+        else if (n > 0)
+          fwd_steps_merged<WQ, false>(win, b3, u, S + o, Sq + o, n, D);
+      }
     }
     __syncthreads();  // buffer `buf` is restaged PIPE - 1 iterations on
     buf = (buf + 1) % PIPE;
@@ -145,58 +187,56 @@ __global__ void __launch_bounds__(NW * 32, 3)
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
-// Data + weight gradient. CTA (channel group, part p) loops over tiles
-// (b, segment) = p, p + nparts, ...; dx rows of a tile need dS rows up to 14
-// steps AFTER it (anti-causal), the weight gradient x rows 14 steps before.
-// dx[t] = sum_K sum_k w_K[k] dS[t + (K-1) - k] for one warp's steps from its
-// dS window (gs[j] = dS[tb + j]); ACC: dx += instead of =.
+// Data + weight gradient, merged by lag l = K-1-k (tap k of kernel K reads
+// x[t - l]):
+//   dx[t]   = sum_l E[l] dS[t + l],  E[l] = w15[14-l] + w7[6-l] + w3[2-l]
+//             (terms present for l <= K-1): 15 multiply-adds per step, not 25;
+//   C[l]   += x[t - l] dS[t], and dw_K[k] = sum C[K-1-k]: 15 lag correlations
+//             per channel serve all 25 tap gradients.
+// dx for one warp's steps from its dS window (gs[j] = dS[tb + j]); ACC: dx +=.
 template <bool ACC, bool FULL>
-__device__ __forceinline__ void dx_steps(const float (&gs)[WIN], const float (&a3)[3],
-                                         const float (&a7)[7], const float (&a15)[15], float* px,
+__device__ __forceinline__ void dx_steps(const float (&gs)[WIN], const float (&E)[15], float* px,
                                          int n, int D) {
 #pragma unroll
   for (int i = 0; i < STEPS; ++i) {
     if (!FULL && i >= n) break;
-    float s3 = 0.f, s7 = 0.f, s15 = 0.f;
+    float v = 0.f;
 #pragma unroll
-    for (int k = 0; k < 3; ++k) s3 += a3[k] * gs[i + 2 - k];
-#pragma unroll
-    for (int k = 0; k < 7; ++k) s7 += a7[k] * gs[i + 6 - k];
-#pragma unroll
-    for (int k = 0; k < 15; ++k) s15 += a15[k] * gs[i + 14 - k];
-    const float v = s3 + s7 + s15;
+    for (int l = 14; l >= 0; --l) v += E[l] * gs[i + l];
     *px = ACC ? *px + v : v;
     px += D;
   }
 }
 
+// CTA (channel group, part p) loops over tiles (b, segment) = p, p + nparts,
+// ...; dx rows of a tile need dS rows up to 14 steps AFTER it (anti-causal),
+// the lag correlations x rows 14 steps before. Writes the CTA's 15 lag sums
+// per channel to parts[p][15][D].
 template <bool ACC>
-__global__ void __launch_bounds__(NW * 32, 2)
+__global__ void __launch_bounds__(NW * 32, 3)
     conv_bwd_kernel(const float* __restrict__ dS, const float* __restrict__ x,
                     const float* __restrict__ w3, const float* __restrict__ w7,
                     const float* __restrict__ w15, float* __restrict__ dx,
                     float* __restrict__ parts, int B, int T, int D, int nseg, int nparts) {
-  // two buffers of {x tile, dS tile}: the next tile is staged while this one
+  // PIPE_B buffers of {x tile, dS tile}: later tiles are staged while this one
   // is consumed
   extern __shared__ __align__(16) float smem[];
   typedef float Tile[ROWS][CW];
-  Tile* sx = reinterpret_cast<Tile*>(smem);                     // [PIPE]
-  Tile* sg = reinterpret_cast<Tile*>(smem + PIPE * ROWS * CW);  // [PIPE]
+  Tile* sx = reinterpret_cast<Tile*>(smem);                     // [PIPE_B]
+  Tile* sg = reinterpret_cast<Tile*>(smem + PIPE_B * ROWS * CW);  // [PIPE_B]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c0 = blockIdx.x * CW;
   const int d = c0 + lane;
   const bool act = d < D;
-  float a3[3], a7[7], a15[15];
+  float E[15], C[15];
 #pragma unroll
-  for (int k = 0; k < 3; ++k) a3[k] = act ? w3[k * D + d] : 0.f;
-#pragma unroll
-  for (int k = 0; k < 7; ++k) a7[k] = act ? w7[k * D + d] : 0.f;
-#pragma unroll
-  for (int k = 0; k < 15; ++k) a15[k] = act ? w15[k * D + d] : 0.f;
-  float g3[3] = {0, 0, 0}, g7[7] = {0, 0, 0, 0, 0, 0, 0};
-  float g15[15];
-#pragma unroll
-  for (int k = 0; k < 15; ++k) g15[k] = 0.f;
+  for (int l = 0; l < 15; ++l) {
+    float e = act ? w15[(14 - l) * D + d] : 0.f;
+    if (l <= 6 && act) e += w7[(6 - l) * D + d];
+    if (l <= 2 && act) e += w3[(2 - l) * D + d];
+    E[l] = e;
+    C[l] = 0.f;
+  }
   const int r0 = warp * STEPS;
   const int items = B * nseg;
   auto stage_item = [&](int it, int buf) {
@@ -209,11 +249,11 @@ __global__ void __launch_bounds__(NW * 32, 2)
     asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty
   };
 #pragma unroll
-  for (int q = 0; q < PIPE - 1; ++q) stage_item(blockIdx.y + q * nparts, q);
+  for (int q = 0; q < PIPE_B - 1; ++q) stage_item(blockIdx.y + q * nparts, q);
   int buf = 0;
   for (int it = blockIdx.y; it < items; it += nparts) {
-    stage_item(it + (PIPE - 1) * nparts, (buf + PIPE - 1) % PIPE);
-    asm volatile("cp.async.wait_group %0;" ::"n"(PIPE - 1) : "memory");
+    stage_item(it + (PIPE_B - 1) * nparts, (buf + PIPE_B - 1) % PIPE_B);
+    asm volatile("cp.async.wait_group %0;" ::"n"(PIPE_B - 1) : "memory");
     __syncthreads();
     const int b = it / nseg;
     const int t0 = (it % nseg) * TS;
@@ -225,72 +265,69 @@ __global__ void __launch_bounds__(NW * 32, 2)
       const int n = T - tb < STEPS ? T - tb : STEPS;
       float* px = dx + ((size_t)b * T + tb) * D + d;
       if (n == STEPS)
-        dx_steps<ACC, true>(gs, a3, a7, a15, px, STEPS, D);
+        dx_steps<ACC, true>(gs, E, px, STEPS, D);
       else if (n > 0)
-        dx_steps<ACC, false>(gs, a3, a7, a15, px, n, D);
-      // weight grads: g_K[k] += x[t-(K-1)+k] * dS[t] (dS zero past T). Window
-      // row j = x[t0 + r0 - 14 + j] is read once and feeds every (k, i) with
-      // i + 14 - (K-1) + k = j; per k the sum still runs over i ascending.
+        dx_steps<ACC, false>(gs, E, px, n, D);
+      // C[l] += x[t - l] dS[t] (dS zero past T). Window row j = x[t0 + r0 -
+      // 14 + j] is read once and feeds every (l, i) with i + 14 - l = j; per
+      // l the sum runs over i ascending.
 #pragma unroll
       for (int j = 0; j < WIN; ++j) {
         const float xv = sx[buf][r0 + j][lane];
 #pragma unroll
-        for (int k = 0; k < 15; ++k) {
-          const int i = j - k;
-          if (i >= 0 && i < STEPS) g15[k] += xv * gs[i];
-        }
-#pragma unroll
-        for (int k = 0; k < 7; ++k) {
-          const int i = j - 8 - k;
-          if (i >= 0 && i < STEPS) g7[k] += xv * gs[i];
-        }
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-          const int i = j - 12 - k;
-          if (i >= 0 && i < STEPS) g3[k] += xv * gs[i];
+        for (int l = 0; l < 15; ++l) {
+          const int i = j - 14 + l;
+          if (i >= 0 && i < STEPS) C[l] += xv * gs[i];
         }
       }
     }
-    __syncthreads();  // buffer `buf` is restaged PIPE - 1 iterations on
-    buf = (buf + 1) % PIPE;
+    __syncthreads();  // buffer `buf` is restaged PIPE_B - 1 iterations on
+    buf = (buf + 1) % PIPE_B;
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   // CTA partial: sum the 8 warps' accumulators in warp order
-  float(*red)[NW][CW] = reinterpret_cast<float(*)[NW][CW]>(smem);  // [25][8][32]
-  static_assert(25 * NW * CW <= 2 * PIPE * ROWS * CW, "reduction scratch");
+  float(*red)[NW][CW] = reinterpret_cast<float(*)[NW][CW]>(smem);  // [15][8][32]
+  static_assert(15 * NW * CW <= 2 * PIPE_B * ROWS * CW, "reduction scratch");
 #pragma unroll
-  for (int k = 0; k < 3; ++k) red[k][warp][lane] = g3[k];
-#pragma unroll
-  for (int k = 0; k < 7; ++k) red[3 + k][warp][lane] = g7[k];
-#pragma unroll
-  for (int k = 0; k < 15; ++k) red[10 + k][warp][lane] = g15[k];
+  for (int l = 0; l < 15; ++l) red[l][warp][lane] = C[l];
   __syncthreads();
-  for (int j = warp; j < 25; j += NW) {
+  for (int l = warp; l < 15; l += NW) {
     float sum = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) sum += red[j][w][lane];
-    if (act) parts[((size_t)blockIdx.y * 25 + j) * D + d] = sum;
+    for (int w = 0; w < NW; ++w) sum += red[l][w][lane];
+    if (act) parts[((size_t)blockIdx.y * 15 + l) * D + d] = sum;
   }
 }
 
+// dw_K[k] += sum over parts of C[K-1-k] (parts in order; one lag sum serves
+// the taps of every kernel size that reach it).
 __global__ void conv_wgrad_reduce(const float* __restrict__ parts, int nparts, int D,
                                   float* __restrict__ dw3, float* __restrict__ dw7,
                                   float* __restrict__ dw15) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // over 25*D
-  if (i >= 25 * D) return;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // over 15*D
+  if (i >= 15 * D) return;
+  // loads in batches of 8 parts (independent), additions in part order
   float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += parts[(size_t)p * 25 * D + i];
-  const int j = i / D, d = i % D;
-  if (j < 3) dw3[j * D + d] += s;
-  else if (j < 10) dw7[(j - 3) * D + d] += s;
-  else dw15[(j - 10) * D + d] += s;
+  for (int p0 = 0; p0 < nparts; p0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      v[j] = p0 + j < nparts ? parts[(size_t)(p0 + j) * 15 * D + i] : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (p0 + j < nparts) s += v[j];
+  }
+  const int l = i / D, d = i % D;
+  dw15[(14 - l) * D + d] += s;
+  if (l <= 6) dw7[(6 - l) * D + d] += s;
+  if (l <= 2) dw3[(2 - l) * D + d] += s;
 }
 
 int nparts_for(int B, int T, int D) {
   const int nseg = (T + TS - 1) / TS;
   const int groups = (D + CW - 1) / CW;
-  int p = (148 * 2) / groups;  // every CTA resident (two per SM)
+  int p = (148 * 3) / groups;  // every CTA resident (three per SM)
   if (p > MAX_PARTS) p = MAX_PARTS;
   if (p > B * nseg) p = B * nseg;
   return p < 1 ? 1 : p;
@@ -320,7 +357,7 @@ cudaError_t conv_fwd(const float* x, const float* w3, const float* w7, const flo
 }
 
 size_t conv_bwd_partials_floats(int B, int T, int D) {
-  return (size_t)nparts_for(B, T, D) * 25 * D;
+  return (size_t)nparts_for(B, T, D) * 15 * D;
 }
 
 cudaError_t conv_bwd(const float* dS, const float* x, const float* w3, const float* w7,
@@ -331,13 +368,13 @@ cudaError_t conv_bwd(const float* dS, const float* x, const float* w3, const flo
   const int nseg = (T + TS - 1) / TS;
   const int np = nparts_for(B, T, D);
   dim3 grid((D + CW - 1) / CW, np);
-  constexpr size_t smem = 2 * PIPE * ROWS * CW * sizeof(float);
+  constexpr size_t smem = 2 * PIPE_B * ROWS * CW * sizeof(float);
   auto kern = accumulate ? conv_bwd_kernel<true> : conv_bwd_kernel<false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   kern<<<grid, NW * 32, smem, s>>>(dS, x, w3, w7, w15, dx, partials, B, T, D, nseg, np);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  conv_wgrad_reduce<<<(25 * D + 255) / 256, 256, 0, s>>>(partials, np, D, dw3, dw7, dw15);
+  conv_wgrad_reduce<<<(15 * D + 255) / 256, 256, 0, s>>>(partials, np, D, dw3, dw7, dw15);
   return launched(2);
 }
 

@@ -233,8 +233,9 @@ int Engine::ensure_capacity(int N, bool with_caches) {
   if (with_caches) {
     f(&dX_, n * D); f(&dsub_, n * D); f(&dS_, n * D); f(&dq_, n * D); f(&dr_, n * D);
     f(&dPZH_, 2 * n * D); f(&dGU_, 2 * n * F); f(&dnf_, n * D);
-    // conv weight-grad partials (<= 192 x 25 x D) and CE loss partials share it
-    const size_t cp = 192 * 25 * D, cep = rnet_k::ce_partials_floats(N) + 8;
+    // conv weight-grad partials and CE loss partials share it
+    const size_t cp = rnet_k::conv_bwd_partials_floats(N, 1, D),
+                 cep = rnet_k::ce_partials_floats(N) + 8;
     f(&conv_parts_, cp > cep ? cp : cep);
   } else {
     dX_ = dsub_ = dS_ = dq_ = dr_ = dPZH_ = dGU_ = dnf_ = conv_parts_ = nullptr;
