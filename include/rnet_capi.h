@@ -60,6 +60,10 @@ int rnet_gemm_f32(int M, int N, int K, const float* A, int lda, int a_mn_major, 
  * No counterpart in the reference (its GEMMs are cuBLAS calls). */
 int rnet_gemm_set_cta_group(int cta_group);
 
+/* Arithmetic of later rnet_gemm_f32 calls in this process: 0 = fp32-accurate
+ * (default), 1 = bf16 operands with fp32 accumulation. */
+int rnet_gemm_set_precision(int precision);
+
 /* ------------------------------------------------------------------ layer ops
  * One entry per function of the reference's include/layers.h:28-153, same
  * argument meaning, same accumulate/overwrite contract:
@@ -170,6 +174,11 @@ int rnet_model_get_grads(rnet_model* m, float* host, size_t n);
 /* Re-derive internal layouts after the caller wrote d_params directly. */
 int rnet_model_params_updated(rnet_model* m);
 int rnet_model_set_conv_quirk(rnet_model* m, int on);
+/* GEMM arithmetic of the model: 0 = fp32-accurate (3xTF32 tcgen05, default),
+ * 1 = bf16 operands with fp32 accumulation (one tcgen05 kind::f16 MMA per
+ * product block; parity with fp32 within 2e-2). Parameters, gradients,
+ * activations and the optimizer stay fp32. */
+int rnet_model_set_precision(rnet_model* m, int precision);
 int rnet_model_forward(rnet_model* m, const int* d_tokens, float* d_logits, int batch,
                        int seq_len);
 int rnet_model_backward(rnet_model* m, const float* d_dlogits, const int* d_tokens, int batch,

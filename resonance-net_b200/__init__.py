@@ -47,6 +47,7 @@ _SIGS = {
     "rnet_device_error": [ctypes.POINTER(ctypes.c_uint), _I],
     "rnet_gemm_f32": [_I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _I, _P, _I, _I, _F, _P],
     "rnet_gemm_set_cta_group": [_I],
+    "rnet_gemm_set_precision": [_I],
     "rnet_rms_norm_forward": [_P, _P, _P, _P, _I, _I, _F, _P],
     "rnet_rms_norm_backward": [_P, _P, _P, _P, _P, _P, _I, _I, _P],
     "rnet_embed_forward": [_P, _P, _P, _I, _I, _I, _P],
@@ -76,6 +77,7 @@ _SIGS = {
     "rnet_model_get_grads": [_P, _P, _SZ],
     "rnet_model_params_updated": [_P],
     "rnet_model_set_conv_quirk": [_P, _I],
+    "rnet_model_set_precision": [_P, _I],
     "rnet_model_forward": [_P, _P, _P, _I, _I],
     "rnet_model_backward": [_P, _P, _P, _I, _I],
     "rnet_model_zero_grad": [_P],
@@ -226,6 +228,10 @@ class Model:
 
     def set_conv_quirk(self, on: bool) -> None:
         check(lib().rnet_model_set_conv_quirk(self._h, int(on)))
+
+    def set_precision(self, bf16: bool) -> None:
+        """GEMM arithmetic: fp32-accurate (default) or bf16 operands / fp32 accumulation."""
+        check(lib().rnet_model_set_precision(self._h, int(bool(bf16))))
 
     def forward(self, d_tokens, d_logits, batch: int, seq_len: int) -> None:
         check(lib().rnet_model_forward(self._h, _ptr(d_tokens), _ptr(d_logits), batch, seq_len))

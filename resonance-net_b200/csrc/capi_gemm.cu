@@ -5,6 +5,15 @@
 #include "gemm.cuh"
 #include "status.h"
 
+static int g_gemm_precision = 0;
+
+extern "C" int rnet_gemm_set_precision(int precision) {
+  if (precision != 0 && precision != 1)
+    return rnet_status::fail(RNET_ERR_ARG, "rnet_gemm_set_precision: expected 0 or 1");
+  g_gemm_precision = precision;
+  return RNET_OK;
+}
+
 extern "C" int rnet_gemm_f32(int M, int N, int K, const float* A, int lda, int a_mn_major,
                              const float* B, int ldb, int b_mn_major, float* C, int ldc,
                              const float* R, int ldr, int op, float alpha, void* stream) {
@@ -21,7 +30,7 @@ extern "C" int rnet_gemm_f32(int M, int N, int K, const float* A, int lda, int a
   e.R = R;
   e.ldr = ldr;
   cudaError_t err = gemm_tf32x3((cudaStream_t)stream, M, N, K, a, b, e, 0, 0,
-                                rnet_status::device_error_word());
+                                rnet_status::device_error_word(), g_gemm_precision);
   if (err != cudaSuccess) {
     const std::string what = std::string("rnet_gemm_f32 (") + gemm_last_reason() + ")";
     return rnet_status::fail_cuda(err, what.c_str());

@@ -205,15 +205,25 @@ __device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint6
         : "memory");
 }
 
-// D(tmem) (+)= A * B, kind::f16 (bf16 inputs, fp32 accumulate).
+// D(tmem) (+)= A * B, kind::f16 (bf16 inputs, fp32 accumulate; both operands
+// bf16), issued like umma_tf32.
+template <int CG = 1>
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
+  if constexpr (CG == 1)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
 }
 
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread finish.
@@ -261,6 +271,9 @@ __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, float (&v)[32]) {
 }
 
 // Shared-memory matrix descriptor (sm_100 UMMA form).
+//   layout 0 = SWIZZLE_NONE (K-major): 8-row x 16 B core matrices, rows 16 B
+//              apart; `lbo` = stride between the core matrices adjacent in K,
+//              `sbo` = stride between 8-row groups.
 //   layout 2 = SWIZZLE_128B (K-major operands): rows of 128 B (32 fp32 along
 //              K), 8-row groups 1024 B apart (SBO), LBO unused (16).
 //   layout 1 = SWIZZLE_128B_BASE32B (MN-major fp32 operands, the only MN-major

@@ -314,7 +314,7 @@ int Engine::profile_read(ProfStats* out, bool reset) {
   PROF(PK_GEMM, 2.0 * (M) * (N) * (K),                                                    \
        4.0 * ((double)(M) * (K) + (double)(N) * (K) +                                     \
               (double)(M) * (N) * (((E).kind == EPI_RESID || (E).kind == EPI_ACCUM) ? 2 : 1)), \
-       gemm_tf32x3(stream_, (M), (N), (K), (A), (B), (E), (PAIR), (SPLITS), err))
+       gemm_tf32x3(stream_, (M), (N), (K), (A), (B), (E), (PAIR), (SPLITS), err, precision))
 #define MM(M, N, K, A, B, E, PAIR) MMS(M, N, K, A, B, E, PAIR, 0)
 // residual accumulation: one K pass (deterministic, one rounding per element)
 #define MM_RES(M, N, K, A, B, C) MMS(M, N, K, A, B, epi_accum(C, N), 0, 1)

@@ -125,6 +125,9 @@ class Engine {
   const rnet_model_config& config() const { return cfg_; }
 
   bool conv_quirk = true;  // reference dmix operand (S + c7 + c15)
+  // GEMM arithmetic: rnet_gemm::PREC_TF32X3 (fp32-accurate, default) or
+  // PREC_BF16 (operands rounded to bf16, fp32 accumulation)
+  int precision = 0;
   DistComm* dist = nullptr;
 
   // workspace capacity in tokens

@@ -46,9 +46,16 @@ struct Epilogue {
 // logical rows n0 and n0 + b_pair_off (used to pair gate/up weights so one
 // accumulator tile holds both). `k_splits` = 0 picks automatically (only
 // EPI_ACCUM may split K). Returns cudaSuccess or the launch error.
+// Arithmetic of the products.
+enum Precision : int {
+  PREC_TF32X3 = 0,  // fp32-accurate: hi*lo + lo*hi + hi*hi tf32 MMAs
+  PREC_BF16 = 1,    // operands rounded to bf16, fp32 accumulation, one MMA
+};
+
 cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand& A,
                         const Operand& B, const Epilogue& epi, int b_pair_off = 0,
-                        int k_splits = 0, unsigned* err_word = nullptr);
+                        int k_splits = 0, unsigned* err_word = nullptr,
+                        int precision = PREC_TF32X3);
 
 // Number of SMs of the current device (cached).
 int num_sms();

@@ -31,6 +31,8 @@
 #include <utility>
 #include <vector>
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
@@ -351,7 +353,9 @@ __device__ __forceinline__ void load_b(uint8_t* sb, const void* map, uint64_t* b
 // A cluster barrier after set-up (barrier init, TMEM alloc) and before
 // teardown (TMEM dealloc, exit) keeps either CTA from touching the other's
 // barriers or TMEM outside their lifetime.
-template <int BN, int BK, int CG>
+// BF = false: 3xTF32 (fp32-accurate). BF = true: operands rounded to bf16 by
+// the split warps (fp32 accumulate), one kind::f16 MMA per K-block.
+template <int BN, int BK, int CG, bool BF>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, const KParams p) {
@@ -430,6 +434,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == MMA_WARP) {
     if (lane == 0 && rank == 0) {
       const uint32_t idesc = make_idesc(BM * CG, BN, 2, p.a_mn, p.b_mn);
+      const uint32_t idesc_bf = make_idesc(BM * CG, BN, 1, 0, 0);  // bf16, both K-major
       // Byte advance of one 8-deep K slice and LBO / SBO / layout per operand.
       const uint32_t a_kstep = p.a_mn ? 1024u : 32u;
       const uint32_t b_kstep = p.b_mn ? 1024u : 32u;
@@ -457,19 +462,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (!mbar_wait(&split[s], ph, p.err, abort_flag)) { ok = false; break; }
             tc_fence_after();
             const uint32_t a_hi = smem_u32(smem + s * C::STAGE_BYTES);
-            const uint32_t b_hi = a_hi + C::A_BYTES;
-            const uint32_t a_lo = a_hi + C::RAW_BYTES;
-            const uint32_t b_lo = b_hi + C::RAW_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < BK / 8; ++kk) {
-              const uint64_t dah = make_sdesc(a_hi + kk * a_kstep, a_lbo, a_sbo, a_lay);
-              const uint64_t dal = make_sdesc(a_lo + kk * a_kstep, a_lbo, a_sbo, a_lay);
-              const uint64_t dbh = make_sdesc(b_hi + kk * b_kstep, b_lbo, b_sbo, b_lay);
-              const uint64_t dbl = make_sdesc(b_lo + kk * b_kstep, b_lbo, b_sbo, b_lay);
-              umma_tf32<CG>(tacc, dah, dbl, idesc, accumulate);
-              umma_tf32<CG>(tacc, dal, dbh, idesc, 1);
-              umma_tf32<CG>(tacc, dah, dbh, idesc, 1);
+            if constexpr (BF) {
+              // bf16 tiles (K-major, no swizzle) written by the split warps
+              const uint32_t a_bf = a_hi + C::RAW_BYTES;
+              const uint32_t b_bf = a_bf + BM * 32;
+              umma_f16<CG>(tacc, make_sdesc(a_bf, 128, 256, 0), make_sdesc(b_bf, 128, 256, 0),
+                           idesc_bf, accumulate);
               accumulate = 1;
+            } else {
+              const uint32_t b_hi = a_hi + C::A_BYTES;
+              const uint32_t a_lo = a_hi + C::RAW_BYTES;
+              const uint32_t b_lo = b_hi + C::RAW_BYTES;
+#pragma unroll
+              for (int kk = 0; kk < BK / 8; ++kk) {
+                const uint64_t dah = make_sdesc(a_hi + kk * a_kstep, a_lbo, a_sbo, a_lay);
+                const uint64_t dal = make_sdesc(a_lo + kk * a_kstep, a_lbo, a_sbo, a_lay);
+                const uint64_t dbh = make_sdesc(b_hi + kk * b_kstep, b_lbo, b_sbo, b_lay);
+                const uint64_t dbl = make_sdesc(b_lo + kk * b_kstep, b_lbo, b_sbo, b_lay);
+                umma_tf32<CG>(tacc, dah, dbl, idesc, accumulate);
+                umma_tf32<CG>(tacc, dal, dbh, idesc, 1);
+                umma_tf32<CG>(tacc, dah, dbh, idesc, 1);
+                accumulate = 1;
+              }
             }
             if constexpr (PAIR) umma_commit_pair(&empty[s]); else umma_commit<CG>(&empty[s]);
           }
@@ -497,19 +511,56 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           if (!mbar_wait(&full[s], ph, p.err, abort_flag)) { ok = false; break; }
-          const float4* raw = reinterpret_cast<const float4*>(smem + s * C::STAGE_BYTES);
-          float4* lo = reinterpret_cast<float4*>(smem + s * C::STAGE_BYTES + C::RAW_BYTES);
-          // lo = x - (x with the low 13 mantissa bits cleared); the layout is
-          // elementwise-identical to the raw tile, so swizzling is irrelevant
+          if constexpr (BF) {
+            // Round the raw fp32 tiles (unswizzled: K-major [rows][16], MN-major
+            // 32-wide chunks of [16 k-rows][32]) to bf16 into K-major core-matrix
+            // order: row r, K-chunk c (8 values) at (r/8)*256 + c*128 + (r%8)*16.
+            // A warp handles 32 consecutive rows of one K-chunk.
+            const uint8_t* rawb = smem + s * C::STAGE_BYTES;
+            uint8_t* bfb = smem + s * C::STAGE_BYTES + C::RAW_BYTES;
+            constexpr int ROWS_ALL = BM + C::B_ROWS;
+#pragma unroll 2
+            for (int q = t; q < 2 * ROWS_ALL; q += NT) {
+              const int kc = (q >> 5) & 1;
+              const int r = (q & 31) + 32 * (q >> 6);
+              const bool is_a = r < BM;
+              const int rr = is_a ? r : r - BM;
+              const uint8_t* src = rawb + (is_a ? 0 : C::A_BYTES);
+              float v[8];
+              if (!(is_a ? p.a_mn : p.b_mn)) {
+                const float4* s4 = reinterpret_cast<const float4*>(src + rr * 64 + kc * 32);
+                const float4 x0 = s4[0], x1 = s4[1];
+                v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+                v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+              } else {
+                const float* sf =
+                    reinterpret_cast<const float*>(src + (rr >> 5) * C::MN_CHUNK + (rr & 31) * 4);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = sf[(kc * 8 + u) * 32];
+              }
+              uint32_t w[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                w[i] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i])) |
+                       ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i + 1])) << 16);
+              *reinterpret_cast<uint4*>(bfb + (is_a ? 0 : BM * 32) + (rr >> 3) * 256 + kc * 128 +
+                                        (rr & 7) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else {
+            const float4* raw = reinterpret_cast<const float4*>(smem + s * C::STAGE_BYTES);
+            float4* lo = reinterpret_cast<float4*>(smem + s * C::STAGE_BYTES + C::RAW_BYTES);
+            // lo = x - (x with the low 13 mantissa bits cleared); the layout is
+            // elementwise-identical to the raw tile, so swizzling is irrelevant
 #pragma unroll 4
-          for (int i = t; i < N4; i += NT) {
-            const float4 x = raw[i];
-            float4 l;
-            l.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
-            l.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
-            l.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
-            l.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
-            lo[i] = l;
+            for (int i = t; i < N4; i += NT) {
+              const float4 x = raw[i];
+              float4 l;
+              l.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+              l.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+              l.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+              l.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+              lo[i] = l;
+            }
           }
           fence_proxy_async_smem();
           __syncwarp();
@@ -608,13 +659,13 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int BK, int CG>
+template <int BN, int BK, int CG, bool BF>
 static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
                           const KParams& kp) {
   using C = Cfg<BN, BK, CG>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK, CG>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK, CG, BF>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES);
     if (e != cudaSuccess) {
@@ -641,7 +692,7 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
     if (CG > 1) {
       int n = 0;
       cfg.gridDim = dim3(max_groups * CG);
-      if (cudaOccupancyMaxActiveClusters(&n, gemm_tf32x3_kernel<BN, BK, CG>, &cfg) ==
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_tf32x3_kernel<BN, BK, CG, BF>, &cfg) ==
               cudaSuccess &&
           n > 0 && n < max_groups)
         max_groups = n;
@@ -653,7 +704,7 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
   }
   const int groups = kp.num_units < max_groups ? kp.num_units : max_groups;
   cfg.gridDim = dim3(groups * CG);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, BK, CG>, ta, tb, kp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, BK, CG, BF>, ta, tb, kp);
   if (e != cudaSuccess) {
     g_reason = "kernel launch";
     return e;
@@ -752,7 +803,8 @@ cudaError_t reserve_workspace(cudaStream_t stream, size_t floats) {
 
 cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand& A,
                         const Operand& B, const Epilogue& epi, int b_pair_off, int k_splits,
-                        unsigned* err_word) {
+                        unsigned* err_word, int precision) {
+  const bool bf = precision == PREC_BF16;
   if (M <= 0 || N <= 0) return cudaSuccess;
   g_reason = "";
   if (K <= 0 || A.p == nullptr || B.p == nullptr) return reject("K <= 0 or null operand");
@@ -837,8 +889,12 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   kp.k_splits = (kp.kb_total + kp.kb_per_split - 1) / kp.kb_per_split;
   kp.num_units = row_owner ? kp.m_tiles : kp.m_tiles * kp.n_tiles * kp.k_splits;
 
-  const CUtensorMapSwizzle kswz = BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  const CUtensorMapSwizzle mswz = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+  // bf16: the split warps read the raw fp32 tiles, so they stay unswizzled
+  const CUtensorMapSwizzle kswz =
+      bf ? CU_TENSOR_MAP_SWIZZLE_NONE
+         : (BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+  const CUtensorMapSwizzle mswz =
+      bf ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   auto map_a = [&](CUtensorMap* m, const float* base) {
     return !A.mn_major ? make_map(m, base, (uint64_t)K, (uint64_t)M, A.ld, BK, BM, kswz)
                        : make_map(m, base, (uint64_t)M, (uint64_t)K, A.ld, 32, BK, mswz);
@@ -856,10 +912,21 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   if (!map_b(&tb, B.p)) return reject("tensor map of B rejected");
 
   cudaError_t e;
-  if (CG == 2)
-    e = BN == 128 ? launch<128, BK, 2>(stream, ta, tb, kp) : launch<256, BK, 2>(stream, ta, tb, kp);
-  else
-    e = BN == 128 ? launch<128, BK, 1>(stream, ta, tb, kp) : launch<256, BK, 1>(stream, ta, tb, kp);
+  if (bf) {
+    if (CG == 2)
+      e = BN == 128 ? launch<128, BK, 2, true>(stream, ta, tb, kp)
+                    : launch<256, BK, 2, true>(stream, ta, tb, kp);
+    else
+      e = BN == 128 ? launch<128, BK, 1, true>(stream, ta, tb, kp)
+                    : launch<256, BK, 1, true>(stream, ta, tb, kp);
+  } else {
+    if (CG == 2)
+      e = BN == 128 ? launch<128, BK, 2, false>(stream, ta, tb, kp)
+                    : launch<256, BK, 2, false>(stream, ta, tb, kp);
+    else
+      e = BN == 128 ? launch<128, BK, 1, false>(stream, ta, tb, kp)
+                    : launch<256, BK, 1, false>(stream, ta, tb, kp);
+  }
   if (e != cudaSuccess || kp.split_stride == 0) return e;
   // fixed-order sum of the partials + the caller's epilogue
   const size_t work = (N % 4 == 0) ? (size_t)M * N / 4 : (size_t)M * N;
