@@ -88,3 +88,38 @@ def dp_step(rank, world, port, out_dir, case):
         np.save(os.path.join(out_dir, "dp_params.npy"), new)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def dp_engine(rank, world, port, out_dir, case):
+    """Data-parallel engine step on `world` GPUs: each rank trains its shard of
+    the batch with the NCCL gradient all-reduce (rnet.Dist); rank 0 writes the
+    updated parameters."""
+    import torch
+    dist = _init(rank, world, port)
+    rnet = importlib.import_module("resonance-net_b200")
+    rdata = importlib.import_module("resonance-net_b200.data")
+    torch.cuda.set_device(rank)
+    cfg = rnet.ModelConfig.make(d_model=case["d_model"], n_layers=case["n_layers"],
+                                d_ff=case["d_ff"], n_slots=case["n_slots"], top_k=case["top_k"],
+                                vocab=case["vocab"], seq_len=case["T"])
+    m = rnet.Model(cfg, device=rank, reference_init=False)
+    m.set_params(rdata.init_params_normal(cfg, seed=case["pseed"]))
+    uid = [rnet.Dist.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    d = rnet.Dist(rank, world, rank, uid[0])
+    m.set_dist(d)
+    tok, tgt = rdata.uniform_tokens(case["B"], case["T"], seed=case["tseed"])
+    per = case["B"] // world
+    sl = slice(rank * per, (rank + 1) * per)
+    d_in = torch.from_numpy(np.ascontiguousarray(tok[sl]).reshape(-1)).cuda()
+    d_tg = torch.from_numpy(np.ascontiguousarray(tgt[sl]).reshape(-1)).cuda()
+    loss = torch.zeros(1, device="cuda")
+    m.train_step(d_in, d_tg, per, case["T"], case["lr"], case["clip"], loss)
+    m.synchronize()
+    if rank == 0:
+        np.save(os.path.join(out_dir, "dp_engine_params.npy"), m.get_params())
+    dist.barrier()
+    m.set_dist(None)
+    d.close()
+    m.close()
+    dist.destroy_process_group()
