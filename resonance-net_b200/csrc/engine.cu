@@ -69,6 +69,9 @@ Engine::~Engine() {
   for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
   cudaFree(scratch_);
   cudaFree(arena_);
+  if (ev_fork_) cudaEventDestroy(ev_fork_);
+  if (ev_join_) cudaEventDestroy(ev_join_);
+  if (wstream_) cudaStreamDestroy(wstream_);
   if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -91,6 +94,9 @@ int Engine::init(int device, bool reference_init) {
   device_ = device;
   CK(cudaSetDevice(device));
   CK(cudaStreamCreate(&stream_));  // blocking w.r.t. the legacy stream, like the reference
+  CK(cudaStreamCreateWithFlags(&wstream_, cudaStreamNonBlocking));
+  CK(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
+  CK(cudaEventCreateWithFlags(&ev_join_, cudaEventDisableTiming));
 
   const size_t D = c.d_model, V = c.vocab_size, F = c.d_ff, S = c.n_slots, L = c.n_layers;
   P_ = 2 * V * D + D + L * layer_count(c);
@@ -316,6 +322,18 @@ int Engine::profile_read(ProfStats* out, bool reset) {
               (double)(M) * (N) * (((E).kind == EPI_RESID || (E).kind == EPI_ACCUM) ? 2 : 1)), \
        gemm_tf32x3(stream_, (M), (N), (K), (A), (B), (E), (PAIR), (SPLITS), err, precision))
 #define MM(M, N, K, A, B, E, PAIR) MMS(M, N, K, A, B, E, PAIR, 0)
+// Weight-gradient GEMM of the backward on the side stream (after fork()):
+// it runs beside the data-gradient work of the same sublayer, so one GEMM's
+// last partial wave fills SMs the other leaves idle. Profiled runs keep it on
+// the main stream so the per-class event timing stays exact.
+#define MM_W(M, N, K, A, B, E)                                                    \
+  do {                                                                            \
+    if (prof_on_) {                                                               \
+      MM(M, N, K, A, B, E, 0);                                                    \
+    } else {                                                                      \
+      CK(gemm_tf32x3(wstream_, (M), (N), (K), (A), (B), (E), 0, 0, err, precision)); \
+    }                                                                             \
+  } while (0)
 // residual accumulation: one K pass (deterministic, one rounding per element)
 #define MM_RES(M, N, K, A, B, C) MMS(M, N, K, A, B, epi_accum(C, N), 0, 1)
 
@@ -430,43 +448,67 @@ int Engine::layer_backward(int l, int B, int T) {
   float* dKT = dKT_ + (size_t)l * S * D;
   float* dVT = dVT_ + (size_t)l * S * D;
   const double ND4 = 4.0 * N * D;
+  // Weight-gradient GEMMs go to the side stream: fork() when their inputs are
+  // ready on the main stream, join() before the main stream overwrites one
+  // of those inputs (dX_ by the RMSNorm backward; dGU_ / dq_ / dPZH_ / dS_
+  // only in later sublayers).
+  auto fork = [&]() -> cudaError_t {
+    if (prof_on_) return cudaSuccess;
+    cudaError_t e = cudaEventRecord(ev_fork_, s);
+    return e != cudaSuccess ? e : cudaStreamWaitEvent(wstream_, ev_fork_, 0);
+  };
+  auto join = [&]() -> cudaError_t {
+    if (prof_on_) return cudaSuccess;
+    cudaError_t e = cudaEventRecord(ev_join_, wstream_);
+    return e != cudaSuccess ? e : cudaStreamWaitEvent(s, ev_join_, 0);
+  };
   // 4. SwiGLU (src/resonance_net.cpp:468-490, src/swiglu_ffn.cu:88-152)
   // dH = dY W_down into the dG half of dGU, then the pointwise SwiGLU
   // gradient in place (a fused epilogue measured 4x slower: its cache reads
   // have too little memory-level parallelism in four epilogue warps)
+  CK(fork());
+  MM_W(D, F, N, mnmaj(dX_, D), mnmaj(a.H, F), epi_accum(g.down, F));
   MM(N, F, D, kmaj(dX_, D), mnmaj(w.down, F), epi_store(dGU_, 2 * F), 0);
   PROF(PK_OTHER, 0, 5.0 * 4 * N * F,
        rnet_k::swiglu_bwd_pointwise(dGU_, 2 * F, a.G, a.U, N, F, s));
-  MM(D, F, N, mnmaj(dX_, D), mnmaj(a.H, F), epi_accum(g.down, F), 0);
+  CK(fork());
+  MM_W(2 * F, D, N, mnmaj(dGU_, 2 * F), mnmaj(a.n4, D), epi_accum(g.gate, D));
   MM(N, D, 2 * F, kmaj(dGU_, 2 * F), mnmaj(w.gate, D), epi_store(dsub_, D), 0);
-  MM(2 * F, D, N, mnmaj(dGU_, 2 * F), mnmaj(a.n4, D), epi_accum(g.gate, D), 0);
+  CK(join());
   PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, a.r3, w.n4, a.rinv4, dX_, g.n4, N, D, 1, s));
   // 3. slot memory (:492-510, src/slot_memory.cu:171-244) — sparse top-k path
+  CK(fork());
+  MM_W(D, D, N, mnmaj(dX_, D), mnmaj(a.r, D), epi_accum(g.pout, D));
   MM(N, D, D, kmaj(dX_, D), mnmaj(w.pout, D), epi_store(dr_, D), 0);
-  MM(D, D, N, mnmaj(dX_, D), mnmaj(a.r, D), epi_accum(g.pout, D), 0);
   CK(cudaMemsetAsync(dKT, 0, (size_t)S * D * sizeof(float), s));
   CK(cudaMemsetAsync(dVT, 0, (size_t)S * D * sizeof(float), s));
   PROF(PK_SLOT_SPARSE_BWD, 8.0 * k * N * D, (3 + 4 * k) * ND4,
        rnet_k::slot_sparse_bwd(dr_, a.idx, a.w, VT_ + (size_t)l * S * D, KT_ + (size_t)l * S * D,
                                a.q, dq_, dVT, dKT, N, D, S, k, err, s));
+  CK(fork());
+  MM_W(D, D, N, mnmaj(dq_, D), mnmaj(a.n3, D), epi_accum(g.pq, D));
   PROF(PK_OTHER, 0, 16.0 * S * D, rnet_k::transpose(dKT, g.keys, S, D, 1, s));
   PROF(PK_OTHER, 0, 16.0 * S * D, rnet_k::transpose(dVT, g.vals, S, D, 1, s));
   MM(N, D, D, kmaj(dq_, D), mnmaj(w.pq, D), epi_store(dsub_, D), 0);
-  MM(D, D, N, mnmaj(dq_, D), mnmaj(a.n3, D), epi_accum(g.pq, D), 0);
+  CK(join());
   PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, a.r2, w.n3, a.rinv3, dX_, g.n3, N, D, 1, s));
   // 2. MinGRU (:512-528, src/min_gru.cu:128-191)
   PROF(PK_SCAN_BWD, 0, 5 * ND4,
        rnet_k::gru_scan_bwd(dX_, a.z, a.h, nullptr, 0, nullptr, dPZH_, dPZH_ + D, 2 * D, g.bz,
                             g.bh, B, T, D, s));
+  CK(fork());
+  MM_W(2 * D, D, N, mnmaj(dPZH_, 2 * D), mnmaj(a.n2, D), epi_accum(g.Wz, D));
   MM(N, D, 2 * D, kmaj(dPZH_, 2 * D), mnmaj(w.Wz, D), epi_store(dsub_, D), 0);
-  MM(2 * D, D, N, mnmaj(dPZH_, 2 * D), mnmaj(a.n2, D), epi_accum(g.Wz, D), 0);
+  CK(join());
   PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, a.r1, w.n2, a.rinv2, dX_, g.n2, N, D, 1, s));
   // 1. causal conv (:530-545, src/causal_conv.cu:132-190)
+  CK(fork());
+  MM_W(D, D, N, mnmaj(dX_, D), mnmaj(conv_quirk ? a.Sq : a.S, D), epi_accum(g.mix, D));
   MM(N, D, D, kmaj(dX_, D), mnmaj(w.mix, D), epi_store(dS_, D), 0);
-  MM(D, D, N, mnmaj(dX_, D), mnmaj(conv_quirk ? a.Sq : a.S, D), epi_accum(g.mix, D), 0);
   PROF(PK_CONV_BWD, 100.0 * N * D, 3 * ND4,
        rnet_k::conv_bwd(dS_, a.n1, w.c3, w.c7, w.c15, dsub_, g.c3, g.c7, g.c15, conv_parts_, B, T,
                         D, 0, s));
+  CK(join());
   PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, Xl, w.n1, a.rinv1, dX_, g.n1, N, D, 1, s));
   return RNET_OK;
 }

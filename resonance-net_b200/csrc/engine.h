@@ -161,6 +161,8 @@ class Engine {
   rnet_model_config cfg_;
   int device_ = 0;
   cudaStream_t stream_ = nullptr;
+  cudaStream_t wstream_ = nullptr;  // backward weight-gradient GEMMs
+  cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
   size_t P_ = 0;
   float* params_ = nullptr;
   float* grads_ = nullptr;
