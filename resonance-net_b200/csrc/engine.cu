@@ -64,8 +64,7 @@ Engine::~Engine() {
   cudaFree(grads_);
   cudaFree(KT_);
   cudaFree(VT_);
-  cudaFree(dKT_);
-  cudaFree(dVT_);
+  cudaFree(dKV_);
   for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
   cudaFree(scratch_);
   cudaFree(arena_);
@@ -125,8 +124,8 @@ int Engine::init(int device, bool reference_init) {
   bind(grads_, G_, &g_embed_, &g_outw_, &g_fnorm_);
   CK(cudaMalloc(&KT_, L * S * D * sizeof(float)));
   CK(cudaMalloc(&VT_, L * S * D * sizeof(float)));
-  CK(cudaMalloc(&dKT_, L * S * D * sizeof(float)));
-  CK(cudaMalloc(&dVT_, L * S * D * sizeof(float)));
+  // key / value scatter gradients, per layer [keys | values] of [S, D] each
+  CK(cudaMalloc(&dKV_, 2 * L * S * D * sizeof(float)));
   const size_t scr = rnet_k::sgd_scratch_floats() + 64;
   CK(cudaMalloc(&scratch_, scr * sizeof(float)));
   loss_dev_ = scratch_ + rnet_k::sgd_scratch_floats();
@@ -178,11 +177,16 @@ int Engine::init(int device, bool reference_init) {
 }
 
 int Engine::refresh_shadows() {
-  const int D = cfg_.d_model, S = cfg_.n_slots;
-  for (int l = 0; l < cfg_.n_layers; ++l) {
-    CK(rnet_k::transpose(W_[l].keys, KT_ + (size_t)l * S * D, D, S, 0, stream_));
-    CK(rnet_k::transpose(W_[l].vals, VT_ + (size_t)l * S * D, D, S, 0, stream_));
-  }
+  const int D = cfg_.d_model, S = cfg_.n_slots, L = cfg_.n_layers;
+  // keys / values of all layers in one launch (keys and values are adjacent
+  // in a layer's parameter range; layers are evenly spaced)
+  const size_t kv = (size_t)(W_[0].vals - W_[0].keys);
+  const size_t layer = L > 1 ? (size_t)(W_[1].keys - W_[0].keys) : 0;
+  for (int l = 1; l < L; ++l)
+    if ((size_t)(W_[l].keys - W_[0].keys) != l * layer || (size_t)(W_[l].vals - W_[l].keys) != kv)
+      return rnet_status::fail(RNET_ERR_ARG, "refresh_shadows: unexpected parameter layout");
+  CK(rnet_k::transpose_pairs(W_[0].keys, kv, layer, KT_, VT_, (size_t)S * D, L, D, S, 0,
+                             stream_));
   return RNET_OK;
 }
 
@@ -445,8 +449,8 @@ int Engine::layer_backward(int l, int B, int T) {
   unsigned* err = rnet_status::device_error_word();
   cudaStream_t s = stream_;
   const float* Xl = X_ + (size_t)l * N * D;
-  float* dKT = dKT_ + (size_t)l * S * D;
-  float* dVT = dVT_ + (size_t)l * S * D;
+  float* dKT = dKV_ + (size_t)l * 2 * S * D;
+  float* dVT = dKT + (size_t)S * D;
   const double ND4 = 4.0 * N * D;
   // Weight-gradient GEMMs go to the side stream: fork() when their inputs are
   // ready on the main stream, join() before the main stream overwrites one
@@ -480,15 +484,16 @@ int Engine::layer_backward(int l, int B, int T) {
   CK(fork());
   MM_W(D, D, N, mnmaj(dX_, D), mnmaj(a.r, D), epi_accum(g.pout, D));
   MM(N, D, D, kmaj(dX_, D), mnmaj(w.pout, D), epi_store(dr_, D), 0);
-  CK(cudaMemsetAsync(dKT, 0, (size_t)S * D * sizeof(float), s));
-  CK(cudaMemsetAsync(dVT, 0, (size_t)S * D * sizeof(float), s));
+  CK(cudaMemsetAsync(dKT, 0, 2 * (size_t)S * D * sizeof(float), s));  // dKT and dVT
   PROF(PK_SLOT_SPARSE_BWD, 8.0 * k * N * D, (3 + 4 * k) * ND4,
        rnet_k::slot_sparse_bwd(dr_, a.idx, a.w, VT_ + (size_t)l * S * D, KT_ + (size_t)l * S * D,
                                a.q, dq_, dVT, dKT, N, D, S, k, err, s));
   CK(fork());
   MM_W(D, D, N, mnmaj(dq_, D), mnmaj(a.n3, D), epi_accum(g.pq, D));
-  PROF(PK_OTHER, 0, 16.0 * S * D, rnet_k::transpose(dKT, g.keys, S, D, 1, s));
-  PROF(PK_OTHER, 0, 16.0 * S * D, rnet_k::transpose(dVT, g.vals, S, D, 1, s));
+  // dKT, dVT are adjacent [S, D] blocks of consecutive layers: both into
+  // the gradient's keys / values in one launch
+  PROF(PK_OTHER, 0, 32.0 * S * D,
+       rnet_k::transpose_pairs(dKT, (size_t)S * D, 0, g.keys, g.vals, 0, 1, S, D, 1, s));
   MM(N, D, D, kmaj(dq_, D), mnmaj(w.pq, D), epi_store(dsub_, D), 0);
   CK(join());
   PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, a.r2, w.n3, a.rinv3, dX_, g.n3, N, D, 1, s));

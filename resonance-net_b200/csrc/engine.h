@@ -170,8 +170,7 @@ class Engine {
   std::vector<LayerParams> W_, G_;
   float* KT_ = nullptr;  // [L][S][D]
   float* VT_ = nullptr;
-  float* dKT_ = nullptr;
-  float* dVT_ = nullptr;
+  float* dKV_ = nullptr;  // [L][keys | values][S][D] scatter gradients
   float* scratch_ = nullptr;  // sgd / ce scratch
   float* loss_dev_ = nullptr;
   float* norm_dev_ = nullptr;

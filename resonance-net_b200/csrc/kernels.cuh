@@ -58,6 +58,12 @@ cudaError_t gru_scan_bwd(const float* dy, const float* z, const float* h, const 
 // ---- slot memory (slot_memory.cu) -----------------------------------------
 // out[j*R + i] = in[i*C + j] (+ accumulate into out if acc)
 cudaError_t transpose(const float* in, float* out, int R, int C, int acc, cudaStream_t s);
+// A batch of 2 * pairs transposes in one launch: matrix (p, q), q in {0, 1},
+// reads in + p * in_stride2 + q * in_stride1 ([R, C]) and writes
+// (q ? out1 : out0) + p * out_stride ([C, R]).
+cudaError_t transpose_pairs(const float* in, size_t in_stride1, size_t in_stride2, float* out0,
+                            float* out1, size_t out_stride, int pairs, int R, int C, int acc,
+                            cudaStream_t s);
 // r[n,:] = sum_j w[n,j] VT[idx[n,j], :]
 cudaError_t slot_gather(const int* idx, const float* w, const float* VT, float* r, int N,
                         int D, int S, int k, unsigned* err, cudaStream_t s);

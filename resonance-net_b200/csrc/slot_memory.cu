@@ -14,10 +14,17 @@ using namespace rnet_dev;
 
 namespace {
 
-__global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out, int R,
-                                 int C, int acc) {
+// out[j*R + i] (+)= in[i*C + j]; blockIdx.z selects matrix z of a batch:
+// in + (z / 2) * in_stride2 + (z % 2) * in_stride1 -> (z % 2 ? out1 : out0) +
+// (z / 2) * out_stride (keys / values of consecutive layers).
+__global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out0,
+                                 float* __restrict__ out1, size_t in_stride1, size_t in_stride2,
+                                 size_t out_stride, int R, int C, int acc) {
   __shared__ float tile[32][33];
   const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  const int z = blockIdx.z;
+  in += (size_t)(z >> 1) * in_stride2 + (size_t)(z & 1) * in_stride1;
+  float* out = ((z & 1) ? out1 : out0) + (size_t)(z >> 1) * out_stride;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int r = r0 + i, c = c0 + threadIdx.x;
     if (r < R && c < C) tile[i][threadIdx.x] = in[(size_t)r * C + c];
@@ -144,8 +151,18 @@ __global__ void topk_kernel(const float* __restrict__ scores, int* __restrict__ 
 
 cudaError_t transpose(const float* in, float* out, int R, int C, int acc, cudaStream_t s) {
   if (R <= 0 || C <= 0) return cudaSuccess;
-  dim3 grid((C + 31) / 32, (R + 31) / 32);
-  transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(in, out, R, C, acc);
+  dim3 grid((C + 31) / 32, (R + 31) / 32, 1);
+  transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(in, out, out, 0, 0, 0, R, C, acc);
+  return launched();
+}
+
+cudaError_t transpose_pairs(const float* in, size_t in_stride1, size_t in_stride2, float* out0,
+                            float* out1, size_t out_stride, int pairs, int R, int C, int acc,
+                            cudaStream_t s) {
+  if (R <= 0 || C <= 0 || pairs <= 0) return cudaSuccess;
+  dim3 grid((C + 31) / 32, (R + 31) / 32, 2 * pairs);
+  transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(in, out0, out1, in_stride1, in_stride2,
+                                                 out_stride, R, C, acc);
   return launched();
 }
 
