@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(NW * 32, 3)
                     const float* __restrict__ w7, const float* __restrict__ w15,
                     float* __restrict__ S, float* __restrict__ Sq, float* __restrict__ c7o,
                     float* __restrict__ c15o, int B, int T, int D, int nseg, int nparts) {
+  rnet_dev::pdl_trigger();
   // persistent over tiles (b, segment) = p, p + nparts, ... of one channel
   // group, PIPE tiles in flight
   extern __shared__ __align__(16) float smem[];
@@ -218,6 +219,7 @@ __global__ void __launch_bounds__(NW * 32, 3)
                     const float* __restrict__ w3, const float* __restrict__ w7,
                     const float* __restrict__ w15, float* __restrict__ dx,
                     float* __restrict__ parts, int B, int T, int D, int nseg, int nparts) {
+  rnet_dev::pdl_trigger();
   // PIPE_B buffers of {x tile, dS tile}: later tiles are staged while this one
   // is consumed
   extern __shared__ __align__(16) float smem[];
@@ -305,6 +307,7 @@ __global__ void __launch_bounds__(NW * 32, 3)
 __global__ void conv_wgrad_reduce(const float* __restrict__ parts, int nparts, int D,
                                   float* __restrict__ dw3, float* __restrict__ dw7,
                                   float* __restrict__ dw15) {
+  rnet_dev::pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;  // over 15*D
   if (i >= 15 * D) return;
   // loads in batches of 8 parts (independent), additions in part order

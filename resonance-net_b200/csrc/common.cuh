@@ -35,6 +35,19 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// ---------------------------------------------------------------- launch chaining
+// GEMM launches carry programmatic stream serialization: a GEMM's CTAs may
+// start (barrier init, TMEM allocation, descriptor prefetch) while the
+// preceding kernel drains, then block in pdl_wait() until that kernel has
+// completed and its memory is visible. Only GEMMs are launched that way: they
+// read their operands through TMA (L2) and their engine epilogues only store.
+// Every kernel calls pdl_trigger() on entry so a following GEMM may launch
+// once all of its CTAs have started. Both are no-ops without the attribute.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)

@@ -23,6 +23,7 @@ __global__ void decode_conv_kernel(const float* __restrict__ n, float* __restric
                                    const int* __restrict__ pos_ptr, const float* __restrict__ w3,
                                    const float* __restrict__ w7, const float* __restrict__ w15,
                                    float* __restrict__ S, int M, int D) {
+  rnet_dev::pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= M * D) return;
   const int m = i / D, d = i % D;
@@ -53,6 +54,7 @@ __global__ void decode_conv_kernel(const float* __restrict__ n, float* __restric
 __global__ void decode_gru_kernel(const float* __restrict__ P, const float* __restrict__ bz,
                                   const float* __restrict__ bh, float* __restrict__ h,
                                   float* __restrict__ x, int M, int D) {
+  rnet_dev::pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= M * D) return;
   const int m = i / D, d = i % D;
@@ -68,6 +70,7 @@ __global__ void decode_gru_kernel(const float* __restrict__ P, const float* __re
 __global__ void extract_state_kernel(const float* __restrict__ n1, const float* __restrict__ h,
                                      float* __restrict__ ring, float* __restrict__ hs, int M,
                                      int T, int D) {
+  rnet_dev::pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= M * D) return;
   const int m = i / D, d = i % D;
@@ -83,6 +86,7 @@ __global__ void extract_state_kernel(const float* __restrict__ n1, const float* 
 // Row gather: out[m] = x[m*T + T-1]
 __global__ void last_rows_kernel(const float* __restrict__ x, float* __restrict__ out, int M,
                                  int T, int D) {
+  rnet_dev::pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= M * D) return;
   const int m = i / D, d = i % D;
@@ -94,6 +98,7 @@ __global__ void last_rows_kernel(const float* __restrict__ x, float* __restrict_
 __global__ void argmax_kernel(const float* __restrict__ logits, int M, int V,
                               int* __restrict__ tok, int* __restrict__ out,
                               int* __restrict__ pos_ptr) {
+  rnet_dev::pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp < M) {
     const float* l = logits + (size_t)warp * V;
@@ -120,6 +125,7 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int M, int V,
 // h[r, f] = silu(gu[r, f]) * gu[r, F + f]  (gate | up rows of width 2F)
 __global__ void silu_mul_rows_kernel(const float* __restrict__ gu, float* __restrict__ h, int M,
                                      int F) {
+  rnet_dev::pdl_trigger();
   const size_t n = (size_t)M * F;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
@@ -149,6 +155,7 @@ __device__ __forceinline__ void top2_merge(float& a1, float& a2, float b1, float
 
 __global__ void topk2_rows_kernel(const float* __restrict__ scores, int* __restrict__ idx,
                                   float* __restrict__ w, int M, int S) {
+  rnet_dev::pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;

@@ -15,6 +15,7 @@ namespace {
 
 __global__ void embed_fwd_kernel(const int* __restrict__ tok, const float* __restrict__ table,
                                  float* __restrict__ out, int N, int V, int D, unsigned* err) {
+  rnet_dev::pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= N) return;
   int t = tok[warp];
@@ -33,6 +34,7 @@ constexpr int EB_COLS = 64;
 __global__ void embed_bwd_kernel(const float* __restrict__ dout, const int* __restrict__ tok,
                                  float* __restrict__ dtable, int N, int V, int D,
                                  int tokens_per_cta) {
+  rnet_dev::pdl_trigger();
   extern __shared__ float acc[];  // [V][EB_COLS]
   const int c0 = blockIdx.x * EB_COLS;
   const int n0 = blockIdx.y * tokens_per_cta;
@@ -61,6 +63,7 @@ constexpr int CE_MAXV = 32;
 __global__ void ce_kernel(const float* __restrict__ logits, const int* __restrict__ tgt,
                           float* __restrict__ dl, float scale, float* __restrict__ part, int N,
                           int V, unsigned* err) {
+  rnet_dev::pdl_trigger();
   __shared__ float wsum[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
@@ -107,6 +110,7 @@ __global__ void ce_kernel(const float* __restrict__ logits, const int* __restric
 }
 
 __global__ void sum_partials(const float* __restrict__ part, int n, float* __restrict__ out) {
+  rnet_dev::pdl_trigger();
   __shared__ float sh[256];
   float a = 0.f;
   for (int i = threadIdx.x; i < n; i += 256) a += part[i];
@@ -120,17 +124,20 @@ __global__ void sum_partials(const float* __restrict__ part, int n, float* __res
 }
 
 __global__ void residual_kernel(float* __restrict__ x, const float* __restrict__ y, size_t n) {
+  rnet_dev::pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     x[i] += y[i];
 }
 __global__ void scale_kernel(float* __restrict__ x, float a, size_t n) {
+  rnet_dev::pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     x[i] *= a;
 }
 __global__ void add3_kernel(const float* __restrict__ a, const float* __restrict__ b,
                             const float* __restrict__ c, float* __restrict__ o, size_t n) {
+  rnet_dev::pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     o[i] = a[i] + b[i] + c[i];
@@ -138,6 +145,7 @@ __global__ void add3_kernel(const float* __restrict__ a, const float* __restrict
 
 __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u,
                                 float* __restrict__ h, size_t n) {
+  rnet_dev::pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
     const float x = g[i];
@@ -159,6 +167,7 @@ __device__ __forceinline__ void swiglu_grad1(float dh, float g, float u, float& 
 __global__ void swiglu_bwd_pointwise_v4(float* __restrict__ dgu, int ld,
                                         const float* __restrict__ G, const float* __restrict__ U,
                                         int N, int F) {
+  rnet_dev::pdl_trigger();
   const int F4 = F >> 2;
   const size_t n4 = (size_t)N * F4;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
@@ -183,6 +192,7 @@ __global__ void swiglu_bwd_pointwise_v4(float* __restrict__ dgu, int ld,
 __global__ void swiglu_bwd_pointwise_1(float* __restrict__ dgu, int ld,
                                        const float* __restrict__ G, const float* __restrict__ U,
                                        int N, int F) {
+  rnet_dev::pdl_trigger();
   const size_t n = (size_t)N * F;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {

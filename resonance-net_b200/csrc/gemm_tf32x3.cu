@@ -359,6 +359,7 @@ template <int BN, int BK, int CG, bool BF>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, const KParams p) {
+  rnet_dev::pdl_trigger();
   using C = Cfg<BN, BK, CG>;
   constexpr bool PAIR = CG == 2;
   extern __shared__ uint8_t smem_raw[];
@@ -407,6 +408,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if constexpr (PAIR) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  rnet_dev::pdl_wait();  // every global access below follows the preceding kernel
 
   if (warp == PRODUCER_WARP) {
     if (lane == 0) {
@@ -678,13 +680,20 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
   cfg.blockDim = dim3(NUM_THREADS);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CG;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = CG > 1 ? 1 : 0;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = CG;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  // RNET_GEMM_PDL=0 launches without programmatic serialization (A/B timing).
+  static const bool pdl = [] {
+    const char* e = getenv("RNET_GEMM_PDL");
+    return !(e && e[0] == '0');
+  }();
+  cfg.attrs = pdl ? attr : attr + 1;
+  cfg.numAttrs = (CG > 1 ? 1 : 0) + (pdl ? 1 : 0);
   // Persistent grid: one CTA (pair) per SM (pair) that can be co-resident.
   static int max_groups = 0;
   if (max_groups == 0) {
@@ -719,6 +728,7 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
 // results do not depend on scheduling) and applies the epilogue.
 __global__ void __launch_bounds__(256)
     splitk_reduce_kernel(const float* __restrict__ ws, int S, int M, int N, Epilogue e) {
+  rnet_dev::pdl_trigger();
   const size_t plane = (size_t)M * N;
   if ((N & 3) == 0) {
     const int N4 = N >> 2;

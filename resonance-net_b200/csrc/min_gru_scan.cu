@@ -92,6 +92,7 @@ __global__ void __launch_bounds__(W * 32)
                     float* __restrict__ zo, float* __restrict__ ho, float* __restrict__ yo,
                     const float* __restrict__ res, float* __restrict__ out,
                     float* __restrict__ out2, int T, int D) {
+  rnet_dev::pdl_trigger();
   extern __shared__ float smem[];
   float* sZ = smem;             // pz, then z
   float* sT = smem + TILE;      // ph, then h~
@@ -153,6 +154,7 @@ __global__ void __launch_bounds__(W * 32)
                     const float* __restrict__ bh, float* __restrict__ dz,
                     float* __restrict__ dht, int ldd, float* __restrict__ dbz,
                     float* __restrict__ dbh, int T, int D) {
+  rnet_dev::pdl_trigger();
   extern __shared__ float smem[];
   float* sZ = smem;
   float* sG = smem + TILE;

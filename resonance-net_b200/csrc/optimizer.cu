@@ -16,6 +16,7 @@ namespace {
 constexpr int NORM_BLOCKS = 592;  // 4 x 148, fixed so the reduction order is fixed
 
 __global__ void sumsq_kernel(const float* __restrict__ g, size_t n, double* __restrict__ part) {
+  rnet_dev::pdl_trigger();
   __shared__ double sh[256];
   double a = 0.0;
   const size_t n4 = n / 4;
@@ -39,6 +40,7 @@ __global__ void sumsq_kernel(const float* __restrict__ g, size_t n, double* __re
 __global__ void finalize_kernel(const double* __restrict__ part, int nparts, float lr,
                                 float clip, int world, float* __restrict__ lr_out,
                                 float* __restrict__ norm_out) {
+  rnet_dev::pdl_trigger();
   __shared__ double sh[256];
   double a = 0.0;
   for (int i = threadIdx.x; i < nparts; i += 256) a += part[i];
@@ -61,6 +63,7 @@ __global__ void finalize_kernel(const double* __restrict__ part, int nparts, flo
 
 __global__ void update_kernel(float* __restrict__ p, const float* __restrict__ g, size_t n,
                               const float* __restrict__ lr_ptr) {
+  rnet_dev::pdl_trigger();
   const float neg = -*lr_ptr;
   const size_t n4 = n / 4;
   float4* p4 = reinterpret_cast<float4*>(p);

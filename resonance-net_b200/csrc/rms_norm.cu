@@ -24,6 +24,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     rms_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
                    float* __restrict__ y, float* __restrict__ rinv, int rows, int D, float eps,
                    float* __restrict__ xcopy) {
+  rnet_dev::pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = D >> 2;
   const float4* w4 = reinterpret_cast<const float4*>(w);
@@ -68,6 +69,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     rms_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                    const float* __restrict__ w, const float* __restrict__ rinv,
                    float* __restrict__ dx, float* __restrict__ dw, int rows, int D, int mode) {
+  rnet_dev::pdl_trigger();
   extern __shared__ float sdw[];  // [WARPS][D]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = D >> 2;
@@ -145,6 +147,7 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
                           const float* __restrict__ w, const float* __restrict__ rinv,
                           float* __restrict__ dx, float* __restrict__ dw, int rows, int D,
                           int mode) {
+  rnet_dev::pdl_trigger();
   // [2 stages][3 arrays][WARPS rows][D]
   extern __shared__ __align__(16) float sbuf[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -20,6 +20,7 @@ namespace {
 __global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out0,
                                  float* __restrict__ out1, size_t in_stride1, size_t in_stride2,
                                  size_t out_stride, int R, int C, int acc) {
+  rnet_dev::pdl_trigger();
   __shared__ float tile[32][33];
   const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
   const int z = blockIdx.z;
@@ -43,6 +44,7 @@ __global__ void transpose_kernel(const float* __restrict__ in, float* __restrict
 __global__ void gather_kernel(const int* __restrict__ idx, const float* __restrict__ w,
                               const float* __restrict__ VT, float* __restrict__ r, int N, int D,
                               int S, int k, unsigned* err) {
+  rnet_dev::pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= N) return;
   int id[8];
@@ -72,6 +74,7 @@ __global__ void sparse_bwd_kernel(const float* __restrict__ dr, const int* __res
                                   float* __restrict__ dq, float* __restrict__ dVT,
                                   float* __restrict__ dKT, int N, int D, int S, int k,
                                   unsigned* err) {
+  rnet_dev::pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= N) return;
   int id[8];
@@ -124,6 +127,7 @@ __global__ void sparse_bwd_kernel(const float* __restrict__ dr, const int* __res
 // inside the score GEMM epilogue and never materialises the scores.
 __global__ void topk_kernel(const float* __restrict__ scores, int* __restrict__ idx,
                             float* __restrict__ w, int N, int S, int k) {
+  rnet_dev::pdl_trigger();
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= N) return;
   const float* sr = scores + (size_t)row * S;
