@@ -17,8 +17,12 @@
 // The C-ABI forward (which returns c7 and c15) sums per scale in the
 // reference's order (sum += x*w over taps in increasing k, zero left padding;
 // S = (c3 + c7) + c15 as its sum3); the model path merges taps by lag.
+#include <cstdlib>
+
 #include "common.cuh"
+#include "gemm.cuh"
 #include "kernels.cuh"
+#include "status.h"
 
 namespace rnet_k {
 using namespace rnet_dev;
@@ -327,6 +331,249 @@ __global__ void conv_wgrad_reduce(const float* __restrict__ parts, int nparts, i
   if (l <= 2) dw3[(2 - l) * D + d] += s;
 }
 
+// ---- TMA-pipelined backward (the model path) --------------------------------
+// One persistent CTA per SM walks a contiguous range of the flattened tiles
+// f = g * I + item (g = 64-channel group, item = (b, 128-step segment), I =
+// items per group), so every SM gets the same number of tiles to within one.
+// STAGES tiles are staged by TMA: the x tile (128 rows) and the dS tile (142
+// rows: 14 steps past the tile, zero past T); lane 0 of warp 0 issues them,
+// STAGES - 1 tiles ahead. A lane owns a channel pair (packed fp32 pairs).
+// Warps 0-7 compute dx for 16 steps each; warps 8-15 the lag correlations of
+// the same steps, taken forward in time,
+//   C[l] = sum_t x[t] dS[t + l]  (= sum_t x[t - l] dS[t], dS zero past T),
+// so x needs no halo. Splitting the two sums over separate warps halves each
+// warp's dependent instruction stream and doubles the warps that hide its
+// latency. When the range moves to the next channel group (and at the end)
+// the correlation warps' C are summed in warp order into partial slot k + g
+// (CTA k, group g: distinct for every intersecting pair), and
+// conv_wgrad_reduce_slots sums each group's CTAs in CTA order.
+namespace tb {
+constexpr int CW = 64;                     // channels per tile (lane = pair)
+constexpr int NW = 8;                      // warps per role (dx, correlations)
+constexpr int THREADS = 2 * NW * 32;
+constexpr int QS = 4;                      // dx steps per interleaved group
+constexpr int RED_L = 3;                   // lags per reduction round
+constexpr uint32_t RED_BYTES = RED_L * NW * CW * 4;
+// STEPS steps per warp, STAGES tiles staged per CTA.
+template <int STEPS_, int STAGES_>
+struct Cfg {
+  static constexpr int STEPS = STEPS_, STAGES = STAGES_;
+  static constexpr int TS = NW * STEPS;            // steps per tile
+  static constexpr int GROWS = TS + HALO;          // dS rows per tile
+  static constexpr int WIN = STEPS + HALO;         // dS window per warp
+  static constexpr uint32_t XBYTES = TS * CW * 4;
+  static constexpr uint32_t GBYTES = GROWS * CW * 4;
+  static constexpr uint32_t STAGE_BYTES = XBYTES + GBYTES;
+  static constexpr size_t SMEM = 128 + STAGES * STAGE_BYTES + RED_BYTES + 64;
+  static_assert(STAGE_BYTES % 128 == 0 && XBYTES % 128 == 0, "TMA destinations 128 B aligned");
+  static_assert(STEPS % QS == 0, "step groups");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+}  // namespace tb
+
+// CTA holding flattened tile f when `total` tiles are split over P CTAs as
+// [k * total / P, (k + 1) * total / P).
+__host__ __device__ __forceinline__ int tile_owner(long long f, long long total, int P) {
+  return (int)(((f + 1) * P + total - 1) / total) - 1;
+}
+
+// Barrier among the correlation warps only.
+__device__ __forceinline__ void corr_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(tb::NW * 32) : "memory");
+}
+
+template <bool ACC, int STEPS_, int STAGES_>
+__global__ void __launch_bounds__(tb::THREADS, 1)
+    conv_bwd_tma_kernel(const __grid_constant__ CUtensorMap mX,
+                        const __grid_constant__ CUtensorMap mG, const float* __restrict__ w3,
+                        const float* __restrict__ w7, const float* __restrict__ w15,
+                        float* __restrict__ dx, float* __restrict__ parts, int T, int D, int nseg,
+                        int I, long long total, unsigned* err) {
+  rnet_dev::pdl_trigger();
+  using K = tb::Cfg<STEPS_, STAGES_>;
+  constexpr int CW = tb::CW, NW = tb::NW, STEPS = K::STEPS, WIN = K::WIN, TS = K::TS;
+  constexpr int STAGES = K::STAGES, RED_L = tb::RED_L, QS = tb::QS;
+  constexpr uint32_t XBYTES = K::XBYTES, STAGE_BYTES = K::STAGE_BYTES, RED_BYTES = tb::RED_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  float* red = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES);  // [RED_L][NW][CW]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + RED_BYTES);
+  uint64_t* empty = full + STAGES;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + STAGES);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool corr = warp >= NW;          // correlation warp (else dx warp)
+  const int r0 = (warp % NW) * STEPS;
+  const int P = gridDim.x, k = blockIdx.x;
+  const long long f_lo = (long long)k * total / P, f_hi = (long long)(k + 1) * total / P;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 2 * NW);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const bool producer = threadIdx.x == 0;
+  bool pok = true;  // producer still issuing
+  // Stage tile number n of this CTA (after its stage's previous tile, n -
+  // STAGES, has been released by every warp).
+  auto issue = [&](int n) {
+    const long long f = f_lo + n;
+    if (!pok || f >= f_hi) return;
+    const int s = n % STAGES;
+    if (!mbar_wait(&empty[s], ((n / STAGES) & 1) ^ 1, err, abort_flag)) {
+      pok = false;
+      return;
+    }
+    const int g = (int)(f / I), it = (int)(f % I);
+    uint8_t* st = smem + s * STAGE_BYTES;
+    mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+    tma_load_3d(st, &mX, &full[s], g * CW, (it % nseg) * TS, it / nseg);
+    tma_load_3d(st + XBYTES, &mG, &full[s], g * CW, (it % nseg) * TS, it / nseg);
+  };
+  if (producer) {
+    tma_prefetch_desc(&mX);
+    tma_prefetch_desc(&mG);
+    for (int n = 0; n < STAGES - 1; ++n) issue(n);
+  }
+
+  uint64_t W[15];  // dx warps: merged taps E[l]; correlation warps: C[l]
+  int cur_g = -1;
+  bool ok = true;
+  // Correlation warps: sum their C in warp order into slot k + g (each runs
+  // the same sequence of flushes, also after a failed wait).
+  auto flush = [&](int g) {
+    const int ct = threadIdx.x - NW * 32;  // thread index among correlation warps
+#pragma unroll
+    for (int l0 = 0; l0 < 15; l0 += RED_L) {
+      corr_sync();  // the previous round's readers are done
+#pragma unroll
+      for (int q = 0; q < RED_L; ++q)
+        reinterpret_cast<uint64_t*>(red)[(q * NW + warp - NW) * (CW / 2) + lane] = W[l0 + q];
+      corr_sync();
+      if (ct < RED_L * CW) {
+        const int q = ct / CW, cc = ct % CW;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) sum += red[(q * NW + w) * CW + cc];
+        if (g * CW + cc < D) parts[((size_t)(k + g) * 15 + l0 + q) * CW + cc] = sum;
+      }
+    }
+  };
+  int n = 0;
+  for (long long f = f_lo; f < f_hi; ++f, ++n) {
+    if (producer) issue(n + STAGES - 1);
+    __syncwarp();
+    const int g = (int)(f / I), it = (int)(f % I);
+    const int d = g * CW + 2 * lane;  // channels d, d + 1 (D % 4 == 0: both or neither)
+    const bool act = d < D;
+    if (g != cur_g) {
+      if (corr) {
+        if (cur_g >= 0) flush(cur_g);
+#pragma unroll
+        for (int l = 0; l < 15; ++l) W[l] = 0;
+      } else {
+#pragma unroll
+        for (int l = 0; l < 15; ++l) {
+          float e0 = 0.f, e1 = 0.f;
+          if (act) {
+            e0 = w15[(14 - l) * D + d];
+            e1 = w15[(14 - l) * D + d + 1];
+            if (l <= 6) {
+              e0 += w7[(6 - l) * D + d];
+              e1 += w7[(6 - l) * D + d + 1];
+            }
+            if (l <= 2) {
+              e0 += w3[(2 - l) * D + d];
+              e1 += w3[(2 - l) * D + d + 1];
+            }
+          }
+          W[l] = pk_make(e0, e1);
+        }
+      }
+      cur_g = g;
+    }
+    const int s = n % STAGES;
+    ok = ok && mbar_wait(&full[s], (n / STAGES) & 1, err, abort_flag);
+    if (ok) {
+      const uint64_t* sx = reinterpret_cast<const uint64_t*>(smem + s * STAGE_BYTES);
+      const uint64_t* sg = reinterpret_cast<const uint64_t*>(smem + s * STAGE_BYTES + XBYTES);
+      uint64_t gs[WIN];  // dS[tb + j], channel pair of this lane
+#pragma unroll
+      for (int j = 0; j < WIN; ++j) gs[j] = sg[(r0 + j) * (CW / 2) + lane];
+      if (corr) {
+#pragma unroll
+        for (int i = 0; i < STEPS; ++i) {
+          const uint64_t xv = sx[(r0 + i) * (CW / 2) + lane];  // zero past T
+#pragma unroll
+          for (int l = 0; l < 15; ++l) W[l] = pk_fma(xv, gs[i + l], W[l]);
+        }
+      } else {
+        const int b = it / nseg, tb = (it % nseg) * TS + r0;
+        const int nv = T - tb;  // valid steps of this warp (may be <= 0)
+        uint64_t* px = reinterpret_cast<uint64_t*>(dx + ((size_t)b * T + tb) * D + d);
+        // QS independent dx chains at a time
+#pragma unroll
+        for (int i0 = 0; i0 < STEPS; i0 += QS) {
+          uint64_t v[QS], prev[ACC ? QS : 1];  // ACC: the group's dx rows, loaded first
+          if (ACC) {
+#pragma unroll
+            for (int q = 0; q < QS; ++q)
+              prev[ACC ? q : 0] = act && i0 + q < nv ? px[(size_t)(i0 + q) * (D / 2)] : 0;
+          }
+#pragma unroll
+          for (int q = 0; q < QS; ++q) v[q] = 0;
+#pragma unroll
+          for (int l = 14; l >= 0; --l) {
+#pragma unroll
+            for (int q = 0; q < QS; ++q) v[q] = pk_fma(W[l], gs[i0 + q + l], v[q]);
+          }
+#pragma unroll
+          for (int q = 0; q < QS; ++q) {
+            const int i = i0 + q;
+            if (act && i < nv) {
+              uint64_t* p = px + (size_t)i * (D / 2);
+              *p = ACC ? pk_add(prev[ACC ? q : 0], v[q]) : v[q];
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  if (corr && cur_g >= 0) flush(cur_g);
+}
+
+// dw_K[k] += sum over the CTAs that worked on channel group g of their lag
+// sums (slot k + g, CTAs in order).
+__global__ void conv_wgrad_reduce_slots(const float* __restrict__ parts, int D, int I,
+                                        long long total, int P, float* __restrict__ dw3,
+                                        float* __restrict__ dw7, float* __restrict__ dw15) {
+  rnet_dev::pdl_trigger();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // over 15*D
+  if (i >= 15 * D) return;
+  const int l = i / D, d = i % D, g = d / tb::CW, cc = d % tb::CW;
+  const int k0 = tile_owner((long long)g * I, total, P);
+  const int k1 = tile_owner((long long)g * I + I - 1, total, P);
+  float s = 0.f;
+  for (int kk = k0; kk <= k1; kk += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      v[j] = kk + j <= k1 ? parts[((size_t)(kk + j + g) * 15 + l) * tb::CW + cc] : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (kk + j <= k1) s += v[j];
+  }
+  dw15[(14 - l) * D + d] += s;
+  if (l <= 6) dw7[(6 - l) * D + d] += s;
+  if (l <= 2) dw3[(2 - l) * D + d] += s;
+}
+
 int nparts_for(int B, int T, int D) {
   const int nseg = (T + TS - 1) / TS;
   const int groups = (D + CW - 1) / CW;
@@ -360,14 +607,80 @@ cudaError_t conv_fwd(const float* x, const float* w3, const float* w7, const flo
 }
 
 size_t conv_bwd_partials_floats(int B, int T, int D) {
-  return (size_t)nparts_for(B, T, D) * 15 * D;
+  const size_t v1 = (size_t)nparts_for(B, T, D) * 15 * D;
+  // TMA path: slots k + g, k < SMs, g < channel groups
+  const size_t v2 = (size_t)(rnet_gemm::num_sms() + (D + tb::CW - 1) / tb::CW) * 15 * tb::CW;
+  return v1 > v2 ? v1 : v2;
 }
+
+namespace {
+
+// The TMA path needs 16-byte aligned dS, x and dx (tensor-map bases, packed
+// stores); RNET_CONV_BWD_TILED=1 forces the cp.async path (A/B timing).
+bool tma_path_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("RNET_CONV_BWD_TILED");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
+
+template <bool ACC, int STEPS, int STAGES>
+cudaError_t launch_bwd_tma(const float* dS, const float* x, const float* w3, const float* w7,
+                           const float* w15, float* dx, float* dw3, float* dw7, float* dw15,
+                           float* parts, int B, int T, int D, cudaStream_t s, bool* done) {
+  using K = tb::Cfg<STEPS, STAGES>;
+  *done = false;
+  const int nseg = (T + K::TS - 1) / K::TS;
+  const int G = (D + tb::CW - 1) / tb::CW;
+  const int I = B * nseg;
+  const long long total = (long long)G * I;
+  const int P = (int)(total < rnet_gemm::num_sms() ? total : rnet_gemm::num_sms());
+  const uint64_t dims[3] = {(uint64_t)D, (uint64_t)T, (uint64_t)B};
+  const uint64_t strides[2] = {(uint64_t)D * 4, (uint64_t)T * D * 4};
+  const uint32_t box_x[3] = {tb::CW, (uint32_t)K::TS, 1};
+  const uint32_t box_g[3] = {tb::CW, (uint32_t)K::GROWS, 1};
+  CUtensorMap mX, mG;
+  if (!rnet_gemm::encode_map_f32(&mX, x, 3, dims, strides, box_x) ||
+      !rnet_gemm::encode_map_f32(&mG, dS, 3, dims, strides, box_g))
+    return cudaSuccess;  // not encodable: the caller takes the cp.async path
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(conv_bwd_tma_kernel<ACC, STEPS, STAGES>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)K::SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  conv_bwd_tma_kernel<ACC, STEPS, STAGES><<<P, tb::THREADS, K::SMEM, s>>>(
+      mX, mG, w3, w7, w15, dx, parts, T, D, nseg, I, total, rnet_status::device_error_word());
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  conv_wgrad_reduce_slots<<<(15 * D + 255) / 256, 256, 0, s>>>(parts, D, I, total, P, dw3, dw7,
+                                                               dw15);
+  *done = true;
+  return launched(2);
+}
+
+}  // namespace
 
 cudaError_t conv_bwd(const float* dS, const float* x, const float* w3, const float* w7,
                      const float* w15, float* dx, float* dw3, float* dw7, float* dw15,
                      float* partials, int B, int T, int D, int accumulate, cudaStream_t s) {
   if (B <= 0 || T <= 0) return cudaSuccess;
   if (D % 4) return cudaErrorInvalidValue;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(dS) | reinterpret_cast<uintptr_t>(x) |
+                         reinterpret_cast<uintptr_t>(dx)) & 15) == 0;
+  if (aligned && tma_path_enabled()) {
+    bool done = false;
+    cudaError_t e;
+    // 128-step tiles, 3 stages (64-step tiles with 5 stages measured slower)
+    e = accumulate ? launch_bwd_tma<true, 16, 3>(dS, x, w3, w7, w15, dx, dw3, dw7, dw15, partials,
+                                                 B, T, D, s, &done)
+                   : launch_bwd_tma<false, 16, 3>(dS, x, w3, w7, w15, dx, dw3, dw7, dw15, partials,
+                                                  B, T, D, s, &done);
+    if (e != cudaSuccess || done) return e;
+  }
   const int nseg = (T + TS - 1) / TS;
   const int np = nparts_for(B, T, D);
   dim3 grid((D + CW - 1) / CW, np);

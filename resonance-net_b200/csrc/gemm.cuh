@@ -6,6 +6,7 @@
 // (element (i,k) at p[k*ld + i]); both are consumed natively by TMA + UMMA
 // (kind::tf32 supports MN-major operands on sm_100a).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -59,6 +60,12 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
 
 // Number of SMs of the current device (cached).
 int num_sms();
+
+// fp32 tiled tensor map of `rank` (<= 5) dimensions, innermost first:
+// dims[i] elements, stride_bytes[i] between consecutive indices of dimension
+// i + 1, box[i] elements per copy; out-of-range elements read as zero.
+bool encode_map_f32(CUtensorMap* m, const float* base, int rank, const uint64_t* dims,
+                    const uint64_t* stride_bytes, const uint32_t* box);
 
 // Grow the split-K workspace of `stream` on the current device to at least
 // `floats` (call before capturing short-M GEMMs into a CUDA graph; calls made

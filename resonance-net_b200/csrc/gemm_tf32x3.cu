@@ -638,6 +638,24 @@ static bool make_map(CUtensorMap* m, const float* base, uint64_t inner, uint64_t
   return r == CUDA_SUCCESS;
 }
 
+bool encode_map_f32(CUtensorMap* m, const float* base, int rank, const uint64_t* dims,
+                    const uint64_t* stride_bytes, const uint32_t* box) {
+  auto enc = get_encode_fn();
+  if (!enc || rank < 1 || rank > 5) return false;
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) st[i] = stride_bytes[i];
+  }
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<float*>(base), d, st, bx,
+                   es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Which argument check or launch step failed last (thread-local).
 static thread_local const char* g_reason = "";
 const char* gemm_last_reason() { return g_reason; }

@@ -67,7 +67,10 @@ def test_rms_norm(rnet, orc, cuda, N, D):
     assert_close(_np(DW), dw0, what="rms dw")
 
 
-@pytest.mark.parametrize("B,T,D", [(2, 32, 64), (3, 100, 64), (4, 256, 512), (1, 5, 128)])
+# (1, 300, 100): channel tail and ragged last segment; (1, 5, 1024): fewer
+# tiles than SMs; (32, 256, 512): CTA tile ranges that straddle channel groups.
+@pytest.mark.parametrize("B,T,D", [(2, 32, 64), (3, 100, 64), (4, 256, 512), (1, 5, 128),
+                                   (1, 300, 100), (1, 5, 1024), (32, 256, 512)])
 @pytest.mark.parametrize("quirk", [1, 0])
 def test_causal_conv(rnet, orc, cuda, B, T, D, quirk):
     torch = cuda
