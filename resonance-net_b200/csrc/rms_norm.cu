@@ -11,6 +11,7 @@
 // stays high (D = 512 -> VPL 4).
 #include "common.cuh"
 #include "kernels.cuh"
+#include "status.h"
 
 namespace rnet_k {
 using namespace rnet_dev;
@@ -132,13 +133,20 @@ __global__ void __launch_bounds__(WARPS * 32)
 
 // Backward for D <= STAGED_MAX_D: persistent CTAs walk groups of WARPS rows
 // (one row per warp); the dy / x (/ dx when accumulating) rows of the next
-// group are copied global -> shared with cp.async while the current group is
-// computed, so loads stay in flight through the reductions and stores.
+// group are copied global -> shared while the current group is computed, so
+// loads stay in flight through the reductions and stores. A group's rows are
+// contiguous: thread 0 moves each array with one bulk copy (completion on the
+// stage's mbarrier), and the other threads do no address arithmetic.
 constexpr int STAGED_MAX_D = 512;
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
-               : "memory");
+// Untiled bulk copy global -> shared (16-byte aligned, size % 16 == 0), no
+// multicast; completes `bytes` on the mbarrier's transaction count.
+__device__ __forceinline__ void bulk_load(void* smem, const void* gmem, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem)), "l"(gmem), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 template <int VPL>
@@ -146,10 +154,12 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
     rms_bwd_staged_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                           const float* __restrict__ w, const float* __restrict__ rinv,
                           float* __restrict__ dx, float* __restrict__ dw, int rows, int D,
-                          int mode) {
+                          int mode, unsigned* err) {
   rnet_dev::pdl_trigger();
   // [2 stages][3 arrays][WARPS rows][D]
   extern __shared__ __align__(16) float sbuf[];
+  __shared__ uint64_t full[2];
+  __shared__ int abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = D >> 2;
   const int narr = mode == 1 ? 3 : 2;
@@ -157,23 +167,24 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
     return sbuf + ((size_t)(st * 3 + arr) * WARPS + wr) * D;
   };
   const int ngroups = (rows + WARPS - 1) / WARPS;
-  // stage group g into stage st: every thread copies 16 B pieces of the rows
+  if (threadIdx.x == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  // stage group g into stage st (thread 0: one bulk copy per array)
   auto stage = [&](int g, int st) {
-    if (g < ngroups) {
+    if (threadIdx.x == 0 && g < ngroups) {
       const int r0 = g * WARPS;
-      const int pieces = narr * WARPS * nv;
-      for (int q = threadIdx.x; q < pieces; q += WARPS * 32) {
-        const int arr = q / (WARPS * nv);
-        const int rem = q - arr * WARPS * nv;
-        const int wr = rem / nv, c = rem - wr * nv;
-        const int row = r0 + wr;
-        if (row < rows) {
-          const float* src = arr == 0 ? dy : (arr == 1 ? x : dx);
-          cp_async16(slot(st, arr, wr) + 4 * c, src + (size_t)row * D + 4 * c);
-        }
-      }
+      const int nr = rows - r0 < WARPS ? rows - r0 : WARPS;
+      const uint32_t bytes = (uint32_t)nr * D * 4;
+      mbar_arrive_expect_tx(&full[st], narr * bytes);
+      bulk_load(slot(st, 0, 0), dy + (size_t)r0 * D, bytes, &full[st]);
+      bulk_load(slot(st, 1, 0), x + (size_t)r0 * D, bytes, &full[st]);
+      if (narr == 3) bulk_load(slot(st, 2, 0), dx + (size_t)r0 * D, bytes, &full[st]);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
   };
   float4 acc[VPL];
 #pragma unroll
@@ -186,14 +197,14 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
     wv[j] = c < nv ? w4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   const float invD = 1.0f / (float)D;
-  int st = 0;
+  int st = 0, it = 0;
+  bool ok = true;  // a failed (timed-out) wait skips the compute, not the barriers
   stage(blockIdx.x, 0);
-  for (int g = blockIdx.x; g < ngroups; g += gridDim.x) {
+  for (int g = blockIdx.x; g < ngroups; g += gridDim.x, ++it) {
     stage(g + gridDim.x, st ^ 1);
-    asm volatile("cp.async.wait_group 1;" ::: "memory");
-    __syncthreads();
+    ok = ok && mbar_wait(&full[st], (it >> 1) & 1, err, &abort_flag);
     const int row = g * WARPS + warp;
-    if (row < rows) {
+    if (ok && row < rows) {
       const float4* dyr = reinterpret_cast<const float4*>(slot(st, 0, warp));
       const float4* xr = reinterpret_cast<const float4*>(slot(st, 1, warp));
       const float4* pr = reinterpret_cast<const float4*>(slot(st, 2, warp));
@@ -237,7 +248,6 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
     __syncthreads();  // stage `st` is refilled next iteration
     st ^= 1;
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   // per-warp partials (reusing the staging buffer), fixed-order sum over warps
   float* sdw = sbuf;
@@ -287,7 +297,8 @@ cudaError_t bwd_t(const float* dy, const float* x, const float* w, const float* 
     int grid = sm_count() * 2;  // two CTAs per SM (2 x 96 KB at D = 512)
     if (grid > ngroups) grid = ngroups;
     rms_bwd_staged_kernel<VPL><<<grid, WARPS * 32, smem, s>>>(dy, x, w, rinv, dx, dw, rows, D,
-                                                              mode);
+                                                              mode,
+                                                              rnet_status::device_error_word());
     return launched();
   }
   // >= 4 rows per warp so the dw partial flush is amortised
