@@ -44,6 +44,16 @@ int rnet_kernel_launches(unsigned long long* n);
  * bit 2 = TMEM allocation failed. Synchronises the device. */
 int rnet_device_error(unsigned* word, int clear);
 
+/* Self-test of the bounded-wait failure path (no reference counterpart): runs
+ * n_ctas CTAs shaped like the pipelined kernels (a TMEM-owning warp and
+ * waiters on an mbarrier) and waits on a barrier that nothing arrives on
+ * (arrive = 0) or that one thread arrives on (arrive = 1), with a wait limit
+ * of timeout_us. A run-out wait sets bit 0 of the device error word, the CTA
+ * frees its TMEM and returns; *timed_out_ctas receives how many CTAs gave up.
+ * Synchronises the device. */
+int rnet_selftest_bounded_wait(int arrive, unsigned timeout_us, int n_ctas,
+                               unsigned* timed_out_ctas);
+
 /* ------------------------------------------------------------------ GEMM engine
  * C[M,N] (op)= alpha * A[M,K] * B[N,K]^T on the tcgen05 3xTF32 engine.
  * a_mn_major = 0: A(i,k) = A[i*lda + k]; 1: A(i,k) = A[k*lda + i]  (same for B).
@@ -136,7 +146,9 @@ int rnet_cross_entropy_forward(const float* logits, const int* targets, float* l
  * device looks up that array's device address; make that first call before
  * any stream capture. All calls share the array, so calls that overlap on the
  * GPU (different streams, no ordering between them) race; calls ordered on
- * one stream are safe. Out-of-range targets are clamped to class 0 without
+ * one stream are safe. The address is cached per device, so do not use this
+ * entry point on a device after cudaDeviceReset. Out-of-range targets are
+ * clamped to class 0 without
  * setting the device error word. */
 int rnet_cross_entropy_forward_noalloc(const float* logits, const int* targets, float* loss,
                                        float* dlogits, int batch_seq, int vocab, void* stream);

@@ -44,9 +44,9 @@ def build() -> None:
     """Compile liboracle.so (and the reference harness when the reference
     sources are present in this container)."""
     subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
-    if os.path.isdir("/root/reference/src"):
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True,
-                       stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+    # skipped by the Makefile when the reference sources are absent
+    subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True,
+                   stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
 
 
 _lib = None
@@ -82,9 +82,15 @@ def param_count(cfg: OrcConfig) -> int:
     return int(lib().orc_param_count(ctypes.byref(cfg)))
 
 
-def train_step(cfg, params, tokens, targets, B, T, lr=3e-4, clip=1.0, quirk=1):
+def train_step(cfg, params, tokens, targets, B, T, lr=3e-4, clip=1.0, quirk=1, forced=None,
+               tau=0.0):
     """One reference training step. Returns dict(loss_sum, grads, params (updated),
-    topk_idx [L,N,k], topk_w [L,N,k], logits [N,V])."""
+    topk_idx [L,N,k], topk_w [L,N,k], logits [N,V], n_forced).
+
+    forced [L,N,k] (optional): on rows whose selection margin is below `tau`
+    and whose selected slot set differs from forced's, use forced's slots
+    (n_forced counts those rows) — the same discrete choices as the
+    implementation under test on near-ties, so the rest compares continuously."""
     params = np.array(params, dtype=np.float32, copy=True)
     n = param_count(cfg)
     grads = np.zeros(n, np.float32)
@@ -96,11 +102,15 @@ def train_step(cfg, params, tokens, targets, B, T, lr=3e-4, clip=1.0, quirk=1):
     loss = _F(0)
     tok = np.ascontiguousarray(tokens, np.int32)
     tgt = np.ascontiguousarray(targets, np.int32)
-    lib().orc_train_step(ctypes.byref(cfg), ptr(params), ptr(grads), ptr(tok), ptr(tgt), B, T,
-                         _F(lr), _F(clip), quirk, ctypes.byref(loss), ptr(idx), ptr(w),
-                         ptr(logits))
+    nf = _I(0)
+    fz = None if forced is None else np.ascontiguousarray(forced, np.int32)
+    if fz is not None:
+        assert fz.shape == idx.shape
+    lib().orc_train_step_forced(ctypes.byref(cfg), ptr(params), ptr(grads), ptr(tok), ptr(tgt),
+                                B, T, _F(lr), _F(clip), quirk, ctypes.byref(loss), ptr(idx),
+                                ptr(w), ptr(logits), ptr(fz), _F(tau), ctypes.byref(nf))
     return dict(loss_sum=loss.value, grads=grads, params=params, params_after=params,
-                topk_idx=idx, topk_w=w, logits=logits)
+                topk_idx=idx, topk_w=w, logits=logits, n_forced=nf.value)
 
 
 def forward(cfg, params, tokens, B, T):
@@ -156,4 +166,89 @@ def ref_lib() -> ctypes.CDLL:
         _ref.ref_get_logits.argtypes = [_P, _P, _I]
         _ref.ref_get_topk.argtypes = [_P, _P, _P, _I]
         _ref.ref_model_destroy.argtypes = [_P]
+        _ref.ref_model_init.restype = _P
+        _ref.ref_model_init.argtypes = [ctypes.POINTER(OrcConfig)]
+        _ref.ref_model_save.argtypes = [_P, ctypes.c_char_p]
+        _ref.ref_model_load_into.argtypes = [_P, ctypes.c_char_p]
+        _ref.ref_get_scores.argtypes = [_P, _I, _P, _I]
     return _ref
+
+
+REFMAIN_REF = os.path.join(HERE, "_ref", "refmain_ref")
+REFMAIN_RNET = os.path.join(HERE, "_ref", "refmain_rnet")
+
+
+class RefModel:
+    """The reference's own ResonanceNet (oracle/_ref/libref.so) on the GPU."""
+
+    def __init__(self, handle):
+        if not handle:
+            raise RuntimeError("reference model creation failed")
+        self.h = handle
+        self.lib = ref_lib()
+
+    @classmethod
+    def from_checkpoint(cls, path: str) -> "RefModel":
+        return cls(ref_lib().ref_model_load(path.encode()))
+
+    @classmethod
+    def init(cls, cfg: OrcConfig) -> "RefModel":
+        """Weights from the reference's own init_weights()."""
+        return cls(ref_lib().ref_model_init(ctypes.byref(cfg)))
+
+    def param_count(self) -> int:
+        return int(self.lib.ref_model_param_count(self.h))
+
+    def params(self) -> np.ndarray:
+        out = np.empty(self.param_count(), np.float32)
+        self.lib.ref_model_get_params(self.h, ptr(out))
+        return out
+
+    def grads(self) -> np.ndarray:
+        out = np.empty(self.param_count(), np.float32)
+        self.lib.ref_model_get_grads(self.h, ptr(out))
+        return out
+
+    def save(self, path: str) -> None:
+        assert self.lib.ref_model_save(self.h, path.encode()) == 1
+
+    def load(self, path: str) -> None:
+        assert self.lib.ref_model_load_into(self.h, path.encode()) == 1
+
+    def train_step(self, tok, tgt, B, T, lr=3e-4, clip=1.0) -> float:
+        tok = np.ascontiguousarray(tok, np.int32)
+        tgt = np.ascontiguousarray(tgt, np.int32)
+        return float(self.lib.ref_train_step(self.h, ptr(tok), ptr(tgt), B, T, lr, clip))
+
+    def topk(self, n_layers, N, k):
+        idx = np.zeros((n_layers, N, k), np.int32)
+        w = np.zeros((n_layers, N, k), np.float32)
+        self.lib.ref_get_topk(self.h, ptr(idx), ptr(w), N)
+        return idx, w
+
+    def scores(self, layer, N, S) -> np.ndarray:
+        out = np.empty((N, S), np.float32)
+        self.lib.ref_get_scores(self.h, layer, ptr(out), N)
+        return out
+
+    def logits(self, N, V) -> np.ndarray:
+        out = np.empty((N, V), np.float32)
+        self.lib.ref_get_logits(self.h, ptr(out), N)
+        return out
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.ref_model_destroy(self.h)
+            self.h = None
+
+
+def margins_from_scores(scores: np.ndarray, k: int = 2) -> np.ndarray:
+    """Selection margin per row, as topk_row in oracle.cpp defines it: the
+    smaller of (k-th minus (k+1)-th largest score) and the smallest gap among
+    the k selected."""
+    top = -np.partition(-scores, k, axis=1)[:, :k + 1]
+    top = -np.sort(-top, axis=1)
+    m = top[:, k - 1] - top[:, k]
+    for a in range(k - 1):
+        m = np.minimum(m, top[:, a] - top[:, a + 1])
+    return m

@@ -327,17 +327,48 @@ static void topk_row(const float* sr, int S, int k, int* idx, float* w, float* m
 
 // src/slot_memory.cu:79-119: q = x proj_q^T; scores = q K (K [D,S]);
 // top-k; r[d] = sum_j w_j V[d, idx_j]; y = r proj_out^T.
-void orc_slot_fwd(const float* x, float* y, const float* keys, const float* values,
-                  const float* pq, const float* pout, float* q, float* scores, int* idx,
-                  float* tw, int B, int T, int D, int S, int k) {
+//
+// `forced` (optional, [N, k]): on rows whose selection margin is below `tau`
+// and whose selected set differs from forced's, the forced slots are used
+// instead (softmax over their scores, in forced order); `n_forced` counts
+// them. Test infrastructure: lets a parity test give the oracle the same
+// discrete slot choices as the implementation under test on near-ties.
+static void slot_fwd_impl(const float* x, float* y, const float* keys, const float* values,
+                          const float* pq, const float* pout, float* q, float* scores, int* idx,
+                          float* tw, int B, int T, int D, int S, int k, const int* forced,
+                          float tau, int* n_forced) {
   const int N = B * T;
   linear(x, pq, q, N, D, D);
   std::vector<float> Kt = transpose(keys, D, S);  // [S, D]
   gemm_nt(N, S, D, q, Kt.data(), scores, false);
   std::vector<float> r((size_t)N * D);
-#pragma omp parallel for schedule(static)
+  int nf = 0;
+#pragma omp parallel for schedule(static) reduction(+ : nf)
   for (int n = 0; n < N; ++n) {
-    topk_row(scores + (size_t)n * S, S, k, idx + (size_t)n * k, tw + (size_t)n * k);
+    float margin = 0.0f;
+    topk_row(scores + (size_t)n * S, S, k, idx + (size_t)n * k, tw + (size_t)n * k,
+             forced ? &margin : nullptr);
+    if (forced && margin < tau) {
+      const int* fr = forced + (size_t)n * k;
+      bool same = true;
+      for (int a = 0; a < k; ++a) {
+        bool found = false;
+        for (int b = 0; b < k; ++b) found = found || fr[a] == idx[(size_t)n * k + b];
+        same = same && found;
+      }
+      if (!same) {
+        ++nf;
+        const float* sr = scores + (size_t)n * S;
+        float mx = sr[fr[0]];
+        for (int j = 1; j < k; ++j) mx = std::fmax(mx, sr[fr[j]]);
+        double e[8], sum = 0.0;
+        for (int j = 0; j < k; ++j) { e[j] = std::exp((double)sr[fr[j]] - mx); sum += e[j]; }
+        for (int j = 0; j < k; ++j) {
+          idx[(size_t)n * k + j] = fr[j];
+          tw[(size_t)n * k + j] = (float)(e[j] / sum);
+        }
+      }
+    }
     for (int d = 0; d < D; ++d) {
       double acc = 0.0;
       for (int j = 0; j < k; ++j)
@@ -346,6 +377,14 @@ void orc_slot_fwd(const float* x, float* y, const float* keys, const float* valu
     }
   }
   linear(r.data(), pout, y, N, D, D);
+  if (n_forced) *n_forced += nf;
+}
+
+void orc_slot_fwd(const float* x, float* y, const float* keys, const float* values,
+                  const float* pq, const float* pout, float* q, float* scores, int* idx,
+                  float* tw, int B, int T, int D, int S, int k) {
+  slot_fwd_impl(x, y, keys, values, pq, pout, q, scores, idx, tw, B, T, D, S, k, nullptr, 0.0f,
+                nullptr);
 }
 
 // src/slot_memory.cu:122-244: dr = dy proj_out; dproj_out += r^T dy (r
@@ -546,6 +585,11 @@ void orc_train_step(const OrcConfig* c, float* params, float* grads, const int* 
                     const int* targets, int B, int T, float lr, float clip, int quirk,
                     float* loss_sum, int* topk_out, float* topw_out, float* logits_out);
 
+void orc_train_step_forced(const OrcConfig* c, float* params, float* grads, const int* tokens,
+                           const int* targets, int B, int T, float lr, float clip, int quirk,
+                           float* loss_sum, int* topk_out, float* topw_out, float* logits_out,
+                           const int* forced, float tau, int* n_forced);
+
 // Backward only (no update): grads = d(loss_sum/N)/d params.
 void orc_grads(const OrcConfig* c, const float* params, float* grads, const int* tokens,
                const int* targets, int B, int T, int quirk, float* loss_sum);
@@ -560,7 +604,8 @@ namespace {
 
 void model_fwd_impl(const OrcConfig* c, const ModelP& P, const int* tokens, int B, int T,
                     float* logits, std::vector<LayerCache>* caches, std::vector<float>* hidden_out,
-                    std::vector<float>* fnormed, std::vector<float>* frms) {
+                    std::vector<float>* fnormed, std::vector<float>* frms,
+                    const int* forced = nullptr, float tau = 0.0f, int* n_forced = nullptr) {
   const int D = c->d_model, F = c->d_ff, S = c->n_slots, V = c->vocab_size, k = c->slot_top_k;
   const int N = B * T;
   const size_t NE = (size_t)N * D;
@@ -585,8 +630,9 @@ void model_fwd_impl(const OrcConfig* c, const ModelP& P, const int* tokens, int 
     C.n3.resize(NE); C.rms3.resize(N); C.q.resize(NE); C.scores.resize((size_t)N * S);
     C.idx.resize((size_t)N * k); C.tw.resize((size_t)N * k);
     orc_rms_norm_fwd(x.data(), W.n3, C.n3.data(), C.rms3.data(), N, D, c->rms_eps);
-    orc_slot_fwd(C.n3.data(), tmp.data(), W.keys, W.vals, W.pq, W.pout, C.q.data(),
-                 C.scores.data(), C.idx.data(), C.tw.data(), B, T, D, S, k);
+    slot_fwd_impl(C.n3.data(), tmp.data(), W.keys, W.vals, W.pq, W.pout, C.q.data(),
+                  C.scores.data(), C.idx.data(), C.tw.data(), B, T, D, S, k,
+                  forced ? forced + (size_t)l * N * k : nullptr, tau, n_forced);
     for (size_t i = 0; i < NE; ++i) x[i] += tmp[i];
     C.r3 = x;
     C.n4.resize(NE); C.rms4.resize(N); C.gc.resize((size_t)N * F); C.uc.resize((size_t)N * F);
@@ -726,13 +772,25 @@ void orc_sgd_step(const OrcConfig* c, float* params, const float* grads, float l
 void orc_train_step(const OrcConfig* c, float* params, float* grads, const int* tokens,
                     const int* targets, int B, int T, float lr, float clip, int quirk,
                     float* loss_sum, int* topk_out, float* topw_out, float* logits_out) {
+  orc_train_step_forced(c, params, grads, tokens, targets, B, T, lr, clip, quirk, loss_sum,
+                        topk_out, topw_out, logits_out, nullptr, 0.0f, nullptr);
+}
+
+// orc_train_step with near-tie slot choices taken from `forced` [L, N, k]
+// (see slot_fwd_impl); n_forced receives how many rows were overridden.
+void orc_train_step_forced(const OrcConfig* c, float* params, float* grads, const int* tokens,
+                           const int* targets, int B, int T, float lr, float clip, int quirk,
+                           float* loss_sum, int* topk_out, float* topw_out, float* logits_out,
+                           const int* forced, float tau, int* n_forced) {
   const int N = B * T, V = c->vocab_size;
+  if (n_forced) *n_forced = 0;
   ModelP P = bind(c, params);
   std::memset(grads, 0, sizeof(float) * orc_param_count(c));
   ModelP G = bind(c, grads);
   std::vector<LayerCache> caches;
   std::vector<float> hidden, fnormed, frms, logits((size_t)N * V), dl((size_t)N * V);
-  model_fwd_impl(c, P, tokens, B, T, logits.data(), &caches, &hidden, &fnormed, &frms);
+  model_fwd_impl(c, P, tokens, B, T, logits.data(), &caches, &hidden, &fnormed, &frms, forced,
+                 tau, n_forced);
   if (logits_out) std::memcpy(logits_out, logits.data(), sizeof(float) * logits.size());
   copy_topk(c, caches, N, topk_out, topw_out);
   float loss = 0.0f;

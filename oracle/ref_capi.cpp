@@ -189,3 +189,31 @@ void ref_forward_device(void* hp, const int* d_in, int B, int T) {
 int ref_sync(void) { return (int)cudaDeviceSynchronize(); }
 
 }  // extern "C"
+
+extern "C" {
+
+// A fresh reference model initialised by its own init_weights()
+// (src/resonance_net.cpp:180-216) for the given 40-byte ModelConfig.
+void* ref_model_init(const ModelConfig* cfg) {
+  Handle* h = new Handle();
+  if (!h->model.init(*cfg)) { delete h; return nullptr; }
+  return h;
+}
+
+// ResonanceNet::save (src/resonance_net.cpp:743-782). Returns 1 on success.
+int ref_model_save(void* hp, const char* path) { return ((Handle*)hp)->model.save(path) ? 1 : 0; }
+
+// ResonanceNet::load into an existing model (src/resonance_net.cpp:784-824).
+int ref_model_load_into(void* hp, const char* path) {
+  return ((Handle*)hp)->model.load(path) ? 1 : 0;
+}
+
+// Last forward's slot scores of one layer, [BS, n_slots] (scores_cache,
+// written by src/slot_memory.cu:79-119).
+void ref_get_scores(void* hp, int layer, float* host, int BS) {
+  Handle* h = (Handle*)hp;
+  cudaMemcpy(host, h->model.cache_[layer].scores_cache,
+             sizeof(float) * (size_t)BS * h->model.cfg_.n_slots, cudaMemcpyDeviceToHost);
+}
+
+}  // extern "C"

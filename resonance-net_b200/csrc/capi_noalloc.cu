@@ -28,7 +28,9 @@ constexpr size_t RNET_NOALLOC_CE_MAX_PARTIALS = 65536;
 static __device__ __align__(256) float g_ce_scratch[RNET_NOALLOC_CE_MAX_PARTIALS];
 
 // Per-device address of g_ce_scratch, looked up once per device with that
-// device current.
+// device current and cached for the life of the process. A cudaDeviceReset
+// unloads the module and may move the array, so this entry point must not be
+// used on a device after cudaDeviceReset has been called on it.
 float* scratch_address(int dev, cudaError_t* err) {
   static std::mutex mu;
   static float* addr[64] = {nullptr};

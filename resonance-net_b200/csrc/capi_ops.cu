@@ -51,6 +51,8 @@ struct Tmp {
 
 unsigned* ew() { return rnet_status::device_error_word(); }
 
+bool a16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
 }  // namespace
 
 extern "C" {
@@ -58,6 +60,9 @@ extern "C" {
 int rnet_rms_norm_forward(const float* x, const float* w, float* y, float* rms_cache,
                           int batch_seq, int dim, float eps, void* stream) {
   NEED(x && w && y, "rms_norm_forward: null pointer");
+  NEED(dim % 4 == 0 && dim <= 2048, "rms_norm_forward: dim must be a multiple of 4, <= 2048");
+  NEED(a16(x) && a16(w) && a16(y),
+       "rms_norm_forward: x, w and y must be 16-byte aligned (float4 rows)");
   CK(rnet_k::rms_norm_fwd(x, w, y, rms_cache, batch_seq, dim, eps, (cudaStream_t)stream));
   return RNET_OK;
 }
@@ -66,6 +71,9 @@ int rnet_rms_norm_backward(const float* dy, const float* x, const float* w,
                            const float* rms_cache, float* dx, float* dw, int batch_seq, int dim,
                            void* stream) {
   NEED(dy && x && w && rms_cache && dx && dw, "rms_norm_backward: null pointer");
+  NEED(dim % 4 == 0 && dim <= 2048, "rms_norm_backward: dim must be a multiple of 4, <= 2048");
+  NEED(a16(dy) && a16(x) && a16(w) && a16(dx),
+       "rms_norm_backward: dy, x, w and dx must be 16-byte aligned (bulk-copied rows)");
   CK(rnet_k::rms_norm_bwd(dy, x, w, rms_cache, dx, dw, batch_seq, dim, 0, (cudaStream_t)stream));
   return RNET_OK;
 }

@@ -110,19 +110,23 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, uint32_t rank
 // Bounded wait on an mbarrier phase. Returns false (and flags the error word)
 // if the phase did not complete within the timeout, or if another role of the
 // same CTA has already given up (abort flag in shared memory).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err,
-                                          volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, unsigned* err,
+                                              volatile int* abort_flag, uint64_t timeout_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > RNET_WAIT_TIMEOUT_NS) {
+    if (global_timer_ns() - t0 > timeout_ns) {
       *abort_flag = 1;
       if (err) atomicOr(err, ERR_WAIT_TIMEOUT);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err,
+                                          volatile int* abort_flag) {
+  return mbar_wait_for(bar, parity, err, abort_flag, RNET_WAIT_TIMEOUT_NS);
 }
 
 // ---------------------------------------------------------------- TMA

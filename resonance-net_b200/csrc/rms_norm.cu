@@ -174,9 +174,13 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
     fence_barrier_init();
   }
   __syncthreads();
-  // stage group g into stage st (thread 0: one bulk copy per array)
+  // Stage group g into stage st (thread 0: one bulk copy per array). After a
+  // timed-out wait (abort_flag) nothing new is issued; thread 0 counts the
+  // copies issued and consumed per stage so the abort path can drain them.
+  int issued[2] = {0, 0}, consumed[2] = {0, 0};
   auto stage = [&](int g, int st) {
-    if (threadIdx.x == 0 && g < ngroups) {
+    if (threadIdx.x == 0 && g < ngroups && !abort_flag) {
+      ++issued[st];
       const int r0 = g * WARPS;
       const int nr = rows - r0 < WARPS ? rows - r0 : WARPS;
       const uint32_t bytes = (uint32_t)nr * D * 4;
@@ -203,6 +207,7 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
   for (int g = blockIdx.x; g < ngroups; g += gridDim.x, ++it) {
     stage(g + gridDim.x, st ^ 1);
     ok = ok && mbar_wait(&full[st], (it >> 1) & 1, err, &abort_flag);
+    if (ok) ++consumed[st];
     const int row = g * WARPS + warp;
     if (ok && row < rows) {
       const float4* dyr = reinterpret_cast<const float4*>(slot(st, 0, warp));
@@ -249,6 +254,18 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
     st ^= 1;
   }
   __syncthreads();
+  if (abort_flag) {
+    // Failure path: wait (bounded) for the bulk copies still in flight into
+    // shared memory, then leave dw untouched; the error word reports it.
+    if (threadIdx.x == 0) {
+      volatile int no_abort = 0;
+      for (int b = 0; b < 2; ++b)
+        while (consumed[b] < issued[b] &&
+               mbar_wait_for(&full[b], consumed[b] & 1, nullptr, &no_abort, RNET_WAIT_TIMEOUT_NS))
+          ++consumed[b];
+    }
+    return;
+  }
   // per-warp partials (reusing the staging buffer), fixed-order sum over warps
   float* sdw = sbuf;
 #pragma unroll

@@ -60,3 +60,20 @@ def topk_sets_match(idx_a, idx_b, scores_margin=None, margin=1e-6):
         keep = np.asarray(scores_margin).reshape(-1) >= margin
         ok = ok | ~keep
     return ok
+
+
+def update_rel_err(p0, pa, pb) -> float:
+    """Norm-relative difference of two SGD updates (pa - p0 vs pb - p0),
+    ignoring elements where the two updated fp32 parameters are within one
+    ulp of each other: both sides round p - lr*g to fp32, so an update that
+    differs by 1e-6 relative can still land one ulp apart, which is a
+    rounding of the parameter, not a difference of the update."""
+    p0 = np.asarray(p0, np.float32)
+    pa = np.asarray(pa, np.float32)
+    pb = np.asarray(pb, np.float32)
+    ulp = np.spacing(np.maximum(np.abs(pa), np.abs(pb)))
+    diff = (pa.astype(np.float64) - pb.astype(np.float64))
+    diff[np.abs(diff) <= ulp] = 0.0
+    db = pb.astype(np.float64) - p0.astype(np.float64)
+    n = np.linalg.norm(db)
+    return float(np.linalg.norm(diff) / (n if n > 0 else 1.0))

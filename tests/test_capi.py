@@ -87,3 +87,24 @@ def test_zipf_bytes_distribution(rdata):
     assert 1.9 < top[0] / top[1] < 2.4
     assert counts.sum() == 200_000
     assert np.array_equal(rdata.zipf_bytes(1000, seed=7), rdata.zipf_bytes(1000, seed=7))
+
+
+def test_rms_norm_rejects_unaligned_pointers_without_launch(rnet):
+    """The RMSNorm kernels move rows as float4 / bulk copies: an offset view
+    (a slice starting at an odd element) is refused with RNET_ERR_ARG before
+    anything is launched, instead of faulting on the GPU."""
+    lib = rnet.lib()
+    buf = np.zeros(4 * 64 + 8, np.float32)
+    base = buf.ctypes.data + (-buf.ctypes.data) % 16  # 16-byte aligned address
+    n0 = rnet.kernel_launches()
+    ok = ctypes.c_void_p(base)
+    odd = ctypes.c_void_p(base + 4)
+    rc = lib.rnet_rms_norm_forward(odd, ok, ok, ok, 4, 64, ctypes.c_float(1e-6), None)
+    assert rc == -1 and "16-byte aligned" in lib.rnet_last_error().decode()
+    rc = lib.rnet_rms_norm_backward(ok, odd, ok, ok, ok, ok, 4, 64, None)
+    assert rc == -1 and "16-byte aligned" in lib.rnet_last_error().decode()
+    rc = lib.rnet_rms_norm_backward(ok, ok, ok, ok, odd, ok, 4, 64, None)
+    assert rc == -1
+    rc = lib.rnet_rms_norm_forward(ok, ok, ok, ok, 4, 62, ctypes.c_float(1e-6), None)
+    assert rc == -1 and "multiple of 4" in lib.rnet_last_error().decode()
+    assert rnet.kernel_launches() == n0

@@ -10,7 +10,8 @@ import os
 import numpy as np
 import pytest
 
-from helpers import FP32_TOL, assert_close, assert_grads_close, rel_err, topk_sets_match
+from helpers import (FP32_TOL, assert_close, assert_grads_close, rel_err, topk_sets_match,
+                     update_rel_err)
 
 pytestmark = pytest.mark.gpu
 
@@ -115,3 +116,49 @@ def test_train_step_bf16_vs_oracle(case, rnet, rdata, orc, cuda):
     assert u <= BF16_TOL, f"{case}: bf16 SGD update rel {u:.3e}"
     # the bf16 path really ran: its error is far above the fp32 path's
     assert g > 1e-5, f"{case}: gradient matches to {g:.1e}: bf16 arithmetic not in effect"
+
+
+def test_train_step_host_matches_device_step(rnet, rdata, orc, cuda):
+    """rnet_model_train_step_host (pinned host tokens in, loss out: the e2e
+    path bench.py times) against rnet_model_train_step on device buffers:
+    same kernels in the same order. The first step gives the same loss bit
+    for bit; parameters agree up to the summation order of the atomically
+    accumulated gradients (embedding and slot-table scatter), so updates
+    agree within 1e-5 and later losses within 1e-6. The first step also
+    matches the oracle."""
+    torch = cuda
+    c = dict(CASES["cfg_small"])
+    cfg, params, tok, tgt = _make(orc, rdata, c)
+    rcfg = _rcfg(rnet, cfg)
+    B, T = c["B"], c["T"]
+    a = rnet.Model(rcfg, device=0, reference_init=False)
+    b = rnet.Model(rcfg, device=0, reference_init=False)
+    a.set_params(params)
+    b.set_params(params)
+    d_in = torch.from_numpy(tok.reshape(-1)).cuda()
+    d_tgt = torch.from_numpy(tgt.reshape(-1)).cuda()
+    h_in = torch.from_numpy(tok.reshape(-1).copy()).pin_memory()
+    h_tgt = torch.from_numpy(tgt.reshape(-1).copy()).pin_memory()
+    loss = torch.zeros(1, device="cuda")
+    for i in range(3):
+        a.train_step(d_in, d_tgt, B, T, 3e-4, 1.0, loss)
+        a.synchronize()
+        lb = b.train_step_host(h_in, h_tgt, B, T, 3e-4, 1.0)
+        if i == 0:  # same parameters in: the same loss bit for bit
+            assert float(loss.item()) == lb, f"step {i}: loss {loss.item()} vs host {lb}"
+        else:
+            assert abs(float(loss.item()) - lb) <= 1e-6 * abs(lb), f"step {i}"
+        pa, pb = a.get_params(), b.get_params()
+        assert update_rel_err(params, pb, pa) <= 1e-5, f"step {i}"
+        if i == 0:
+            ref = orc.train_step(cfg, params, tok, tgt, B, T, 3e-4, 1.0, quirk=1)
+            assert abs(lb - ref["loss_sum"]) <= FP32_TOL * abs(ref["loss_sum"])
+            d = b.get_params().astype(np.float64) - params
+            assert rel_err(d, ref["params_after"] - params) <= FP32_TOL
+    # pageable (non-pinned) host buffers take the same path
+    lp = b.train_step_host(tok.reshape(-1).copy(), tgt.reshape(-1).copy(), B, T, 3e-4, 1.0)
+    a.train_step(d_in, d_tgt, B, T, 3e-4, 1.0, loss)
+    a.synchronize()
+    assert abs(float(loss.item()) - lp) <= 1e-6 * abs(lp)
+    a.close()
+    b.close()

@@ -42,7 +42,8 @@ def cta_group(request, rnet):
     rnet.call("rnet_gemm_set_cta_group", 0)
 
 
-@pytest.mark.parametrize("N,D", [(64, 64), (1000, 512), (7, 2048)])
+# (1003, 256) and (13, 512): staged backward with a last 8-row group of 3 and 5 rows
+@pytest.mark.parametrize("N,D", [(64, 64), (1000, 512), (7, 2048), (1003, 256), (13, 512)])
 def test_rms_norm(rnet, orc, cuda, N, D):
     torch = cuda
     r = _rng(N + D)

@@ -178,3 +178,24 @@ def test_oracle_matches_reference_golden(case, orc, rdata):
     d0 = out["params"].astype(np.float64) - g["params"]
     d1 = g["params_after"].astype(np.float64) - g["params"]
     assert rel_err(d0, d1) <= FP32_TOL
+
+
+def test_forced_selection_hook(orc, rdata):
+    """train_step(forced=...) overrides only rows inside the tie band whose
+    selected set differs; with its own choices nothing changes."""
+    cfg = orc.make_config(64, 1, 128, 64, 2, 256, seq_len=32)
+    params = rdata.init_params_normal(cfg, seed=1234)
+    tok, tgt = rdata.uniform_tokens(2, 32, seed=1)
+    a = orc.train_step(cfg, params, tok, tgt, 2, 32)
+    b = orc.train_step(cfg, params, tok, tgt, 2, 32, forced=a["topk_idx"], tau=1e30)
+    assert b["n_forced"] == 0
+    np.testing.assert_array_equal(a["grads"], b["grads"])
+    f = a["topk_idx"].copy()
+    f[0, 5] = [(f[0, 5, 0] + 1) % 64 if (f[0, 5, 0] + 1) % 64 != f[0, 5, 1] else
+               (f[0, 5, 0] + 2) % 64, f[0, 5, 1]]
+    c = orc.train_step(cfg, params, tok, tgt, 2, 32, forced=f, tau=0.0)
+    assert c["n_forced"] == 0  # outside the band: not overridden
+    d = orc.train_step(cfg, params, tok, tgt, 2, 32, forced=f, tau=1e30)
+    assert d["n_forced"] == 1
+    np.testing.assert_array_equal(d["topk_idx"][0, 5], f[0, 5])
+    assert not np.array_equal(d["grads"], a["grads"])
