@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--cg", type=int, default=0, help="--op: GEMM CTA group (0 auto, 1, 2)")
     ap.add_argument("--decode", action="store_true",
                     help="config 4: prefill + batched greedy decode instead of training")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="skip the config-4 decode object of the default (1-GPU) line")
     ap.add_argument("--streams", type=int, default=256, help="--decode: streams over all GPUs")
     ap.add_argument("--prompt", type=int, default=4096, help="--decode: prefill length")
     ap.add_argument("--gen", type=int, default=1024, help="--decode: decode steps")
@@ -350,8 +352,11 @@ def run_ours(args, rank, world, local):
     }
     if world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(importlib.import_module("resonance-net_b200.data"))
-    print(json.dumps(out), flush=True)
     _finish(pg, model, dist_h)
+    if world == 1 and not args.no_decode:
+        out["decode"] = decode_measure(rnet, rdata, torch, None, 0, 1, local, args.streams,
+                                       args.prompt, args.gen, args.warmup, args.steps)
+    print(json.dumps(out), flush=True)
 
 
 def _finish(pg, model, dist_h):
@@ -406,6 +411,7 @@ def run_reference(args, rank, world, local):
         clocks.mark(False)
         ck = clocks.stop()
         ms = e0.elapsed_time(e1)
+        dec = None if args.no_decode else reference_infer(R, h, torch, np)
         R.ref_model_destroy(h)
     finally:
         sys.stdout.flush()
@@ -426,7 +432,38 @@ def run_reference(args, rank, world, local):
                                       "CUDA build (unmodified sources, sm_100a) timed on the "
                                       "same B200, full config"},
            "clocks": ck}
+    if dec is not None:
+        out["decode"] = dec
     print(json.dumps(out), flush=True)
+
+
+def reference_infer(R, h, torch, np, prompt_len=5):
+    """The reference's only inference path, as-is (src/main.cpp:266-384
+    infer): batch 1, and for every generated token the context (prompt plus
+    tokens so far, up to seq_len = 256) is uploaded and the WHOLE prefix is
+    recomputed by ResonanceNet::forward; the last row's logits come back to
+    the host. Greedy choice stands in for its host top-p sampling (host-side,
+    not timed differently). Timed with CUDA events around the loop."""
+    S = CFG["seq_len"]
+    rng = np.random.default_rng(3)
+    ctx = list(rng.integers(32, 127, size=prompt_len))
+    logits = np.empty((S, CFG["vocab"]), np.float32)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    n = 0
+    while len(ctx) < S:
+        tok = np.ascontiguousarray(ctx, np.int32)
+        R.ref_forward(h, tok.ctypes.data, 1, len(ctx), logits.ctypes.data)
+        ctx.append(int(np.argmax(logits[len(ctx) - 1])))
+        n += 1
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    return {"metric": "decode tok/s, batch 1, full-prefix recompute (reference infer path)",
+            "value": round(n / (ms * 1e-3), 1), "unit": "tok/s", "tokens": n,
+            "context": f"{prompt_len}-token prompt grown to {S} (the checkpoint's seq_len cap)",
+            "ms_per_token": round(ms / n, 3)}
 
 
 def run_op(args):
@@ -537,23 +574,13 @@ def run_op(args):
                       "ms_per_call": round(e0.elapsed_time(e1) / args.steps, 4)}), flush=True)
 
 
-def run_decode(args, rank, world, local):
-    """Config 4: prefill of `streams` Zipf-byte prompts of length `prompt` through
-    the chunked scan, then `gen` greedy decode steps carrying the O(1) recurrent
-    state (graph-replayed step). Streams are split over the ranks with no
-    collective (strong scaling of a fixed stream count)."""
+def decode_measure(rnet, rdata, torch, pg, rank, world, local, streams, T, G, warmup, steps):
+    """Config 4 on this rank's share of `streams`: prefill of Zipf-byte prompts of
+    length T through the chunked scan, then G greedy decode steps carrying the
+    O(1) recurrent state (graph-replayed step). Returns the result dict on
+    rank 0 (None elsewhere)."""
     import numpy as np
-    import torch
-    rnet = importlib.import_module("resonance-net_b200")
-    rdata = importlib.import_module("resonance-net_b200.data")
-    torch.cuda.set_device(local)
-    pg = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-        pg = dist
-    M = args.streams // world
-    T, G = args.prompt, args.gen
+    M = streams // world
     cfg = rnet.ModelConfig.make(d_model=CFG["d_model"], n_layers=CFG["n_layers"],
                                 d_ff=CFG["d_ff"], n_slots=CFG["n_slots"], top_k=CFG["top_k"],
                                 vocab=CFG["vocab"], seq_len=T)
@@ -591,8 +618,8 @@ def run_decode(args, rank, world, local):
         barrier()
         return max_over_ranks(e0.elapsed_time(e1)) / reps
 
-    reps = max(1, min(args.steps, 3))
-    for _ in range(max(1, args.warmup)):
+    reps = max(1, min(steps, 3))
+    for _ in range(max(1, warmup)):
         dec.prefill(d_tok, T)
     dec.generate(8, d_out, True)  # captures the decode-step graph
     n0 = rnet.kernel_launches()
@@ -612,10 +639,10 @@ def run_decode(args, rank, world, local):
         dec.generate(G, d_out, True)
         h_out.copy_(d_out, non_blocking=True)
     ms_e2e = timed(e2e, 1)
+    dec.close()
+    model.close()
     if rank != 0:
-        if pg:
-            pg.destroy_process_group()
-        return
+        return None
     peaks = measured_peaks()
     # one decode step streams every weight once and reads + writes each
     # stream's state (14 conv rows + h per layer)
@@ -627,18 +654,18 @@ def run_decode(args, rank, world, local):
     D_, F_, S_, V_ = CFG["d_model"], CFG["d_ff"], CFG["n_slots"], CFG["vocab"]
     flops_tok = CFG["n_layers"] * (10 * D_ * D_ + 2 * D_ * S_ + 6 * D_ * F_) + 2 * D_ * V_
     tflops = M * flops_tok / (step_ms * 1e-3) / 1e12
-    out = {
-        "metric": "decode tok/s (d512 L8, 256 streams x 1024 greedy steps after a 4096-token prefill)",
-        "value": round(args.streams * G / (ms_decode * 1e-3), 1), "unit": "tok/s",
-        "n_gpus": world, "steps": 1, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "fp32 (3xTF32 tcgen05)", "data": "synthetic Zipf(1.1) byte prompts, N(0,0.02) weights",
+    return {
+        "metric": f"decode tok/s (d512 L8, {streams} streams x {G} greedy steps after a "
+                  f"{T}-token prefill)",
+        "value": round(streams * G / (ms_decode * 1e-3), 1), "unit": "tok/s",
+        "n_gpus": world, "ms_per_step": round(step_ms, 4),
+        "dtype": "fp32 (3xTF32 tcgen05)",
         "config": {"workload": "config 4: prefill + greedy decode", "model": "ResonanceNet d512 L8",
-                   "streams": args.streams, "streams_per_gpu": M, "prompt": T, "decode_steps": G,
+                   "streams": streams, "streams_per_gpu": M, "prompt": T, "decode_steps": G,
                    "parallelism": f"streams sharded over {world} GPU(s), no collective"},
-        "prefill": {"value": round(args.streams * T / (ms_prefill * 1e-3), 1), "unit": "tok/s",
+        "prefill": {"value": round(streams * T / (ms_prefill * 1e-3), 1), "unit": "tok/s",
                     "ms": round(ms_prefill, 3)},
-        "e2e": {"value": round(args.streams * G / (ms_e2e * 1e-3), 1), "unit": "generated tok/s",
+        "e2e": {"value": round(streams * G / (ms_e2e * 1e-3), 1), "unit": "generated tok/s",
                 "note": "prompt H2D + prefill + decode + tokens D2H",
                 "h2d_bytes_per_step": int(4 * M * T), "d2h_bytes_per_step": int(4 * M * G)},
         "gpu_launches": int(launches),
@@ -650,11 +677,35 @@ def run_decode(args, rank, world, local):
                      "ceiling_3xtf32": round(peaks["bf16"] / 6, 1),
                      "frac_of_3xtf32_ceiling": round(tflops / (peaks["bf16"] / 6), 4),
                      "flops_per_step": M * flops_tok,
-                     "hbm": {"achieved_GBps": round(hbm_gbs, 1), "frac": round(hbm_gbs / peaks["hbm"], 4),
+                     "hbm": {"achieved_GBps": round(hbm_gbs, 1),
+                             "frac": round(hbm_gbs / peaks["hbm"], 4),
                              "bytes_per_step": weight_bytes + state_bytes}},
+        "reference_note": "the reference has no recurrent decode: its only inference path "
+                          "(src/main.cpp:266-384 infer) recomputes the whole prefix at batch 1 "
+                          "for every token; bench.py --impl reference reports that reading "
+                          "as-is in its own line's 'decode' object",
         "clocks": ck,
     }
-    print(json.dumps(out), flush=True)
+
+
+def run_decode(args, rank, world, local):
+    """Config 4 alone (--decode): strong scaling of a fixed stream count."""
+    import torch
+    rnet = importlib.import_module("resonance-net_b200")
+    rdata = importlib.import_module("resonance-net_b200.data")
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        pg = dist
+    out = decode_measure(rnet, rdata, torch, pg, rank, world, local, args.streams, args.prompt,
+                         args.gen, args.warmup, args.steps)
+    if out is not None:
+        out.update({"steps": 1, "warmup": args.warmup, "higher_is_better": True,
+                    "scaling": "strong", "vs_baseline": None,
+                    "data": "synthetic Zipf(1.1) byte prompts, N(0,0.02) weights"})
+        print(json.dumps(out), flush=True)
     if pg:
         pg.destroy_process_group()
 

@@ -245,6 +245,16 @@ int rnet_decoder_step(rnet_decoder* d, const int* d_tokens);
 /* n_steps greedy steps (fed back on the device); d_out [n_steps, n_streams]
  * (device, may be NULL). use_graph = 1 replays one captured CUDA graph per step. */
 int rnet_decoder_generate(rnet_decoder* d, int n_steps, int* d_out, int use_graph);
+/* Next-token rule of prefill / step / generate: temperature <= 0 = greedy
+ * argmax (default); otherwise the reference infer loop's temperature + top-p
+ * sampling (src/main.cpp:327-360: softmax at `temperature`, probabilities
+ * sorted descending, smallest prefix reaching `top_p`, sample within it),
+ * computed on the device. The uniform for stream m at the sampled token's
+ * position pos is a splitmix64 hash of (seed, m, pos), so runs are
+ * reproducible and independent of batching; it is not the reference CLI's
+ * std::mt19937 stream. Ties in probability order by token id. */
+int rnet_decoder_set_sampling(rnet_decoder* d, float temperature, float top_p,
+                              unsigned long long seed);
 /* Device pointers to the current logits [n_streams, vocab] and next tokens
  * [n_streams], and the state buffer with its size per stream in floats. */
 int rnet_decoder_outputs(rnet_decoder* d, const float** d_logits, const int** d_next);

@@ -98,6 +98,7 @@ _SIGS = {
     "rnet_decoder_prefill": [_P, _P, _I],
     "rnet_decoder_step": [_P, _P],
     "rnet_decoder_generate": [_P, _I, _P, _I],
+    "rnet_decoder_set_sampling": [_P, _F, _F, ctypes.c_ulonglong],
     "rnet_decoder_outputs": [_P, ctypes.POINTER(_P), ctypes.POINTER(_P)],
     "rnet_decoder_state": [_P, ctypes.POINTER(_P), ctypes.POINTER(_SZ)],
     "rnet_decoder_outputs_host": [_P, _P, _P],
@@ -312,6 +313,10 @@ class Decoder:
 
     def step(self, d_tokens=None) -> None:
         check(lib().rnet_decoder_step(self.handle, _ptr(d_tokens)))
+
+    def set_sampling(self, temperature: float = 0.0, top_p: float = 1.0, seed: int = 0) -> None:
+        """Greedy (temperature 0) or temperature + top-p sampling on the device."""
+        check(lib().rnet_decoder_set_sampling(self.handle, temperature, top_p, seed))
 
     def generate(self, n_steps: int, d_out=None, use_graph: bool = True) -> None:
         check(lib().rnet_decoder_generate(self.handle, n_steps, _ptr(d_out), int(use_graph)))

@@ -276,6 +276,26 @@ int rnet_decoder_step(rnet_decoder* d, const int* d_tokens) {
   return d->m->e->decode_step(&d->d, d_tokens);
 }
 
+int rnet_decoder_set_sampling(rnet_decoder* d, float temperature, float top_p,
+                              unsigned long long seed) {
+  if (!d) return rnet_status::fail(RNET_ERR_ARG, "null decoder");
+  if (!(temperature >= 0.0f) || !(top_p > 0.0f && top_p <= 1.0f))
+    return rnet_status::fail(RNET_ERR_ARG,
+                             "rnet_decoder_set_sampling: need temperature >= 0, 0 < top_p <= 1");
+  if (d->m->e->config().vocab_size > 1024 && temperature > 0.0f)
+    return rnet_status::fail(RNET_ERR_UNSUPPORTED, "sampling supports vocab_size <= 1024");
+  RNET_TRY_CUDA(cudaStreamSynchronize(d->m->e->stream()));
+  d->d.temperature = temperature;
+  d->d.top_p = top_p;
+  d->d.seed = seed;
+  // the captured step has the sampling parameters baked in: capture again
+  if (d->d.exec) cudaGraphExecDestroy(d->d.exec);
+  if (d->d.graph) cudaGraphDestroy(d->d.graph);
+  d->d.exec = nullptr;
+  d->d.graph = nullptr;
+  return RNET_OK;
+}
+
 int rnet_decoder_generate(rnet_decoder* d, int n_steps, int* d_out, int use_graph) {
   if (!d || n_steps < 0) return rnet_status::fail(RNET_ERR_ARG, "bad argument");
   return d->m->e->generate(&d->d, n_steps, d_out, use_graph != 0);

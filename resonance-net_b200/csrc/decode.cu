@@ -122,6 +122,105 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int M, int V,
   if (pos_ptr && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(pos_ptr, 1);
 }
 
+// Counter-based uniform in [0, 1) with 24 random bits: splitmix64 of
+// (seed, stream, position). The same function is restated by the tests.
+__device__ __forceinline__ float sample_uniform(unsigned long long seed, int stream, int pos) {
+  unsigned long long z = seed + 0x9E3779B97F4A7C15ull * (1ull + (unsigned long long)stream) +
+                         0xD1B54A32D192ED03ull * (unsigned long long)(unsigned)pos;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+
+// Temperature + top-p (nucleus) sampling per row, the rule of the
+// reference's infer loop (src/main.cpp:327-360): p = exp((l - max) / T)
+// summed in index order and normalised; probabilities sorted descending
+// (ties: lower token first); cutoff = first prefix whose running sum reaches
+// top_p (all V if none does); r = u * (sum of the kept probabilities); the
+// token is the first in sorted order whose running sum reaches r. The sums
+// run sequentially in the reference's order (thread 0). One CTA per row,
+// blockDim = SORT_N >= V. u comes from sample_uniform(seed, row, position
+// of the sampled token) where that position is *pos_ptr + advance;
+// advance = 1 also advances *pos_ptr (decode step), 0 leaves it (prefill).
+constexpr int SORT_N = 1024;
+__global__ void __launch_bounds__(SORT_N) sample_topp_kernel(
+    const float* __restrict__ logits, int M, int V, float temperature, float top_p,
+    unsigned long long seed, int* __restrict__ tok, int* __restrict__ pos_ptr, int advance) {
+  rnet_dev::pdl_trigger();
+  __shared__ float p[SORT_N];
+  __shared__ int id[SORT_N];
+  __shared__ float red[32];
+  const int row = blockIdx.x, t = threadIdx.x, n = blockDim.x;
+  const float* l = logits + (size_t)row * V;
+  const float v = t < V ? l[t] : -INFINITY;
+  // row maximum
+  float m = rnet_dev::warp_max(v);
+  if ((t & 31) == 0) red[t >> 5] = m;
+  __syncthreads();
+  if (t < 32) {
+    float x = t < (n >> 5) ? red[t] : -INFINITY;
+    x = rnet_dev::warp_max(x);
+    if (t == 0) red[0] = x;
+  }
+  __syncthreads();
+  const float mx = red[0];
+  p[t] = t < V ? expf((v - mx) / temperature) : -1.0f;  // padding sorts last
+  id[t] = t;
+  __syncthreads();
+  if (t == 0) {
+    float sum = 0.0f;
+    for (int i = 0; i < V; ++i) sum += p[i];
+    red[1] = sum;
+  }
+  __syncthreads();
+  if (t < V) p[t] /= red[1];
+  __syncthreads();
+  // bitonic sort, descending by probability, ascending token on ties
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const int o = t ^ j;
+      if (o > t) {
+        const float pa = p[t], pb = p[o];
+        const int ia = id[t], ib = id[o];
+        const bool a_first = pa > pb || (pa == pb && ia < ib);
+        const bool desc = (t & k) == 0;
+        if (desc != a_first) {
+          p[t] = pb; p[o] = pa;
+          id[t] = ib; id[o] = ia;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if (t == 0) {
+    float cum = 0.0f;
+    int cutoff = V;
+    for (int i = 0; i < V; ++i) {
+      cum += p[i];
+      if (cum >= top_p) { cutoff = i + 1; break; }
+    }
+    float resum = 0.0f;
+    for (int i = 0; i < cutoff; ++i) resum += p[i];
+    const int at = *pos_ptr + advance;
+    const float r = sample_uniform(seed, row, at) * resum;
+    int pick = id[0];
+    cum = 0.0f;
+    for (int i = 0; i < cutoff; ++i) {
+      cum += p[i];
+      if (cum >= r) { pick = id[i]; break; }
+    }
+    tok[row] = pick;
+  }
+  // every row has read *pos_ptr before any CTA could advance it: the advance
+  // happens in a separate single-thread launch (see sample_rows)
+}
+
+__global__ void advance_pos_kernel(int* pos_ptr) {
+  rnet_dev::pdl_trigger();
+  if (threadIdx.x == 0) atomicAdd(pos_ptr, 1);
+}
+
 // h[r, f] = silu(gu[r, f]) * gu[r, F + f]  (gate | up rows of width 2F)
 __global__ void silu_mul_rows_kernel(const float* __restrict__ gu, float* __restrict__ h, int M,
                                      int F) {
@@ -271,6 +370,19 @@ cudaError_t last_rows(const float* x, float* out, int M, int T, int D, cudaStrea
 cudaError_t argmax_rows(const float* logits, int M, int V, int* tok, int* out, int* pos,
                         cudaStream_t s) {
   argmax_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(logits, M, V, tok, out, pos);
+  return launched();
+}
+
+cudaError_t sample_rows(const float* logits, int M, int V, float temperature, float top_p,
+                        unsigned long long seed, int* tok, int* pos, int advance, cudaStream_t s) {
+  if (temperature <= 0.0f) return argmax_rows(logits, M, V, tok, nullptr, advance ? pos : nullptr, s);
+  if (V > SORT_N) return cudaErrorInvalidValue;
+  int n = 32;
+  while (n < V) n <<= 1;
+  sample_topp_kernel<<<M, n, 0, s>>>(logits, M, V, temperature, top_p, seed, tok, pos, advance);
+  cudaError_t e = launched();
+  if (e != cudaSuccess || !advance) return e;
+  advance_pos_kernel<<<1, 32, 0, s>>>(pos);
   return launched();
 }
 

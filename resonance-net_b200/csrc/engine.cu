@@ -652,7 +652,8 @@ int Engine::prefill(Decoder* d, const int* d_tokens, int T) {
   MM(M, V, D, kmaj(d->n, D), kmaj(outw_, D), epi_store(d->logits, V), 0);
   CK(cudaMemcpyAsync(d->pos, &T, sizeof(int), cudaMemcpyHostToDevice, s));
   CK(cudaStreamSynchronize(s));  // &T is a stack value
-  CK(rnet_k::argmax_rows(d->logits, M, V, d->tok, nullptr, nullptr, s));
+  CK(rnet_k::sample_rows(d->logits, M, V, d->temperature, d->top_p, d->seed, d->tok, d->pos, 0,
+                         s));
   return RNET_OK;
 }
 
@@ -689,7 +690,8 @@ int Engine::decode_step(Decoder* d, const int* d_tokens) {
   }
   CK(rnet_k::rms_norm_fwd(d->x, fnorm_, d->n, nullptr, M, D, eps, s));
   MM(M, V, D, kmaj(d->n, D), kmaj(outw_, D), epi_store(d->logits, V), 0);
-  CK(rnet_k::argmax_rows(d->logits, M, V, d->tok, nullptr, d->pos, s));
+  CK(rnet_k::sample_rows(d->logits, M, V, d->temperature, d->top_p, d->seed, d->tok, d->pos, 1,
+                         s));
   return RNET_OK;
 }
 

@@ -79,6 +79,12 @@ struct Decoder {
   cudaGraphExec_t exec = nullptr;
   cudaGraph_t graph = nullptr;
   int graph_kernels = 0;
+  // next-token rule: greedy when temperature <= 0, else temperature + top-p
+  // sampling (src/main.cpp:327-360) with a counter-based uniform per
+  // (seed, stream, position)
+  float temperature = 0.0f;
+  float top_p = 1.0f;
+  unsigned long long seed = 0;
 };
 
 class Engine {

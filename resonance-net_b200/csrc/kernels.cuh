@@ -118,6 +118,12 @@ cudaError_t decode_extract_state(const float* n1, const float* h, float* ring, f
 cudaError_t last_rows(const float* x, float* out, int M, int T, int D, cudaStream_t s);
 cudaError_t argmax_rows(const float* logits, int M, int V, int* tok, int* out, int* pos,
                         cudaStream_t s);
+// Next token per row: greedy (temperature <= 0, as argmax_rows) or
+// temperature + top-p sampling with the reference infer loop's rule
+// (src/main.cpp:327-360); the uniform comes from (seed, row, position of the
+// sampled token = *pos + advance); advance = 1 advances *pos afterwards.
+cudaError_t sample_rows(const float* logits, int M, int V, float temperature, float top_p,
+                        unsigned long long seed, int* tok, int* pos, int advance, cudaStream_t s);
 
 // ---- optimizer (optimizer.cu) ---------------------------------------------
 // Global-norm clip + SGD over one flat buffer, no host synchronisation:

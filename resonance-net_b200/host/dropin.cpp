@@ -270,43 +270,30 @@ bool ResonanceNet::load(const std::string& path) {
 
 // Declared by the reference (include/resonance_net.h:82-83) but never
 // defined there. Here: prefill the prompt with the chunked scan, then one
-// recurrent step per token carrying the O(1) state; temperature <= 0 is
-// greedy, otherwise sampling from softmax(logits / temperature) with
-// std::mt19937(42).
+// recurrent step per token carrying the O(1) state, all on the device (the
+// steps replay one captured CUDA graph). temperature <= 0 is greedy;
+// otherwise the next token follows the reference infer loop's rule
+// (src/main.cpp:327-360: softmax at `temperature`, top-p 0.9 nucleus),
+// sampled on the device with a fixed seed (42).
 void ResonanceNet::generate(const int* prompt, int prompt_len, int* output, int max_tokens,
                             float temperature) {
   if (!model_ || prompt_len <= 0 || max_tokens <= 0) return;
   rnet_decoder* dec = nullptr;
   die(rnet_decoder_create(model_, 1, &dec), "generate: decoder");
+  die(rnet_decoder_set_sampling(dec, temperature > 0.f ? temperature : 0.f, 0.9f, 42ull),
+      "generate: sampling");
   int* d_tok = nullptr;
-  CUDA_CHECK(cudaMalloc(&d_tok, sizeof(int) * prompt_len));
+  CUDA_CHECK(cudaMalloc(&d_tok, sizeof(int) * (prompt_len > max_tokens ? prompt_len : max_tokens)));
   CUDA_CHECK(cudaMemcpy(d_tok, prompt, sizeof(int) * prompt_len, cudaMemcpyHostToDevice));
   die(rnet_decoder_prefill(dec, d_tok, prompt_len), "generate: prefill");
-  const int V = cfg_.vocab_size;
-  std::vector<float> logits(V);
-  std::vector<double> p(V);
-  std::mt19937 rng(42);
-  for (int i = 0; i < max_tokens; ++i) {
-    int next = 0;
-    die(rnet_decoder_outputs_host(dec, logits.data(), &next), "generate: outputs");
-    if (temperature > 0.f) {
-      const float mx = *std::max_element(logits.begin(), logits.end());
-      double sum = 0.0;
-      for (int v = 0; v < V; ++v) sum += (p[v] = std::exp((logits[v] - mx) / temperature));
-      std::uniform_real_distribution<double> u(0.0, sum);
-      const double r = u(rng);
-      double c = 0.0;
-      next = V - 1;
-      for (int v = 0; v < V; ++v) {
-        c += p[v];
-        if (c >= r) { next = v; break; }
-      }
-    }
-    output[i] = next;
-    if (i + 1 < max_tokens) {
-      CUDA_CHECK(cudaMemcpy(d_tok, &next, sizeof(int), cudaMemcpyHostToDevice));
-      die(rnet_decoder_step(dec, d_tok), "generate: step");
-    }
+  // the first token comes from the prefill; each further one from a step
+  int next = 0;
+  die(rnet_decoder_outputs_host(dec, nullptr, &next), "generate: outputs");
+  output[0] = next;
+  if (max_tokens > 1) {
+    die(rnet_decoder_generate(dec, max_tokens - 1, d_tok, 1), "generate: decode");
+    CUDA_CHECK(cudaMemcpy(output + 1, d_tok, sizeof(int) * (max_tokens - 1),
+                          cudaMemcpyDeviceToHost));
   }
   cudaFree(d_tok);
   rnet_decoder_destroy(dec);

@@ -77,3 +77,110 @@ def test_graph_replay_equals_eager(rnet, rdata, orc, cuda):
         m.close()
     np.testing.assert_array_equal(outs[0][0], outs[1][0])
     np.testing.assert_array_equal(outs[0][1], outs[1][1])
+
+
+# ------------------------------------------------------------------ sampling
+M64 = (1 << 64) - 1
+
+
+def sample_uniform(seed, stream, pos):
+    """Restatement of the device's counter-based uniform (splitmix64 of
+    seed, stream and the sampled token's position; 24 random bits)."""
+    z = (seed + 0x9E3779B97F4A7C15 * (1 + stream) + 0xD1B54A32D192ED03 * pos) & M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M64
+    z ^= z >> 31
+    return np.float32((z >> 40) * (1.0 / 16777216.0))
+
+
+def topp_sample(logits, temperature, top_p, u):
+    """src/main.cpp:327-360 restated in float32 with sequential sums; ties
+    in probability are ordered by token id. Returns (token, boundary gap):
+    the gap is how close r came to a running-sum boundary (tokens whose gap
+    is within float rounding may legitimately differ)."""
+    f = np.float32
+    mx = logits.max()
+    p = np.exp(((logits - mx) / f(temperature)).astype(f)).astype(f)
+    s = f(0)
+    for v in p:
+        s = f(s + v)
+    p = (p / s).astype(f)
+    order = sorted(range(len(p)), key=lambda i: (-p[i], i))
+    cum, cutoff = f(0), len(p)
+    for i, t in enumerate(order):
+        cum = f(cum + p[t])
+        if cum >= f(top_p):
+            cutoff = i + 1
+            break
+    resum = f(0)
+    for t in order[:cutoff]:
+        resum = f(resum + p[t])
+    r = f(u * resum)
+    cum, pick, gap = f(0), order[0], np.inf
+    for t in order[:cutoff]:
+        cum = f(cum + p[t])
+        gap = min(gap, abs(float(cum) - float(r)))
+        if cum >= r:
+            pick = t
+            break
+    return pick, gap
+
+
+def test_device_topp_sampling_matches_reference_rule(rnet, rdata, orc, cuda):
+    """Temperature 0.8 / top-p 0.9 (the reference CLI's settings) on 64
+    streams: every sampled token equals the reference rule applied to the
+    same logits with the same uniform, for the prefill's token and the next
+    steps (eager and graph-replayed)."""
+    torch = cuda
+    M, T, steps, seed = 64, 24, 6, 1234
+    cfg, _, params, prompt = _setup(rnet, rdata, orc, M, T, std=0.3, seed=8)
+    m = rnet.Model(cfg, device=0, reference_init=False)
+    m.set_params(params)
+    dec = rnet.Decoder(m, M)
+    dec.set_sampling(0.8, 0.9, seed)
+    dec.prefill(torch.from_numpy(prompt.reshape(-1)).cuda(), T)
+    checked = skipped = not_argmax = 0
+    for i in range(steps + 1):
+        lg, nx = dec.outputs_host()
+        for r in range(M):
+            want, gap = topp_sample(lg[r], 0.8, 0.9, sample_uniform(seed, r, T + i))
+            if gap < 1e-6:
+                skipped += 1
+                continue
+            checked += 1
+            not_argmax += int(nx[r] != lg[r].argmax())
+            assert nx[r] == want, f"step {i} stream {r}: device {nx[r]} vs rule {want}"
+        if i < steps:
+            dec.step(None)
+    assert checked >= 0.99 * M * (steps + 1), (checked, skipped)
+    # the graph-replayed steps sample the same tokens as eager steps
+    outs = []
+    for graph in (False, True):
+        d2 = rnet.Decoder(m, M)
+        d2.set_sampling(0.8, 0.9, seed)
+        d2.prefill(torch.from_numpy(prompt.reshape(-1)).cuda(), T)
+        out = torch.zeros(steps, M, dtype=torch.int32, device="cuda")
+        d2.generate(steps, out, use_graph=graph)
+        outs.append(out.cpu().numpy())
+        d2.close()
+    np.testing.assert_array_equal(outs[0], outs[1])
+    # sampling really samples: over all steps some tokens are not the argmax
+    assert not_argmax > 0
+    # back to greedy
+    dec.set_sampling(0.0, 1.0, 0)
+    dec.prefill(torch.from_numpy(prompt.reshape(-1)).cuda(), T)
+    lg, nx = dec.outputs_host()
+    np.testing.assert_array_equal(nx, lg.argmax(axis=1))
+    dec.close()
+    m.close()
+
+
+def test_sampling_argument_checks(rnet, rdata, orc, cuda):
+    cfg, _, params, _ = _setup(rnet, rdata, orc, 2, 8)
+    m = rnet.Model(cfg, device=0, reference_init=False)
+    dec = rnet.Decoder(m, 2)
+    for bad in ((-1.0, 0.9), (0.8, 0.0), (0.8, 1.5)):
+        with pytest.raises(rnet.RnetError):
+            dec.set_sampling(*bad, 0)
+    dec.close()
+    m.close()
