@@ -63,6 +63,15 @@ int rnet_gemm_f32(int M, int N, int K, const float* A, int lda, int a_mn_major, 
                   int ldb, int b_mn_major, float* C, int ldc, const float* R, int ldr, int op,
                   float alpha, void* stream);
 
+/* C[M,N] (op)= alpha * A[M,K] * B[N,K]^T with bf16 A and B (same majors as
+ * rnet_gemm_f32; row pitch a multiple of 8 elements, 16-byte aligned) on the
+ * tcgen05 kind::f16 path: bf16 tiles staged by TMA straight from memory, fp32
+ * accumulation, fp32 C. C16 (optional, op 0 / 2): also store the result as
+ * bf16 with row pitch ldc. No counterpart in the reference (fp32 only). */
+int rnet_gemm_bf16(int M, int N, int K, const void* A, int lda, int a_mn_major, const void* B,
+                   int ldb, int b_mn_major, float* C, int ldc, const float* R, int ldr, int op,
+                   float alpha, void* C16, void* stream);
+
 /* Tile shape selection of the GEMM engine for every later call in this
  * process: 0 = automatic (CTA pairs, one 256-row MMA over two SMs, whenever
  * M > 128; single-CTA 128-row tiles otherwise), 1 = always single-CTA,
@@ -187,9 +196,12 @@ int rnet_model_get_grads(rnet_model* m, float* host, size_t n);
 int rnet_model_params_updated(rnet_model* m);
 int rnet_model_set_conv_quirk(rnet_model* m, int on);
 /* GEMM arithmetic of the model: 0 = fp32-accurate (3xTF32 tcgen05, default),
- * 1 = bf16 operands with fp32 accumulation (one tcgen05 kind::f16 MMA per
- * product block; parity with fp32 within 2e-2). Parameters, gradients,
- * activations and the optimizer stay fp32. */
+ * 1 = bf16: every GEMM of the train step reads bf16 operands from memory
+ * (tcgen05 kind::f16, fp32 accumulation): a bf16 shadow of the fp32 master
+ * weights that the SGD update rewrites, and bf16 copies of the activations
+ * and gradients that feed GEMMs, written by their producers. Master weights,
+ * gradients, norms, scan, conv, slot selection and the optimizer stay fp32.
+ * Parity with fp32 within 2e-2. */
 int rnet_model_set_precision(rnet_model* m, int precision);
 int rnet_model_forward(rnet_model* m, const int* d_tokens, float* d_logits, int batch,
                        int seq_len);

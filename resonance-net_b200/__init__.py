@@ -47,6 +47,7 @@ _SIGS = {
     "rnet_device_error": [ctypes.POINTER(ctypes.c_uint), _I],
     "rnet_selftest_bounded_wait": [_I, ctypes.c_uint, _I, ctypes.POINTER(ctypes.c_uint)],
     "rnet_gemm_f32": [_I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _I, _P, _I, _I, _F, _P],
+    "rnet_gemm_bf16": [_I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _I, _P, _I, _I, _F, _P, _P],
     "rnet_gemm_set_cta_group": [_I],
     "rnet_gemm_set_precision": [_I],
     "rnet_rms_norm_forward": [_P, _P, _P, _P, _I, _I, _F, _P],

@@ -137,8 +137,7 @@ int rnet_model_set_precision(rnet_model* m, int precision) {
   CHECK_M(m);
   if (precision != 0 && precision != 1)
     return rnet_status::fail(RNET_ERR_ARG, "rnet_model_set_precision: expected 0 (fp32) or 1 (bf16)");
-  m->e->precision = precision;
-  return RNET_OK;
+  return m->e->set_precision(precision);
 }
 
 int rnet_model_forward(rnet_model* m, const int* d_tokens, float* d_logits, int batch,

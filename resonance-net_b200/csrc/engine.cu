@@ -26,6 +26,13 @@ namespace {
 
 Operand kmaj(const float* p, int ld) { return Operand{p, ld, false}; }
 Operand mnmaj(const float* p, int ld) { return Operand{p, ld, true}; }
+// fp32 operand, or its bf16 copy when `bf` (same shape and pitch)
+Operand kop(bool bf, const float* p, const __nv_bfloat16* h, int ld) {
+  return bf ? bf16_operand(h, ld, false) : kmaj(p, ld);
+}
+Operand mop(bool bf, const float* p, const __nv_bfloat16* h, int ld) {
+  return bf ? bf16_operand(h, ld, true) : mnmaj(p, ld);
+}
 
 Epilogue epi_store(float* C, int ldc) {
   Epilogue e;
@@ -64,6 +71,8 @@ Engine::~Engine() {
   cudaFree(grads_);
   cudaFree(KT_);
   cudaFree(VT_);
+  cudaFree(params16_);
+  cudaFree(KT16_);
   cudaFree(dKV_);
   for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
   cudaFree(scratch_);
@@ -176,7 +185,23 @@ int Engine::init(int device, bool reference_init) {
   return refresh_shadows();
 }
 
-int Engine::refresh_shadows() {
+int Engine::set_precision(int p) {
+  if (p != 0 && p != 1) return rnet_status::fail(RNET_ERR_ARG, "precision must be 0 or 1");
+  if (p == 1 && !params16_) {
+    const size_t KT = (size_t)cfg_.n_layers * cfg_.n_slots * cfg_.d_model;
+    CK(cudaMalloc(&params16_, P_ * sizeof(__nv_bfloat16)));
+    CK(cudaMalloc(&KT16_, KT * sizeof(__nv_bfloat16)));
+  }
+  precision = p;
+  return refresh_shadows();
+}
+
+int Engine::refresh_shadows() { return refresh_shadows_impl(false); }
+
+// Transposed key / value copies (and, in bf16 mode, the bf16 shadows of the
+// parameters — unless the SGD update has just written them — and of the
+// transposed keys) after a weight change.
+int Engine::refresh_shadows_impl(bool params16_current) {
   const int D = cfg_.d_model, S = cfg_.n_slots, L = cfg_.n_layers;
   // keys / values of all layers in one launch (keys and values are adjacent
   // in a layer's parameter range; layers are evenly spaced)
@@ -187,6 +212,10 @@ int Engine::refresh_shadows() {
       return rnet_status::fail(RNET_ERR_ARG, "refresh_shadows: unexpected parameter layout");
   CK(rnet_k::transpose_pairs(W_[0].keys, kv, layer, KT_, VT_, (size_t)S * D, L, D, S, 0,
                              stream_));
+  if (precision == 1) {
+    if (!params16_current) CK(rnet_k::to_bf16(params_, params16_, P_, stream_));
+    CK(rnet_k::to_bf16(KT_, KT16_, (size_t)L * S * D, stream_));
+  }
   return RNET_OK;
 }
 
@@ -214,7 +243,8 @@ int Engine::get_grads_host(float* h, size_t n) {
 }
 
 int Engine::ensure_capacity(int N, bool with_caches) {
-  if (N <= cap_N_ && (cap_caches_ || !with_caches)) return RNET_OK;
+  const bool bf = precision == 1;
+  if (N <= cap_N_ && (cap_caches_ || !with_caches) && (cap_bf16_ || !bf)) return RNET_OK;
   const size_t D = cfg_.d_model, F = cfg_.d_ff, S = cfg_.n_slots, V = cfg_.vocab_size;
   const size_t L = cfg_.n_layers, k = cfg_.slot_top_k;
   const size_t n = (size_t)N;
@@ -222,6 +252,10 @@ int Engine::ensure_capacity(int N, bool with_caches) {
   std::vector<std::pair<void**, size_t>> plan;  // (slot, bytes)
   act_.assign(nact, LayerAct{});
   auto f = [&](float** p, size_t cnt) { plan.push_back({(void**)p, cnt * sizeof(float)}); };
+  auto hb = [&](__nv_bfloat16** p, size_t cnt) {
+    if (bf) plan.push_back({(void**)p, cnt * sizeof(__nv_bfloat16)});
+    else *p = nullptr;
+  };
   for (size_t l = 0; l < nact; ++l) {
     LayerAct& a = act_[l];
     f(&a.n1, n * D); f(&a.n2, n * D); f(&a.n3, n * D); f(&a.n4, n * D);
@@ -232,7 +266,10 @@ int Engine::ensure_capacity(int N, bool with_caches) {
     f(&a.w, n * k);
     f(&a.r1, n * D); f(&a.r2, n * D); f(&a.r3, n * D);
     f(&a.G, n * F); f(&a.U, n * F); f(&a.H, n * F);
+    hb(&a.n2h, n * D); hb(&a.n3h, n * D); hb(&a.n4h, n * D); hb(&a.Sh, n * D);
+    hb(&a.Sqh, n * D); hb(&a.qh, n * D); hb(&a.rh, n * D); hb(&a.Hh, n * F);
   }
+  hb(&nfh_, n * D);
   f(&X_, (with_caches ? (L + 1) : 2) * n * D);
   f(&nf_, n * D);
   f(&rinvf_, n);
@@ -247,7 +284,10 @@ int Engine::ensure_capacity(int N, bool with_caches) {
     const size_t cp = rnet_k::conv_bwd_partials_floats(N, 1, D),
                  cep = rnet_k::ce_partials_floats(N) + 8;
     f(&conv_parts_, cp > cep ? cp : cep);
+    hb(&dlogitsh_, n * V); hb(&dXh_, n * D); hb(&dGUh_, 2 * n * F); hb(&dqh_, n * D);
+    hb(&dPZHh_, 2 * n * D);
   } else {
+    dlogitsh_ = dXh_ = dGUh_ = dqh_ = dPZHh_ = nullptr;
     dX_ = dsub_ = dS_ = dq_ = dr_ = dPZH_ = dGU_ = dnf_ = conv_parts_ = nullptr;
   }
   size_t total = 0;
@@ -266,6 +306,7 @@ int Engine::ensure_capacity(int N, bool with_caches) {
   }
   cap_N_ = N;
   cap_caches_ = with_caches;
+  cap_bf16_ = bf;
   have_cache_ = false;
   return RNET_OK;
 }
@@ -352,6 +393,7 @@ int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B,
   const float* KT = KT_ + (size_t)l * S * D;
   const float* VT = VT_ + (size_t)l * S * D;
   const double ND4 = 4.0 * N * D;
+  const bool bf = precision == 1;
   // 1. multi-scale causal conv (reference layer_forward :287-299)
   // Residual sums are seeded by the kernel that already holds the residual
   // row (RMSNorm input copy, scan second output) and the GEMM accumulates
@@ -361,43 +403,60 @@ int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B,
   PROF(PK_CONV_FWD, 50.0 * N * D, (conv_quirk ? 3 : 2) * ND4,
        rnet_k::conv_fwd(a.n1, w.c3, w.c7, w.c15, a.S, conv_quirk ? a.Sq : nullptr, nullptr,
                         nullptr, B, T, D, s));
-  MM_RES(N, D, D, kmaj(a.S, D), kmaj(w.mix, D), a.r1);
+  if (bf) {
+    PROF(PK_OTHER, 0, 6.0 * N * D, rnet_k::to_bf16(a.S, a.Sh, (size_t)N * D, s));
+    if (train && conv_quirk)
+      PROF(PK_OTHER, 0, 6.0 * N * D, rnet_k::to_bf16(a.Sq, a.Sqh, (size_t)N * D, s));
+  }
+  MM_RES(N, D, D, kop(bf, a.S, a.Sh, D), kop(bf, w.mix, bf ? h16(w.mix) : nullptr, D), a.r1);
   // 2. MinGRU (:301-313): P = n2 [Wz;Wh]^T, fused gate + scan + residual
-  PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(a.r1, w.n2, a.n2, a.rinv2, N, D, eps, s));
-  MM(N, 2 * D, D, kmaj(a.n2, D), kmaj(w.Wz, D), epi_store(a.P, 2 * D), 0);
+  PROF(PK_RMS_FWD, 0, 2 * ND4,
+       rnet_k::rms_norm_fwd(a.r1, w.n2, a.n2, a.rinv2, N, D, eps, s, nullptr, a.n2h));
+  MM(N, 2 * D, D, kop(bf, a.n2, a.n2h, D), kop(bf, w.Wz, bf ? h16(w.Wz) : nullptr, D),
+     epi_store(a.P, 2 * D), 0);
   // training keeps e = h~ - h_prev (all the backward needs), prefill keeps h
   PROF(PK_SCAN_FWD, 0, 7 * ND4,
        rnet_k::gru_scan_fwd(a.P, a.P + D, 2 * D, w.bz, w.bh, a.z, a.h, nullptr, a.r1, a.r2, B, T,
                             D, s, train, a.r3));
   // 3. slot memory (:315-330)
-  PROF(PK_RMS_FWD, 0, 2 * ND4, rnet_k::rms_norm_fwd(a.r2, w.n3, a.n3, a.rinv3, N, D, eps, s));
-  MM(N, D, D, kmaj(a.n3, D), kmaj(w.pq, D), epi_store(a.q, D), 0);
+  PROF(PK_RMS_FWD, 0, 2 * ND4,
+       rnet_k::rms_norm_fwd(a.r2, w.n3, a.n3, a.rinv3, N, D, eps, s, nullptr, a.n3h));
+  {
+    Epilogue e = epi_store(a.q, D);
+    e.C16 = bf ? a.qh : nullptr;
+    MM(N, D, D, kop(bf, a.n3, a.n3h, D), kop(bf, w.pq, bf ? h16(w.pq) : nullptr, D), e, 0);
+  }
   if (k == 2) {
     Epilogue e;
     e.kind = EPI_TOP2;
     e.topk_idx = a.idx;
     e.topk_w = a.w;
-    MM(N, S, D, kmaj(a.q, D), kmaj(KT, D), e, 0);
+    MM(N, S, D, kop(bf, a.q, a.qh, D),
+       kop(bf, KT, bf ? KT16_ + (size_t)l * S * D : nullptr, D), e, 0);
   } else {
     MM(N, S, D, kmaj(a.q, D), kmaj(KT, D), epi_store(scores_, S), 0);
     PROF(PK_OTHER, 0, 4.0 * N * S, rnet_k::topk_rows(scores_, a.idx, a.w, N, S, k, s));
   }
   PROF(PK_SLOT_GATHER, 2.0 * k * N * D, (1 + k) * ND4,
        rnet_k::slot_gather(a.idx, a.w, VT, a.r, N, D, S, k, err, s));
-  MM_RES(N, D, D, kmaj(a.r, D), kmaj(w.pout, D), a.r3);
+  if (bf) PROF(PK_OTHER, 0, 6.0 * N * D, rnet_k::to_bf16(a.r, a.rh, (size_t)N * D, s));
+  MM_RES(N, D, D, kop(bf, a.r, a.rh, D), kop(bf, w.pout, bf ? h16(w.pout) : nullptr, D), a.r3);
   // 4. SwiGLU FFN (:332-342): paired gate|up tiles, SiLU*up in the epilogue
-  PROF(PK_RMS_FWD, 0, 3 * ND4, rnet_k::rms_norm_fwd(a.r3, w.n4, a.n4, a.rinv4, N, D, eps, s, Xn));
+  PROF(PK_RMS_FWD, 0, 3 * ND4,
+       rnet_k::rms_norm_fwd(a.r3, w.n4, a.n4, a.rinv4, N, D, eps, s, Xn, a.n4h));
   {
     Epilogue e;
     e.kind = EPI_SWIGLU_FWD;
     e.G = a.G;
     e.U = a.U;
     e.H = a.H;
+    e.H16 = bf ? a.Hh : nullptr;
     e.ldf = F;
-    MM(N, F, D, kmaj(a.n4, D), kmaj(w.gate, D), e, F);  // 2*N*F*D each for gate and up
+    MM(N, F, D, kop(bf, a.n4, a.n4h, D), kop(bf, w.gate, bf ? h16(w.gate) : nullptr, D), e,
+       F);  // 2*N*F*D each for gate and up
     if (prof_on_) prof_.back().flops *= 2.0;
   }
-  MM_RES(N, D, F, kmaj(a.H, F), kmaj(w.down, F), Xn);
+  MM_RES(N, D, F, kop(bf, a.H, a.Hh, F), kop(bf, w.down, bf ? h16(w.down) : nullptr, F), Xn);
   return RNET_OK;
 }
 
@@ -419,8 +478,11 @@ int Engine::forward(const int* d_tokens, float* d_logits, int B, int T) {
     if (rc) return rc;
   }
   const float* XL = caches ? X_ + (size_t)cfg_.n_layers * ND : X_ + (size_t)(cfg_.n_layers & 1) * ND;
-  PROF(PK_RMS_FWD, 0, 8.0 * ND, rnet_k::rms_norm_fwd(XL, fnorm_, nf_, rinvf_, N, D, cfg_.rms_eps, s));
-  MM(N, V, D, kmaj(nf_, D), kmaj(outw_, D), epi_store(d_logits, V), 0);
+  const bool bf = precision == 1;
+  PROF(PK_RMS_FWD, 0, 8.0 * ND,
+       rnet_k::rms_norm_fwd(XL, fnorm_, nf_, rinvf_, N, D, cfg_.rms_eps, s, nullptr, nfh_));
+  MM(N, V, D, kop(bf, nf_, nfh_, D), kop(bf, outw_, bf ? h16(outw_) : nullptr, D),
+     epi_store(d_logits, V), 0);
   have_cache_ = caches;
   last_B_ = B;
   last_T_ = T;
@@ -433,11 +495,14 @@ int Engine::head_backward(const float* d_dlogits, int N) {
   unsigned* err = rnet_status::device_error_word();
   cudaStream_t s = stream_;
   // src/resonance_net.cpp:428-442
-  MM(N, D, V, kmaj(d_dlogits, V), mnmaj(outw_, D), epi_store(dnf_, D), 0);
-  MM(V, D, N, mnmaj(d_dlogits, V), mnmaj(nf_, D), epi_accum(g_outw_, D), 0);
+  const bool bf = precision == 1;
+  if (bf) PROF(PK_OTHER, 0, 6.0 * N * V, rnet_k::to_bf16(d_dlogits, dlogitsh_, (size_t)N * V, s));
+  MM(N, D, V, kop(bf, d_dlogits, dlogitsh_, V), mop(bf, outw_, bf ? h16(outw_) : nullptr, D),
+     epi_store(dnf_, D), 0);
+  MM(V, D, N, mop(bf, d_dlogits, dlogitsh_, V), mop(bf, nf_, nfh_, D), epi_accum(g_outw_, D), 0);
   const float* XL = X_ + (size_t)cfg_.n_layers * N * D;
   PROF(PK_RMS_BWD, 0, 12.0 * N * D,
-       rnet_k::rms_norm_bwd(dnf_, XL, fnorm_, rinvf_, dX_, g_fnorm_, N, D, 0, s));
+       rnet_k::rms_norm_bwd(dnf_, XL, fnorm_, rinvf_, dX_, g_fnorm_, N, D, 0, s, dXh_));
   return RNET_OK;
 }
 
@@ -452,6 +517,8 @@ int Engine::layer_backward(int l, int B, int T) {
   float* dKT = dKV_ + (size_t)l * 2 * S * D;
   float* dVT = dKT + (size_t)S * D;
   const double ND4 = 4.0 * N * D;
+  const bool bf = precision == 1;
+  auto W16 = [&](const float* p) { return bf ? h16(p) : nullptr; };
   // Weight-gradient GEMMs go to the side stream: fork() when their inputs are
   // ready on the main stream, join() before the main stream overwrites one
   // of those inputs (dX_ by the RMSNorm backward; dGU_ / dq_ / dPZH_ / dS_
@@ -471,50 +538,60 @@ int Engine::layer_backward(int l, int B, int T) {
   // gradient in place (a fused epilogue measured 4x slower: its cache reads
   // have too little memory-level parallelism in four epilogue warps)
   CK(fork());
-  MM_W(D, F, N, mnmaj(dX_, D), mnmaj(a.H, F), epi_accum(g.down, F));
-  MM(N, F, D, kmaj(dX_, D), mnmaj(w.down, F), epi_store(dGU_, 2 * F), 0);
+  MM_W(D, F, N, mop(bf, dX_, dXh_, D), mop(bf, a.H, a.Hh, F), epi_accum(g.down, F));
+  MM(N, F, D, kop(bf, dX_, dXh_, D), mop(bf, w.down, W16(w.down), F), epi_store(dGU_, 2 * F), 0);
   PROF(PK_OTHER, 0, 5.0 * 4 * N * F,
        rnet_k::swiglu_bwd_pointwise(dGU_, 2 * F, a.G, a.U, N, F, s));
+  if (bf) PROF(PK_OTHER, 0, 12.0 * N * F, rnet_k::to_bf16(dGU_, dGUh_, 2 * (size_t)N * F, s));
   CK(fork());
-  MM_W(2 * F, D, N, mnmaj(dGU_, 2 * F), mnmaj(a.n4, D), epi_accum(g.gate, D));
-  MM(N, D, 2 * F, kmaj(dGU_, 2 * F), mnmaj(w.gate, D), epi_store(dsub_, D), 0);
+  MM_W(2 * F, D, N, mop(bf, dGU_, dGUh_, 2 * F), mop(bf, a.n4, a.n4h, D), epi_accum(g.gate, D));
+  MM(N, D, 2 * F, kop(bf, dGU_, dGUh_, 2 * F), mop(bf, w.gate, W16(w.gate), D),
+     epi_store(dsub_, D), 0);
   CK(join());
-  PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, a.r3, w.n4, a.rinv4, dX_, g.n4, N, D, 1, s));
+  PROF(PK_RMS_BWD, 0, 4 * ND4,
+       rnet_k::rms_norm_bwd(dsub_, a.r3, w.n4, a.rinv4, dX_, g.n4, N, D, 1, s, dXh_));
   // 3. slot memory (:492-510, src/slot_memory.cu:171-244) — sparse top-k path
   CK(fork());
-  MM_W(D, D, N, mnmaj(dX_, D), mnmaj(a.r, D), epi_accum(g.pout, D));
-  MM(N, D, D, kmaj(dX_, D), mnmaj(w.pout, D), epi_store(dr_, D), 0);
+  MM_W(D, D, N, mop(bf, dX_, dXh_, D), mop(bf, a.r, a.rh, D), epi_accum(g.pout, D));
+  MM(N, D, D, kop(bf, dX_, dXh_, D), mop(bf, w.pout, W16(w.pout), D), epi_store(dr_, D), 0);
   CK(cudaMemsetAsync(dKT, 0, 2 * (size_t)S * D * sizeof(float), s));  // dKT and dVT
   PROF(PK_SLOT_SPARSE_BWD, 8.0 * k * N * D, (3 + 4 * k) * ND4,
        rnet_k::slot_sparse_bwd(dr_, a.idx, a.w, VT_ + (size_t)l * S * D, KT_ + (size_t)l * S * D,
                                a.q, dq_, dVT, dKT, N, D, S, k, err, s));
+  if (bf) PROF(PK_OTHER, 0, 6.0 * N * D, rnet_k::to_bf16(dq_, dqh_, (size_t)N * D, s));
   CK(fork());
-  MM_W(D, D, N, mnmaj(dq_, D), mnmaj(a.n3, D), epi_accum(g.pq, D));
+  MM_W(D, D, N, mop(bf, dq_, dqh_, D), mop(bf, a.n3, a.n3h, D), epi_accum(g.pq, D));
   // dKT, dVT are adjacent [S, D] blocks of consecutive layers: both into
   // the gradient's keys / values in one launch
   PROF(PK_OTHER, 0, 32.0 * S * D,
        rnet_k::transpose_pairs(dKT, (size_t)S * D, 0, g.keys, g.vals, 0, 1, S, D, 1, s));
-  MM(N, D, D, kmaj(dq_, D), mnmaj(w.pq, D), epi_store(dsub_, D), 0);
+  MM(N, D, D, kop(bf, dq_, dqh_, D), mop(bf, w.pq, W16(w.pq), D), epi_store(dsub_, D), 0);
   CK(join());
-  PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, a.r2, w.n3, a.rinv3, dX_, g.n3, N, D, 1, s));
+  PROF(PK_RMS_BWD, 0, 4 * ND4,
+       rnet_k::rms_norm_bwd(dsub_, a.r2, w.n3, a.rinv3, dX_, g.n3, N, D, 1, s, dXh_));
   // 2. MinGRU (:512-528, src/min_gru.cu:128-191)
   PROF(PK_SCAN_BWD, 0, 5 * ND4,
        rnet_k::gru_scan_bwd(dX_, a.z, a.h, nullptr, 0, nullptr, dPZH_, dPZH_ + D, 2 * D, g.bz,
                             g.bh, B, T, D, s));
+  if (bf) PROF(PK_OTHER, 0, 12.0 * N * D, rnet_k::to_bf16(dPZH_, dPZHh_, 2 * (size_t)N * D, s));
   CK(fork());
-  MM_W(2 * D, D, N, mnmaj(dPZH_, 2 * D), mnmaj(a.n2, D), epi_accum(g.Wz, D));
-  MM(N, D, 2 * D, kmaj(dPZH_, 2 * D), mnmaj(w.Wz, D), epi_store(dsub_, D), 0);
+  MM_W(2 * D, D, N, mop(bf, dPZH_, dPZHh_, 2 * D), mop(bf, a.n2, a.n2h, D), epi_accum(g.Wz, D));
+  MM(N, D, 2 * D, kop(bf, dPZH_, dPZHh_, 2 * D), mop(bf, w.Wz, W16(w.Wz), D),
+     epi_store(dsub_, D), 0);
   CK(join());
-  PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, a.r1, w.n2, a.rinv2, dX_, g.n2, N, D, 1, s));
+  PROF(PK_RMS_BWD, 0, 4 * ND4,
+       rnet_k::rms_norm_bwd(dsub_, a.r1, w.n2, a.rinv2, dX_, g.n2, N, D, 1, s, dXh_));
   // 1. causal conv (:530-545, src/causal_conv.cu:132-190)
   CK(fork());
-  MM_W(D, D, N, mnmaj(dX_, D), mnmaj(conv_quirk ? a.Sq : a.S, D), epi_accum(g.mix, D));
-  MM(N, D, D, kmaj(dX_, D), mnmaj(w.mix, D), epi_store(dS_, D), 0);
+  MM_W(D, D, N, mop(bf, dX_, dXh_, D),
+       mop(bf, conv_quirk ? a.Sq : a.S, conv_quirk ? a.Sqh : a.Sh, D), epi_accum(g.mix, D));
+  MM(N, D, D, kop(bf, dX_, dXh_, D), mop(bf, w.mix, W16(w.mix), D), epi_store(dS_, D), 0);
   PROF(PK_CONV_BWD, 100.0 * N * D, 3 * ND4,
        rnet_k::conv_bwd(dS_, a.n1, w.c3, w.c7, w.c15, dsub_, g.c3, g.c7, g.c15, conv_parts_, B, T,
                         D, 0, s));
   CK(join());
-  PROF(PK_RMS_BWD, 0, 4 * ND4, rnet_k::rms_norm_bwd(dsub_, Xl, w.n1, a.rinv1, dX_, g.n1, N, D, 1, s));
+  PROF(PK_RMS_BWD, 0, 4 * ND4,
+       rnet_k::rms_norm_bwd(dsub_, Xl, w.n1, a.rinv1, dX_, g.n1, N, D, 1, s, dXh_));
   return RNET_OK;
 }
 
@@ -554,11 +631,13 @@ int Engine::step(float lr, float clip) {
     if (rc) return rc;
     world = dist_world(dist);
   }
-  PROF(PK_SGD, 2.0 * P_, 16.0 * P_,
-       rnet_k::sgd_clip_step(params_, grads_, P_, lr, clip, world, scratch_, norm_dev_, stream_));
+  const bool bf = precision == 1;
+  PROF(PK_SGD, 2.0 * P_, (bf ? 18.0 : 16.0) * P_,
+       rnet_k::sgd_clip_step(params_, grads_, P_, lr, clip, world, scratch_, norm_dev_, stream_,
+                             bf ? params16_ : nullptr));
   cudaEvent_t pa = nullptr;
   if (prof_on_) prof_begin(&pa);
-  int rc = refresh_shadows();
+  int rc = refresh_shadows_impl(bf);
   if (prof_on_) prof_end(pa, PK_OTHER, 0, 16.0 * 2 * cfg_.n_layers * cfg_.n_slots * cfg_.d_model);
   return rc;
 }

@@ -7,6 +7,7 @@
 // gradient buckets are contiguous ranges. Within a layer Wz|Wh and gate|up
 // are adjacent in that order, which the fused GEMMs use as [2D,D] / [2F,D].
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -34,6 +35,8 @@ struct LayerAct {
   float* w;
   float *r1, *r2, *r3;
   float *G, *U, *H;
+  // bf16 copies of the GEMM operands (bf16 mode only, else null)
+  __nv_bfloat16 *n2h, *n3h, *n4h, *Sh, *Sqh, *qh, *rh, *Hh;
 };
 
 class DistComm;  // dist.cu
@@ -131,9 +134,14 @@ class Engine {
   const rnet_model_config& config() const { return cfg_; }
 
   bool conv_quirk = true;  // reference dmix operand (S + c7 + c15)
-  // GEMM arithmetic: rnet_gemm::PREC_TF32X3 (fp32-accurate, default) or
-  // PREC_BF16 (operands rounded to bf16, fp32 accumulation)
+  // GEMM arithmetic: 0 = fp32-accurate (3xTF32, default); 1 = bf16: every
+  // GEMM operand of the train step is a bf16 copy in memory (weights: a bf16
+  // shadow of the fp32 master parameters, refreshed by the SGD update;
+  // activations: bf16 side outputs of their producers), read by TMA as bf16
+  // tiles into kind::f16 MMAs with fp32 accumulation. Everything else
+  // (norms, scan, conv, slot top-2 / gather, loss, optimizer) stays fp32.
   int precision = 0;
+  int set_precision(int p);
   DistComm* dist = nullptr;
 
   // workspace capacity in tokens
@@ -175,6 +183,10 @@ class Engine {
   float *embed_, *outw_, *fnorm_, *g_embed_, *g_outw_, *g_fnorm_;
   std::vector<LayerParams> W_, G_;
   float* KT_ = nullptr;  // [L][S][D]
+  __nv_bfloat16* params16_ = nullptr;  // bf16 shadow of params_ (bf16 mode)
+  __nv_bfloat16* KT16_ = nullptr;      // bf16 shadow of KT_ (bf16 mode)
+  __nv_bfloat16* h16(const float* p) const { return params16_ + (p - params_); }
+  int refresh_shadows_impl(bool params16_current);
   float* VT_ = nullptr;
   float* dKV_ = nullptr;  // [L][keys | values][S][D] scatter gradients
   float* scratch_ = nullptr;  // sgd / ce scratch
@@ -190,6 +202,9 @@ class Engine {
   float* X_ = nullptr;  // [L+1][N][D]
   float *nf_, *rinvf_, *dlogits_, *logits_;
   float *dX_, *dsub_, *dS_, *dq_, *dr_, *dPZH_, *dGU_, *dnf_, *conv_parts_, *scores_;
+  __nv_bfloat16 *nfh_ = nullptr, *dlogitsh_ = nullptr, *dXh_ = nullptr, *dGUh_ = nullptr,
+                *dqh_ = nullptr, *dPZHh_ = nullptr;
+  bool cap_bf16_ = false;
   bool have_cache_ = false;
   int last_B_ = 0, last_T_ = 0;
 };

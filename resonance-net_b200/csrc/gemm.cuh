@@ -7,16 +7,28 @@
 // (kind::tf32 supports MN-major operands on sm_100a).
 #pragma once
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
 namespace rnet_gemm {
 
 struct Operand {
-  const float* p = nullptr;
+  const float* p = nullptr;  // fp32 data, or bf16 data when bf16 is set
   int ld = 0;            // elements between consecutive stored rows
   bool mn_major = false; // see header comment
+  bool bf16 = false;     // bf16 elements (both operands must then be bf16)
 };
+
+// A bf16 operand (ld a multiple of 8, base 16-byte aligned).
+inline Operand bf16_operand(const __nv_bfloat16* p, int ld, bool mn_major) {
+  Operand o;
+  o.p = reinterpret_cast<const float*>(p);
+  o.ld = ld;
+  o.mn_major = mn_major;
+  o.bf16 = true;
+  return o;
+}
 
 enum EpiKind : int {
   EPI_STORE = 0,       // C = alpha*acc
@@ -41,9 +53,15 @@ struct Epilogue {
   // top-2
   int* topk_idx = nullptr;
   float* topk_w = nullptr;
+  // optional bf16 copies of the stored result (row stride ldc for C16, ldf
+  // for H16), for a following GEMM that reads bf16 operands: C16 with
+  // EPI_STORE / EPI_RESID, H16 with EPI_SWIGLU_FWD
+  __nv_bfloat16* C16 = nullptr;
+  __nv_bfloat16* H16 = nullptr;
 };
 
-// Launch. `b_pair_off` > 0 makes every B tile two halves of BN/2 rows taken at
+// Launch. Both operands fp32 (3xTF32 or bf16-rounded per `precision`) or
+// both bf16 (one kind::f16 MMA per 16-deep slice from bf16 tiles). `b_pair_off` > 0 makes every B tile two halves of BN/2 rows taken at
 // logical rows n0 and n0 + b_pair_off (used to pair gate/up weights so one
 // accumulator tile holds both). `k_splits` = 0 picks automatically (only
 // EPI_ACCUM may split K). Returns cudaSuccess or the launch error.

@@ -67,27 +67,31 @@ struct KParams {
 
 // BN = MMA N (accumulator columns per tile). CG = 2: one MMA covers the
 // 2*BM rows of a CTA pair; each CTA stages its BM rows of A and BN/2 rows of B.
-template <int BN, int BK, int CG>
+// ELEM = bytes per staged element (4: fp32 tiles; 2: bf16 tiles read straight
+// from bf16 operands), LO = a twin buffer per stage (the split warps' lo or
+// bf16 tiles).
+template <int BN, int BK, int CG, int ELEM = 4, bool LO = true>
 struct Cfg {
-  static constexpr int ROW_BYTES = BK * 4;            // K-major row (64 or 128 B)
-  static constexpr int MN_CHUNK = 128 * BK;           // MN-major box: 32 elems x BK rows
+  static constexpr int ROW_BYTES = BK * ELEM;         // K-major row (64 or 128 B)
+  static constexpr int MN_ELEMS = 128 / ELEM;         // MN-major box width (one 128 B row)
+  static constexpr int MN_CHUNK = 128 * BK;           // MN-major box: MN_ELEMS x BK rows
   static constexpr int B_ROWS = BN / CG;              // B rows staged by this CTA
-  static constexpr int A_BYTES = BM * BK * 4;
-  static constexpr int B_BYTES = B_ROWS * BK * 4;
+  static constexpr int A_BYTES = BM * BK * ELEM;
+  static constexpr int B_BYTES = B_ROWS * BK * ELEM;
   static constexpr int RAW_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGE_BYTES = 2 * RAW_BYTES;  // raw (= hi) + lo
+  static constexpr int STAGE_BYTES = LO ? 2 * RAW_BYTES : RAW_BYTES;  // raw (= hi) + lo
   static constexpr int STAGES_FIT = SMEM_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int EPI_BYTES = NUM_EPI_WARPS * EPI_TILE_FLOATS * 4;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
   // UMMA smem-descriptor parameters
-  static constexpr uint32_t K_LAYOUT = BK == 32 ? 2u : 4u;  // SWIZZLE_128B / SWIZZLE_64B
+  static constexpr uint32_t K_LAYOUT = ROW_BYTES == 128 ? 2u : 4u;  // SWIZZLE_128B / _64B
   static constexpr uint32_t K_SBO = 8 * ROW_BYTES;          // 8-row core-matrix group
-  static_assert(BK == 16 || BK == 32, "BK");
+  static_assert((ELEM == 4 && (BK == 16 || BK == 32)) || (ELEM == 2 && BK == 64), "BK");
   static_assert(CG == 1 || CG == 2, "CG");
   static_assert(STAGES >= 2, "stages");
-  static_assert(B_ROWS % 32 == 0, "B rows");
+  static_assert(B_ROWS % MN_ELEMS == 0, "B rows");
 };
 
 __device__ __forceinline__ void unit_range(const KParams& p, int unit, int& mt, int& nt0,
@@ -123,7 +127,7 @@ __device__ __forceinline__ float silu_fast(float g) { return g / (1.0f + __expf(
 // op 0 = store, 1 = red.add, 2 = store R + v (R row stride ldr).
 __device__ __forceinline__ void tile_out(float* st, const float (&v)[32], float* dst, int ld,
                                          const float* R, int ldr, int row0, int col0, int M,
-                                         int N, int op) {
+                                         int N, int op, __nv_bfloat16* dst16 = nullptr) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int i = 0; i < 32; ++i) st[lane * TILE_LD + i] = v[i];
@@ -146,17 +150,46 @@ __device__ __forceinline__ void tile_out(float* st, const float (&v)[32], float*
             x.x += r.x; x.y += r.y; x.z += r.z; x.w += r.w;
           }
           *reinterpret_cast<float4*>(g) = x;
+          if (dst16) {
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(x.x, x.y);
+            const __nv_bfloat162 hi = __floats2bfloat162_rn(x.z, x.w);
+            uint2 u;
+            u.x = *reinterpret_cast<const uint32_t*>(&lo);
+            u.y = *reinterpret_cast<const uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(dst16 + (size_t)row * ld + col) = u;
+          }
         }
       } else {
         const float xs[4] = {x.x, x.y, x.z, x.w};
         for (int q = 0; q < 4 && col + q < N; ++q) {
-          if (op == 1) atomicAdd(g + q, xs[q]);
-          else g[q] = xs[q] + (op == 2 ? R[(size_t)row * ldr + col + q] : 0.f);
+          if (op == 1) {
+            atomicAdd(g + q, xs[q]);
+          } else {
+            g[q] = xs[q] + (op == 2 ? R[(size_t)row * ldr + col + q] : 0.f);
+            if (dst16) dst16[(size_t)row * ld + col + q] = __float2bfloat16_rn(g[q]);
+          }
         }
       }
     }
   }
   __syncwarp();
+}
+
+// 32 consecutive values a * v[i] as bf16 (four 16-byte stores).
+__device__ __forceinline__ void store_bf16_row32(__nv_bfloat16* dst, const float (&v)[32], float a,
+                                                 const void*) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 u;
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(a * v[8 * j + 2 * i], a * v[8 * j + 2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    u.x = w[0]; u.y = w[1]; u.z = w[2]; u.w = w[3];
+    reinterpret_cast<uint4*>(dst)[j] = u;
+  }
 }
 
 // Direct thread-per-row store of one 32-column chunk (row stride ld): eight
@@ -175,6 +208,7 @@ __device__ __forceinline__ void store_row_chunk(const KParams& p, int kind, int 
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         dst[j] = make_float4(a * v[4 * j], a * v[4 * j + 1], a * v[4 * j + 2], a * v[4 * j + 3]);
+      if (e.C16) store_bf16_row32(e.C16 + (size_t)row * e.ldc + col0, v, a, nullptr);
     } else if (kind == EPI_ACCUM) {
       float* dst = e.C + (size_t)row * e.ldc + col0;
 #pragma unroll
@@ -184,12 +218,17 @@ __device__ __forceinline__ void store_row_chunk(const KParams& p, int kind, int 
     } else {  // EPI_RESID
       const float4* r = reinterpret_cast<const float4*>(e.R + (size_t)row * e.ldr + col0);
       float4* dst = reinterpret_cast<float4*>(e.C + (size_t)row * e.ldc + col0);
+      float o[32];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float4 q = r[j];
-        dst[j] = make_float4(q.x + a * v[4 * j], q.y + a * v[4 * j + 1], q.z + a * v[4 * j + 2],
-                             q.w + a * v[4 * j + 3]);
+        o[4 * j] = q.x + a * v[4 * j];
+        o[4 * j + 1] = q.y + a * v[4 * j + 1];
+        o[4 * j + 2] = q.z + a * v[4 * j + 2];
+        o[4 * j + 3] = q.w + a * v[4 * j + 3];
+        dst[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
       }
+      if (e.C16) store_bf16_row32(e.C16 + (size_t)row * e.ldc + col0, o, 1.0f, nullptr);
     }
   } else {
     for (int i = 0; i < 32; ++i) {
@@ -199,6 +238,8 @@ __device__ __forceinline__ void store_row_chunk(const KParams& p, int kind, int 
         if (kind == EPI_STORE) *dst = a * v[i];
         else if (kind == EPI_ACCUM) atomicAdd(dst, a * v[i]);
         else *dst = e.R[(size_t)row * e.ldr + col] + a * v[i];
+        if (e.C16 && kind != EPI_ACCUM)
+          e.C16[(size_t)row * e.ldc + col] = __float2bfloat16_rn(*dst);
       }
     }
   }
@@ -246,7 +287,7 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
       tile_out(tile, v, e.U, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = silu_fast(g[i]) * v[i];
-      tile_out(tile, v, e.H, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0);
+      tile_out(tile, v, e.H, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0, e.H16);
     }
     return;
   }
@@ -295,15 +336,15 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
 
 // ------------------------------------------------------------------ TMA tiles
 // A tile [BM x BK] of k-block k0 starting at row m0 into sa.
-template <int BN, int BK, int CG>
+template <class C>
 __device__ __forceinline__ void load_a(uint8_t* sa, const void* map, uint64_t* bar,
                                        const KParams& p, int k0, int m0) {
-  using C = Cfg<BN, BK, CG>;
   if (!p.a_mn) {
     tma_load_2d(sa, map, bar, k0, m0);
   } else {
 #pragma unroll
-    for (int j = 0; j < BM / 32; ++j) tma_load_2d(sa + j * C::MN_CHUNK, map, bar, m0 + 32 * j, k0);
+    for (int j = 0; j < BM / C::MN_ELEMS; ++j)
+      tma_load_2d(sa + j * C::MN_CHUNK, map, bar, m0 + C::MN_ELEMS * j, k0);
   }
 }
 
@@ -311,10 +352,10 @@ __device__ __forceinline__ void load_a(uint8_t* sa, const void* map, uint64_t* b
 // two BN/2 halves (rows n0 and n0 + pair offset) for paired operands.
 // CG = 2: CTA `rank` stages MMA columns [rank*BN/2, (rank+1)*BN/2), which
 // for paired operands is the first (rank 0) or the paired (rank 1) half.
-template <int BN, int BK, int CG>
+template <class C, int BN, int CG>
 __device__ __forceinline__ void load_b(uint8_t* sb, const void* map, uint64_t* bar,
                                        const KParams& p, int k0, int nt, int rank) {
-  using C = Cfg<BN, BK, CG>;
+  constexpr int W = C::MN_ELEMS;
   if (CG == 2 || p.b_pair_off == 0) {
     const int n0 = p.b_pair_off == 0 ? nt * BN + rank * C::B_ROWS
                                      : nt * (BN / 2) + rank * p.b_pair_off;
@@ -322,8 +363,8 @@ __device__ __forceinline__ void load_b(uint8_t* sb, const void* map, uint64_t* b
       tma_load_2d(sb, map, bar, k0, n0);
     } else {
 #pragma unroll
-      for (int j = 0; j < C::B_ROWS / 32; ++j)
-        tma_load_2d(sb + j * C::MN_CHUNK, map, bar, n0 + 32 * j, k0);
+      for (int j = 0; j < C::B_ROWS / W; ++j)
+        tma_load_2d(sb + j * C::MN_CHUNK, map, bar, n0 + W * j, k0);
     }
   } else {
     const int n0 = nt * (BN / 2);
@@ -332,9 +373,10 @@ __device__ __forceinline__ void load_b(uint8_t* sb, const void* map, uint64_t* b
       tma_load_2d(sb + (BN / 2) * C::ROW_BYTES, map, bar, k0, n0 + p.b_pair_off);
     } else {
 #pragma unroll
-      for (int j = 0; j < BN / 64; ++j) {
-        tma_load_2d(sb + j * C::MN_CHUNK, map, bar, n0 + 32 * j, k0);
-        tma_load_2d(sb + (j + BN / 64) * C::MN_CHUNK, map, bar, n0 + p.b_pair_off + 32 * j, k0);
+      for (int j = 0; j < BN / 2 / W; ++j) {
+        tma_load_2d(sb + j * C::MN_CHUNK, map, bar, n0 + W * j, k0);
+        tma_load_2d(sb + (j + BN / 2 / W) * C::MN_CHUNK, map, bar, n0 + p.b_pair_off + W * j,
+                    k0);
       }
     }
   }
@@ -353,14 +395,18 @@ __device__ __forceinline__ void load_b(uint8_t* sb, const void* map, uint64_t* b
 // A cluster barrier after set-up (barrier init, TMEM alloc) and before
 // teardown (TMEM dealloc, exit) keeps either CTA from touching the other's
 // barriers or TMEM outside their lifetime.
-// BF = false: 3xTF32 (fp32-accurate). BF = true: operands rounded to bf16 by
-// the split warps (fp32 accumulate), one kind::f16 MMA per K-block.
-template <int BN, int BK, int CG, bool BF>
+// MODE 0: 3xTF32 (fp32-accurate). MODE 1: fp32 operands rounded to bf16 by
+// the split warps (fp32 accumulate), one kind::f16 MMA per K-block. MODE 2:
+// bf16 operands in global memory, staged by TMA as they are (64-deep
+// K-blocks, SWIZZLE_128B) and fed to kind::f16 MMAs directly; the split
+// warps have nothing to do and the MMA issuer waits on the TMA barrier.
+template <int BN, int BK, int CG, int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, const KParams p) {
   rnet_dev::pdl_trigger();
-  using C = Cfg<BN, BK, CG>;
+  constexpr bool BF = MODE == 1;
+  using C = Cfg<BN, BK, CG, MODE == 2 ? 2 : 4, MODE != 2>;
   constexpr bool PAIR = CG == 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -385,7 +431,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&split[s], NUM_SPLIT_WARPS * CG);
+      mbar_init(&split[s], MODE == 2 ? CG : NUM_SPLIT_WARPS * CG);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -427,8 +473,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint8_t* sb = sa + C::A_BYTES;
             mbar_arrive_expect_tx(&full[s], C::RAW_BYTES);
             const int k0 = kb * BK;
-            load_a<BN, BK, CG>(sa, &tmA, &full[s], p, k0, m0);
-            load_b<BN, BK, CG>(sb, &tmB, &full[s], p, k0, nt, rank);
+            load_a<C>(sa, &tmA, &full[s], p, k0, m0);
+            load_b<C, BN, CG>(sb, &tmB, &full[s], p, k0, nt, rank);
           }
         }
       }
@@ -437,6 +483,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0 && rank == 0) {
       const uint32_t idesc = make_idesc(BM * CG, BN, 2, p.a_mn, p.b_mn);
       const uint32_t idesc_bf = make_idesc(BM * CG, BN, 1, 0, 0);  // bf16, both K-major
+      const uint32_t idesc_st = make_idesc(BM * CG, BN, 1, p.a_mn, p.b_mn);  // MODE 2
       // Byte advance of one 8-deep K slice and LBO / SBO / layout per operand.
       const uint32_t a_kstep = p.a_mn ? 1024u : 32u;
       const uint32_t b_kstep = p.b_mn ? 1024u : 32u;
@@ -461,10 +508,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s = it % C::STAGES;
             const uint32_t ph = (it / C::STAGES) & 1;
-            if (!mbar_wait(&split[s], ph, p.err, abort_flag)) { ok = false; break; }
+            if (!mbar_wait((MODE == 2 && CG == 1) ? &full[s] : &split[s], ph, p.err,
+                           abort_flag)) {
+              ok = false;
+              break;
+            }
             tc_fence_after();
             const uint32_t a_hi = smem_u32(smem + s * C::STAGE_BYTES);
-            if constexpr (BF) {
+            if constexpr (MODE == 2) {
+              // bf16 SWIZZLE_128B tiles: K-major rows of 64 elements (a
+              // 16-deep slice is +32 B inside the swizzle atom; 8-row groups
+              // 1024 B apart); MN-major: 64-wide MN chunks MN_CHUNK apart,
+              // K rows 128 B apart (a 16-deep slice is +2048 B, 8-row K
+              // groups 1024 B apart)
+              const uint32_t b_hi = a_hi + C::A_BYTES;
+#pragma unroll
+              for (int kk = 0; kk < BK / 16; ++kk) {
+                const uint64_t da =
+                    p.a_mn ? make_sdesc(a_hi + kk * 2048, C::MN_CHUNK, 1024, 2)
+                           : make_sdesc(a_hi + kk * 32, 16, 1024, 2);
+                const uint64_t db =
+                    p.b_mn ? make_sdesc(b_hi + kk * 2048, C::MN_CHUNK, 1024, 2)
+                           : make_sdesc(b_hi + kk * 32, 16, 1024, 2);
+                umma_f16<CG>(tacc, da, db, idesc_st, accumulate);
+                accumulate = 1;
+              }
+            } else if constexpr (BF) {
               // bf16 tiles (K-major, no swizzle) written by the split warps
               const uint32_t a_bf = a_hi + C::RAW_BYTES;
               const uint32_t b_bf = a_bf + BM * 32;
@@ -500,6 +569,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_wait(drain, 0, p.err, &no_abort);
     }
   } else if (warp >= FIRST_SPLIT_WARP) {
+   if constexpr (MODE == 2 && CG == 2) {
+    // bf16 tiles need no split work, but the pair's MMA (issued by the even
+    // CTA) reads both CTAs' tiles: one thread per CTA relays "this CTA's
+    // tiles of stage s have landed" to the even CTA's split[s] barrier
+    if (warp == FIRST_SPLIT_WARP && lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int unit = group; unit < p.num_units && ok; unit += n_groups) {
+        int mt, nt0, nt1, kb0, kb1;
+        unit_range(p, unit, mt, nt0, nt1, kb0, kb1);
+        for (int nt = nt0; nt < nt1 && ok; ++nt) {
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int s = it % C::STAGES;
+            const uint32_t ph = (it / C::STAGES) & 1;
+            if (!mbar_wait(&full[s], ph, p.err, abort_flag)) { ok = false; break; }
+            mbar_arrive_cluster(&split[s], 0);
+          }
+        }
+      }
+    }
+   } else if constexpr (MODE != 2) {
     const int t = threadIdx.x - FIRST_SPLIT_WARP * 32;
     constexpr int NT = NUM_SPLIT_WARPS * 32;
     constexpr int N4 = C::RAW_BYTES / 16;
@@ -572,6 +662,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+   }
   } else {  // epilogue warps 0..3
     const int q = warp;  // TMEM lane quadrant
     uint32_t tc = 0;
@@ -622,17 +713,18 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// 2-D fp32 tensor map. box = {box_inner, box_outer} elements.
+// 2-D fp32 (or bf16) tensor map. box = {box_inner, box_outer} elements.
 static bool make_map(CUtensorMap* m, const float* base, uint64_t inner, uint64_t outer,
                      uint64_t ld_elems, uint32_t box_inner, uint32_t box_outer,
-                     CUtensorMapSwizzle swz) {
+                     CUtensorMapSwizzle swz, bool bf16 = false) {
   auto enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {ld_elems * sizeof(float)};
+  cuuint64_t strides[1] = {ld_elems * (bf16 ? 2 : 4)};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                   const_cast<float*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -679,13 +771,13 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int BK, int CG, bool BF>
+template <int BN, int BK, int CG, int MODE>
 static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
                           const KParams& kp) {
-  using C = Cfg<BN, BK, CG>;
+  using C = Cfg<BN, BK, CG, MODE == 2 ? 2 : 4, MODE != 2>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK, CG, BF>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK, CG, MODE>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES);
     if (e != cudaSuccess) {
@@ -719,7 +811,7 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
     if (CG > 1) {
       int n = 0;
       cfg.gridDim = dim3(max_groups * CG);
-      if (cudaOccupancyMaxActiveClusters(&n, gemm_tf32x3_kernel<BN, BK, CG, BF>, &cfg) ==
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_tf32x3_kernel<BN, BK, CG, MODE>, &cfg) ==
               cudaSuccess &&
           n > 0 && n < max_groups)
         max_groups = n;
@@ -731,7 +823,7 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
   }
   const int groups = kp.num_units < max_groups ? kp.num_units : max_groups;
   cfg.gridDim = dim3(groups * CG);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, BK, CG, BF>, ta, tb, kp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, BK, CG, MODE>, ta, tb, kp);
   if (e != cudaSuccess) {
     g_reason = "kernel launch";
     return e;
@@ -832,20 +924,24 @@ cudaError_t reserve_workspace(cudaStream_t stream, size_t floats) {
 cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand& A,
                         const Operand& B, const Epilogue& epi, int b_pair_off, int k_splits,
                         unsigned* err_word, int precision) {
-  const bool bf = precision == PREC_BF16;
   if (M <= 0 || N <= 0) return cudaSuccess;
   g_reason = "";
   if (K <= 0 || A.p == nullptr || B.p == nullptr) return reject("K <= 0 or null operand");
-  if ((A.ld % 4) || (B.ld % 4) || (reinterpret_cast<uintptr_t>(A.p) & 15) ||
+  if (A.bf16 != B.bf16) return reject("one bf16 and one fp32 operand");
+  const bool st16 = A.bf16;  // bf16 storage: MODE 2
+  const bool bf = !st16 && precision == PREC_BF16;
+  const int ld_mult = st16 ? 8 : 4;
+  if ((A.ld % ld_mult) || (B.ld % ld_mult) || (reinterpret_cast<uintptr_t>(A.p) & 15) ||
       (reinterpret_cast<uintptr_t>(B.p) & 15))
-    return reject("operand ld not a multiple of 4 or operand not 16-byte aligned");
+    return reject("operand row pitch not a multiple of 16 bytes or operand not 16-byte aligned");
+  if (st16 && (b_pair_off % 8)) return reject("bf16 paired offset not a multiple of 8");
   const bool paired = b_pair_off > 0;
   const bool row_owner = epi.kind == EPI_TOP2;
-  constexpr int BK = 16;
+  const int BK = st16 ? 64 : 16;
   // Short M: split K over a workspace when the output tiles cannot fill the
   // SMs (store / residual epilogues, and accumulation asked for in one pass).
   int ws_splits = 1;
-  if (!paired && !row_owner && g_force_cg == 0 && M <= 1024 &&
+  if (!paired && !row_owner && g_force_cg == 0 && M <= 1024 && !epi.C16 &&
       (epi.kind == EPI_STORE || epi.kind == EPI_RESID ||
        (epi.kind == EPI_ACCUM && k_splits == 1))) {
     const int tiles = ((M + BM - 1) / BM) * ((N + 127) / 128);
@@ -917,43 +1013,54 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   kp.k_splits = (kp.kb_total + kp.kb_per_split - 1) / kp.kb_per_split;
   kp.num_units = row_owner ? kp.m_tiles : kp.m_tiles * kp.n_tiles * kp.k_splits;
 
-  // bf16: the split warps read the raw fp32 tiles, so they stay unswizzled
+  // bf16 (MODE 1): the split warps read the raw fp32 tiles, so they stay
+  // unswizzled. bf16 storage (MODE 2): 128-byte rows, SWIZZLE_128B both ways.
   const CUtensorMapSwizzle kswz =
-      bf ? CU_TENSOR_MAP_SWIZZLE_NONE
-         : (BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+      st16 ? CU_TENSOR_MAP_SWIZZLE_128B
+           : bf ? CU_TENSOR_MAP_SWIZZLE_NONE
+                : (BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   const CUtensorMapSwizzle mswz =
-      bf ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+      st16 ? CU_TENSOR_MAP_SWIZZLE_128B
+           : bf ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+  const uint32_t mn_box = st16 ? 64 : 32;
   auto map_a = [&](CUtensorMap* m, const float* base) {
-    return !A.mn_major ? make_map(m, base, (uint64_t)K, (uint64_t)M, A.ld, BK, BM, kswz)
-                       : make_map(m, base, (uint64_t)M, (uint64_t)K, A.ld, 32, BK, mswz);
+    return !A.mn_major ? make_map(m, base, (uint64_t)K, (uint64_t)M, A.ld, BK, BM, kswz, st16)
+                       : make_map(m, base, (uint64_t)M, (uint64_t)K, A.ld, mn_box, BK, mswz, st16);
   };
   const uint64_t b_rows = paired ? (uint64_t)b_pair_off + N : (uint64_t)N;
   // K-major box rows = the rows one TMA copy stages (a half tile when paired
   // or when a CTA pair splits B).
   const uint32_t b_box = (paired || CG == 2) ? BN / 2 : BN;
   auto map_b = [&](CUtensorMap* m, const float* base) {
-    return !B.mn_major ? make_map(m, base, (uint64_t)K, b_rows, B.ld, BK, b_box, kswz)
-                       : make_map(m, base, b_rows, (uint64_t)K, B.ld, 32, BK, mswz);
+    return !B.mn_major ? make_map(m, base, (uint64_t)K, b_rows, B.ld, BK, b_box, kswz, st16)
+                       : make_map(m, base, b_rows, (uint64_t)K, B.ld, mn_box, BK, mswz, st16);
   };
   CUtensorMap ta, tb;
   if (!map_a(&ta, A.p)) return reject("tensor map of A rejected");
   if (!map_b(&tb, B.p)) return reject("tensor map of B rejected");
 
   cudaError_t e;
-  if (bf) {
+  if (st16) {
     if (CG == 2)
-      e = BN == 128 ? launch<128, BK, 2, true>(stream, ta, tb, kp)
-                    : launch<256, BK, 2, true>(stream, ta, tb, kp);
+      e = BN == 128 ? launch<128, 64, 2, 2>(stream, ta, tb, kp)
+                    : launch<256, 64, 2, 2>(stream, ta, tb, kp);
     else
-      e = BN == 128 ? launch<128, BK, 1, true>(stream, ta, tb, kp)
-                    : launch<256, BK, 1, true>(stream, ta, tb, kp);
+      e = BN == 128 ? launch<128, 64, 1, 2>(stream, ta, tb, kp)
+                    : launch<256, 64, 1, 2>(stream, ta, tb, kp);
+  } else if (bf) {
+    if (CG == 2)
+      e = BN == 128 ? launch<128, 16, 2, 1>(stream, ta, tb, kp)
+                    : launch<256, 16, 2, 1>(stream, ta, tb, kp);
+    else
+      e = BN == 128 ? launch<128, 16, 1, 1>(stream, ta, tb, kp)
+                    : launch<256, 16, 1, 1>(stream, ta, tb, kp);
   } else {
     if (CG == 2)
-      e = BN == 128 ? launch<128, BK, 2, false>(stream, ta, tb, kp)
-                    : launch<256, BK, 2, false>(stream, ta, tb, kp);
+      e = BN == 128 ? launch<128, 16, 2, 0>(stream, ta, tb, kp)
+                    : launch<256, 16, 2, 0>(stream, ta, tb, kp);
     else
-      e = BN == 128 ? launch<128, BK, 1, false>(stream, ta, tb, kp)
-                    : launch<256, BK, 1, false>(stream, ta, tb, kp);
+      e = BN == 128 ? launch<128, 16, 1, 0>(stream, ta, tb, kp)
+                    : launch<256, 16, 1, 0>(stream, ta, tb, kp);
   }
   if (e != cudaSuccess || kp.split_stride == 0) return e;
   // fixed-order sum of the partials + the caller's epilogue

@@ -1,6 +1,7 @@
 // Launchers of the non-GEMM ResonanceNet kernels (all sm_100a, fp32).
 // Every launcher is asynchronous on `s` and returns the launch status.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 namespace rnet_k {
@@ -12,13 +13,19 @@ cudaError_t launched(unsigned n = 1);
 // ---- RMSNorm (rms_norm.cu) ------------------------------------------------
 // y = x * rinv * w, rinv = rsqrt(mean(x^2) + eps)        (y may be null)
 // xcopy (optional): also store x there (seeds a residual sum that a GEMM then
-// accumulates into).
+// accumulates into). y16 (optional): y rounded to bf16 as well (the operand
+// of a following bf16 GEMM).
 cudaError_t rms_norm_fwd(const float* x, const float* w, float* y, float* rinv, int rows,
-                         int D, float eps, cudaStream_t s, float* xcopy = nullptr);
+                         int D, float eps, cudaStream_t s, float* xcopy = nullptr,
+                         __nv_bfloat16* y16 = nullptr);
 // dx_norm = rinv*(dy*w - xhat*mean(dy*w*xhat)); dw += sum_rows dy*xhat.
 // mode 0: dx = dx_norm (overwrite); mode 1: dx += dx_norm (residual stream).
+// dx16 (optional): the final dx rounded to bf16 as well.
 cudaError_t rms_norm_bwd(const float* dy, const float* x, const float* w, const float* rinv,
-                         float* dx, float* dw, int rows, int D, int mode, cudaStream_t s);
+                         float* dx, float* dw, int rows, int D, int mode, cudaStream_t s,
+                         __nv_bfloat16* dx16 = nullptr);
+// y = bf16(x), n elements (x, y 16-byte aligned when n % 8 == 0 is used).
+cudaError_t to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s);
 
 // ---- depthwise causal convolution (causal_conv.cu) -------------------------
 // c3/c7/c15 of x over each length-T sequence, S = c3 + c7 + c15.
@@ -130,8 +137,10 @@ cudaError_t sample_rows(const float* logits, int M, int V, float temperature, fl
 //   lr_eff = lr/world * min(1, clip / (||g|| / world))   (if clip > 0)
 //   p -= lr_eff * g
 // `scratch` = sgd_scratch_floats() floats. norm_out (optional) gets ||g||.
+// params16 (optional): the updated parameters rounded to bf16 as well.
 size_t sgd_scratch_floats();
 cudaError_t sgd_clip_step(float* params, const float* grads, size_t n, float lr, float clip,
-                          int world, float* scratch, float* norm_out, cudaStream_t s);
+                          int world, float* scratch, float* norm_out, cudaStream_t s,
+                          __nv_bfloat16* params16 = nullptr);
 
 }  // namespace rnet_k

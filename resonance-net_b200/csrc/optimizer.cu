@@ -62,7 +62,7 @@ __global__ void finalize_kernel(const double* __restrict__ part, int nparts, flo
 }
 
 __global__ void update_kernel(float* __restrict__ p, const float* __restrict__ g, size_t n,
-                              const float* __restrict__ lr_ptr) {
+                              const float* __restrict__ lr_ptr, __nv_bfloat16* __restrict__ p16) {
   rnet_dev::pdl_trigger();
   const float neg = -*lr_ptr;
   const size_t n4 = n / 4;
@@ -74,17 +74,57 @@ __global__ void update_kernel(float* __restrict__ p, const float* __restrict__ g
     const float4 b = g4[i];
     a.x += neg * b.x; a.y += neg * b.y; a.z += neg * b.z; a.w += neg * b.w;
     p4[i] = a;
+    if (p16) {
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
+      uint2 u;
+      u.x = *reinterpret_cast<const uint32_t*>(&lo);
+      u.y = *reinterpret_cast<const uint32_t*>(&hi);
+      reinterpret_cast<uint2*>(p16)[i] = u;
+    }
   }
   if (blockIdx.x == 0)
-    for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) p[i] += neg * g[i];
+    for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) {
+      p[i] += neg * g[i];
+      if (p16) p16[i] = __float2bfloat16_rn(p[i]);
+    }
+}
+
+__global__ void to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y,
+                               size_t n) {
+  rnet_dev::pdl_trigger();
+  const size_t n4 = n / 4;
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const float4 a = x4[i];
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&lo);
+    u.y = *reinterpret_cast<const uint32_t*>(&hi);
+    reinterpret_cast<uint2*>(y)[i] = u;
+  }
+  if (blockIdx.x == 0)
+    for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) y[i] = __float2bfloat16_rn(x[i]);
 }
 
 }  // namespace
 
 size_t sgd_scratch_floats() { return 2 * NORM_BLOCKS + 8; }
 
+cudaError_t to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) {
+  if (!n) return cudaSuccess;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 7))
+    return cudaErrorInvalidValue;
+  size_t grid = (n / 4 + 255) / 256;
+  if (grid > 148 * 8) grid = 148 * 8;
+  if (grid < 1) grid = 1;
+  to_bf16_kernel<<<(unsigned)grid, 256, 0, s>>>(x, y, n);
+  return launched();
+}
+
 cudaError_t sgd_clip_step(float* params, const float* grads, size_t n, float lr, float clip,
-                          int world, float* scratch, float* norm_out, cudaStream_t s) {
+                          int world, float* scratch, float* norm_out, cudaStream_t s,
+                          __nv_bfloat16* params16) {
   if (!n) return cudaSuccess;
   if ((reinterpret_cast<uintptr_t>(params) | reinterpret_cast<uintptr_t>(grads)) & 15)
     return cudaErrorInvalidValue;
@@ -92,7 +132,7 @@ cudaError_t sgd_clip_step(float* params, const float* grads, size_t n, float lr,
   float* lr_dev = scratch + 2 * NORM_BLOCKS;
   sumsq_kernel<<<NORM_BLOCKS, 256, 0, s>>>(grads, n, part);
   finalize_kernel<<<1, 256, 0, s>>>(part, NORM_BLOCKS, lr, clip, world, lr_dev, norm_out);
-  update_kernel<<<148 * 8, 256, 0, s>>>(params, grads, n, lr_dev);
+  update_kernel<<<148 * 8, 256, 0, s>>>(params, grads, n, lr_dev, params16);
   return launched(3);
 }
 

@@ -20,11 +20,19 @@ namespace {
 
 constexpr int WARPS = 8;
 
+__device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float4 v) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t*>(&a);
+  u.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
 template <int VPL>
 __global__ void __launch_bounds__(WARPS * 32)
     rms_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
                    float* __restrict__ y, float* __restrict__ rinv, int rows, int D, float eps,
-                   float* __restrict__ xcopy) {
+                   float* __restrict__ xcopy, __nv_bfloat16* __restrict__ y16) {
   rnet_dev::pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = D >> 2;
@@ -57,8 +65,10 @@ __global__ void __launch_bounds__(WARPS * 32)
         const int c = lane + 32 * j;
         if (c < nv) {
           const float4 g = w4[c];
-          yr[c] = make_float4(v[j].x * ri * g.x, v[j].y * ri * g.y, v[j].z * ri * g.z,
-                              v[j].w * ri * g.w);
+          const float4 o = make_float4(v[j].x * ri * g.x, v[j].y * ri * g.y, v[j].z * ri * g.z,
+                                       v[j].w * ri * g.w);
+          yr[c] = o;
+          if (y16) st_bf16x4(y16 + (size_t)row * D + 4 * c, o);
         }
       }
     }
@@ -69,7 +79,8 @@ template <int VPL>
 __global__ void __launch_bounds__(WARPS * 32)
     rms_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                    const float* __restrict__ w, const float* __restrict__ rinv,
-                   float* __restrict__ dx, float* __restrict__ dw, int rows, int D, int mode) {
+                   float* __restrict__ dx, float* __restrict__ dw, int rows, int D, int mode,
+                   __nv_bfloat16* __restrict__ dx16) {
   rnet_dev::pdl_trigger();
   extern __shared__ float sdw[];  // [WARPS][D]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -110,6 +121,7 @@ __global__ void __launch_bounds__(WARPS * 32)
                                ri * (g[j].w * ww.w - xh[j].w * dot));
         o.x += prev[j].x; o.y += prev[j].y; o.z += prev[j].z; o.w += prev[j].w;
         dxr[c] = o;
+        if (dx16) st_bf16x4(dx16 + (size_t)row * D + 4 * c, o);
         acc[j].x += g[j].x * xh[j].x;
         acc[j].y += g[j].y * xh[j].y;
         acc[j].z += g[j].z * xh[j].z;
@@ -154,7 +166,7 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
     rms_bwd_staged_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                           const float* __restrict__ w, const float* __restrict__ rinv,
                           float* __restrict__ dx, float* __restrict__ dw, int rows, int D,
-                          int mode, unsigned* err) {
+                          int mode, unsigned* err, __nv_bfloat16* __restrict__ dx16) {
   rnet_dev::pdl_trigger();
   // [2 stages][3 arrays][WARPS rows][D]
   extern __shared__ __align__(16) float sbuf[];
@@ -243,6 +255,7 @@ __global__ void __launch_bounds__(WARPS * 32, 2)
             o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
           }
           dxr[c] = o;
+          if (dx16) st_bf16x4(dx16 + (size_t)row * D + 4 * c, o);
           acc[j].x += gv[j].x * xh[j].x;
           acc[j].y += gv[j].y * xh[j].y;
           acc[j].z += gv[j].z * xh[j].z;
@@ -290,17 +303,17 @@ int sm_count() {
 
 template <int VPL>
 cudaError_t fwd_t(const float* x, const float* w, float* y, float* rinv, int rows, int D,
-                  float eps, cudaStream_t s, float* xcopy) {
+                  float eps, cudaStream_t s, float* xcopy, __nv_bfloat16* y16) {
   const int need = (rows + WARPS - 1) / WARPS;
   const int cap = sm_count() * 8;
   rms_fwd_kernel<VPL><<<need < cap ? need : cap, WARPS * 32, 0, s>>>(x, w, y, rinv, rows, D, eps,
-                                                                          xcopy);
+                                                                          xcopy, y16);
   return launched();
 }
 
 template <int VPL>
 cudaError_t bwd_t(const float* dy, const float* x, const float* w, const float* rinv, float* dx,
-                  float* dw, int rows, int D, int mode, cudaStream_t s) {
+                  float* dw, int rows, int D, int mode, cudaStream_t s, __nv_bfloat16* dx16) {
   if constexpr (VPL * 128 <= STAGED_MAX_D) {
     const size_t smem = (size_t)2 * 3 * WARPS * D * sizeof(float);
     static bool set = false;
@@ -315,7 +328,8 @@ cudaError_t bwd_t(const float* dy, const float* x, const float* w, const float* 
     if (grid > ngroups) grid = ngroups;
     rms_bwd_staged_kernel<VPL><<<grid, WARPS * 32, smem, s>>>(dy, x, w, rinv, dx, dw, rows, D,
                                                               mode,
-                                                              rnet_status::device_error_word());
+                                                              rnet_status::device_error_word(),
+                                                              dx16);
     return launched();
   }
   // >= 4 rows per warp so the dw partial flush is amortised
@@ -332,34 +346,35 @@ cudaError_t bwd_t(const float* dy, const float* x, const float* w, const float* 
       set = true;
     }
   }
-  rms_bwd_kernel<VPL><<<grid, WARPS * 32, smem, s>>>(dy, x, w, rinv, dx, dw, rows, D, mode);
+  rms_bwd_kernel<VPL><<<grid, WARPS * 32, smem, s>>>(dy, x, w, rinv, dx, dw, rows, D, mode, dx16);
   return launched();
 }
 
 }  // namespace
 
 cudaError_t rms_norm_fwd(const float* x, const float* w, float* y, float* rinv, int rows, int D,
-                         float eps, cudaStream_t s, float* xcopy) {
+                         float eps, cudaStream_t s, float* xcopy, __nv_bfloat16* y16) {
   if (rows <= 0) return cudaSuccess;
   if (D % 4 != 0 || D > 2048) return cudaErrorInvalidValue;
   const int vpl = (D + 127) / 128;
-  if (vpl <= 1) return fwd_t<1>(x, w, y, rinv, rows, D, eps, s, xcopy);
-  if (vpl <= 2) return fwd_t<2>(x, w, y, rinv, rows, D, eps, s, xcopy);
-  if (vpl <= 4) return fwd_t<4>(x, w, y, rinv, rows, D, eps, s, xcopy);
-  if (vpl <= 8) return fwd_t<8>(x, w, y, rinv, rows, D, eps, s, xcopy);
-  return fwd_t<16>(x, w, y, rinv, rows, D, eps, s, xcopy);
+  if (vpl <= 1) return fwd_t<1>(x, w, y, rinv, rows, D, eps, s, xcopy, y16);
+  if (vpl <= 2) return fwd_t<2>(x, w, y, rinv, rows, D, eps, s, xcopy, y16);
+  if (vpl <= 4) return fwd_t<4>(x, w, y, rinv, rows, D, eps, s, xcopy, y16);
+  if (vpl <= 8) return fwd_t<8>(x, w, y, rinv, rows, D, eps, s, xcopy, y16);
+  return fwd_t<16>(x, w, y, rinv, rows, D, eps, s, xcopy, y16);
 }
 
 cudaError_t rms_norm_bwd(const float* dy, const float* x, const float* w, const float* rinv,
-                         float* dx, float* dw, int rows, int D, int mode, cudaStream_t s) {
+                         float* dx, float* dw, int rows, int D, int mode, cudaStream_t s,
+                         __nv_bfloat16* dx16) {
   if (rows <= 0) return cudaSuccess;
   if (D % 4 != 0 || D > 2048) return cudaErrorInvalidValue;
   const int vpl = (D + 127) / 128;
-  if (vpl <= 1) return bwd_t<1>(dy, x, w, rinv, dx, dw, rows, D, mode, s);
-  if (vpl <= 2) return bwd_t<2>(dy, x, w, rinv, dx, dw, rows, D, mode, s);
-  if (vpl <= 4) return bwd_t<4>(dy, x, w, rinv, dx, dw, rows, D, mode, s);
-  if (vpl <= 8) return bwd_t<8>(dy, x, w, rinv, dx, dw, rows, D, mode, s);
-  return bwd_t<16>(dy, x, w, rinv, dx, dw, rows, D, mode, s);
+  if (vpl <= 1) return bwd_t<1>(dy, x, w, rinv, dx, dw, rows, D, mode, s, dx16);
+  if (vpl <= 2) return bwd_t<2>(dy, x, w, rinv, dx, dw, rows, D, mode, s, dx16);
+  if (vpl <= 4) return bwd_t<4>(dy, x, w, rinv, dx, dw, rows, D, mode, s, dx16);
+  if (vpl <= 8) return bwd_t<8>(dy, x, w, rinv, dx, dw, rows, D, mode, s, dx16);
+  return bwd_t<16>(dy, x, w, rinv, dx, dw, rows, D, mode, s, dx16);
 }
 
 }  // namespace rnet_k
