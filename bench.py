@@ -38,6 +38,9 @@ sys.path.insert(0, ROOT)
 METRIC = "train tok/s (d512 L8 B64 T256)"
 UNIT = "tok/s"
 CFG = dict(d_model=512, n_layers=8, d_ff=1024, n_slots=1024, top_k=2, vocab=256, seq_len=256)
+# the scaled model, bf16 GEMM operands, per-GPU B16 x T2048
+CFG5 = dict(d_model=2048, n_layers=24, d_ff=5632, n_slots=8192, top_k=2, vocab=256, seq_len=2048)
+METRIC5 = "train tok/s (d2048 L24 F5632 S8192, B16 T2048 per GPU, bf16)"
 LR, CLIP = 3e-4, 1.0
 POOL = 8
 
@@ -48,8 +51,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=64)
-    ap.add_argument("--seq", type=int, default=256)
+    ap.add_argument("--model", choices=["c2", "c5"], default="c2",
+                    help="c2: config 2 (default, fp32); c5: config 5 (d2048 L24, bf16, "
+                         "activation recompute)")
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--seq", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--bf16", action="store_true",
                     help="bf16 GEMM operands with fp32 accumulation (default: fp32-accurate)")
@@ -213,11 +219,32 @@ def run_ours(args, rank, world, local):
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
         pg = dist
     B, T = args.batch, args.seq
-    cfg = rnet.ModelConfig.make(d_model=CFG["d_model"], n_layers=CFG["n_layers"],
-                                d_ff=CFG["d_ff"], n_slots=CFG["n_slots"], top_k=CFG["top_k"],
-                                vocab=CFG["vocab"], seq_len=CFG["seq_len"])
+    c5 = args.model == "c5"
+    C = CFG5 if c5 else CFG
+    cfg = rnet.ModelConfig.make(d_model=C["d_model"], n_layers=C["n_layers"],
+                                d_ff=C["d_ff"], n_slots=C["n_slots"], top_k=C["top_k"],
+                                vocab=C["vocab"], seq_len=C["seq_len"])
     model = rnet.Model(cfg, device=local, reference_init=False)
-    model.set_params(rdata.init_params_normal(cfg, seed=1234))
+    if c5:
+        # 2.14B parameters: N(0, 0.02) drawn on the device (same rule as
+        # init_params_normal: norm gains 1, biases 0), one seeded generator
+        flat = torch.empty(model.num_params, device="cuda")
+        g = torch.Generator(device="cuda").manual_seed(1234)
+        off = 0
+        for name, n in rdata.tensor_layout(cfg):
+            base = name.split(".")[-1]
+            if base.startswith("norm") or base == "final_norm":
+                flat[off:off + n].fill_(1.0)
+            elif base in ("bz", "bh"):
+                flat[off:off + n].zero_()
+            else:
+                flat[off:off + n].normal_(0.0, 0.02, generator=g)
+            off += n
+        model.set_params_device(flat)
+        del flat
+        model.set_recompute(True)
+    else:
+        model.set_params(rdata.init_params_normal(cfg, seed=1234))
     model.set_precision(args.bf16)
     dist_h = None
     if world > 1:
@@ -324,16 +351,22 @@ def run_ours(args, rank, world, local):
                 kernels[k]["GBps"] = round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1)
                 kernels[k]["hbm_frac"] = round(kernels[k]["GBps"] / peaks["hbm"], 3)
     out = {
-        "metric": METRIC, "value": round(tokens / (ms * 1e-3), 1), "unit": UNIT,
+        "metric": METRIC5 if c5 else METRIC, "value": round(tokens / (ms * 1e-3), 1), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
         "dtype": ("bf16 GEMM operands, fp32 accumulate (tcgen05 kind::f16)" if args.bf16
                   else "fp32 (3xTF32 tcgen05)"),
         "data": "synthetic Zipf(1.1) byte tokens, N(0,0.02) weights",
-        "config": {"workload": "train step, d512 L8 F1024 S1024 top2 V256", "model": "ResonanceNet",
-                   "global_batch": world * B, "seq_len": T, "parallelism": f"dp{world}",
-                   "per_gpu_batch": B, "l2": "working set per step ~6.5 GB >> 126 MB L2 (no flush)"},
+        "config": ({"workload": "config 5 train step, d2048 L24 F5632 S8192 top2 V256, bf16 GEMM "
+                                "operands, fp32 master weights, activation recompute, "
+                                + ("bf16 gradient all-reduce" if world > 1 else "1 GPU"),
+                    "model": "ResonanceNet", "global_batch": world * B, "seq_len": T,
+                    "parallelism": f"dp{world}", "per_gpu_batch": B,
+                    "l2": "working set per step ~45 GB >> 126 MB L2 (no flush)"} if c5 else
+                   {"workload": "train step, d512 L8 F1024 S1024 top2 V256", "model": "ResonanceNet",
+                    "global_batch": world * B, "seq_len": T, "parallelism": f"dp{world}",
+                    "per_gpu_batch": B, "l2": "working set per step ~6.5 GB >> 126 MB L2 (no flush)"}),
         "e2e": {"value": round(tokens / (ms_e2e * 1e-3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": 2 * B * T * 4, "d2h_bytes_per_step": 4},
         "gpu_launches": int(launches),
@@ -376,6 +409,13 @@ def run_reference(args, rank, world, local):
     import oracle
     rdata = importlib.import_module("resonance-net_b200.data")
     base = {"impl": "reference", "metric": METRIC, "unit": UNIT}
+    if args.model == "c5":
+        print(json.dumps({**base, "metric": METRIC5, "unavailable":
+                          "config 5 is not safely runnable on the reference: its per-layer cache "
+                          "is sized from free memory (src/resonance_net.cpp:91-101) while forward "
+                          "still uses it for N <= 64*seq_len (src/resonance_net.cpp:245)"}),
+              flush=True)
+        return
     if not oracle.ref_available():
         print(json.dumps({**base, "unavailable": "oracle/_ref/libref.so (reference CUDA build) "
                                                  "not built"}), flush=True)
@@ -712,6 +752,15 @@ def run_decode(args, rank, world, local):
 
 def main():
     args = parse()
+    if args.model == "c5":
+        args.batch = args.batch or 16
+        args.seq = args.seq or 2048
+        args.bf16 = True
+        args.no_decode = True
+        args.no_cpu_baseline = True
+    else:
+        args.batch = args.batch or 64
+        args.seq = args.seq or 256
     rank, world, local = env_rank()
     if args.op:
         run_op(args)

@@ -190,6 +190,9 @@ int rnet_model_param_count(const rnet_model* m, size_t* n);
 int rnet_model_device_buffers(rnet_model* m, float** d_params, float** d_grads);
 int rnet_model_stream(rnet_model* m, void** stream);
 int rnet_model_set_params(rnet_model* m, const float* host, size_t n);
+/* Same as rnet_model_set_params from a device buffer (any stream order: the
+ * call synchronises the model's stream). No counterpart in the reference. */
+int rnet_model_set_params_device(rnet_model* m, const float* d_params, size_t n);
 int rnet_model_get_params(rnet_model* m, float* host, size_t n);
 int rnet_model_get_grads(rnet_model* m, float* host, size_t n);
 /* Re-derive internal layouts after the caller wrote d_params directly. */
@@ -203,6 +206,12 @@ int rnet_model_set_conv_quirk(rnet_model* m, int on);
  * gradients, norms, scan, conv, slot selection and the optimizer stay fp32.
  * Parity with fp32 within 2e-2. */
 int rnet_model_set_precision(rnet_model* m, int precision);
+/* Activation recompute (no counterpart in the reference): 1 = keep only each
+ * layer's input from the forward and recompute the layer's caches right
+ * before its backward (one layer of caches resident instead of n_layers, at
+ * the cost of one more forward per step); results are unchanged. With it on,
+ * rnet_model_topk is unavailable. Default 0. */
+int rnet_model_set_recompute(rnet_model* m, int on);
 int rnet_model_forward(rnet_model* m, const int* d_tokens, float* d_logits, int batch,
                        int seq_len);
 int rnet_model_backward(rnet_model* m, const float* d_dlogits, const int* d_tokens, int batch,

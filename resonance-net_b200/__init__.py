@@ -76,10 +76,12 @@ _SIGS = {
     "rnet_model_stream": [_P, ctypes.POINTER(_P)],
     "rnet_model_set_params": [_P, _P, _SZ],
     "rnet_model_get_params": [_P, _P, _SZ],
+    "rnet_model_set_params_device": [_P, _P, _SZ],
     "rnet_model_get_grads": [_P, _P, _SZ],
     "rnet_model_params_updated": [_P],
     "rnet_model_set_conv_quirk": [_P, _I],
     "rnet_model_set_precision": [_P, _I],
+    "rnet_model_set_recompute": [_P, _I],
     "rnet_model_forward": [_P, _P, _P, _I, _I],
     "rnet_model_backward": [_P, _P, _P, _I, _I],
     "rnet_model_zero_grad": [_P],
@@ -217,6 +219,9 @@ class Model:
     def set_params(self, host) -> None:
         check(lib().rnet_model_set_params(self._h, _ptr(host), host.size))
 
+    def set_params_device(self, d_params) -> None:
+        check(lib().rnet_model_set_params_device(self._h, _ptr(d_params), self.num_params))
+
     def get_params(self):
         import numpy as np
         out = np.empty(self.num_params, np.float32)
@@ -235,6 +240,10 @@ class Model:
     def set_precision(self, bf16: bool) -> None:
         """GEMM arithmetic: fp32-accurate (default) or bf16 operands / fp32 accumulation."""
         check(lib().rnet_model_set_precision(self._h, int(bool(bf16))))
+
+    def set_recompute(self, on: bool) -> None:
+        """Keep only layer inputs and recompute each layer's caches in backward."""
+        check(lib().rnet_model_set_recompute(self._h, int(bool(on))))
 
     def forward(self, d_tokens, d_logits, batch: int, seq_len: int) -> None:
         check(lib().rnet_model_forward(self._h, _ptr(d_tokens), _ptr(d_logits), batch, seq_len))

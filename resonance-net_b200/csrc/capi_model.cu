@@ -115,6 +115,18 @@ int rnet_model_set_params(rnet_model* m, const float* host, size_t n) {
   CHECK_M(m);
   return m->e->set_params_host(host, n);
 }
+int rnet_model_set_params_device(rnet_model* m, const float* d_params, size_t n) {
+  CHECK_M(m);
+  if (!d_params) return rnet_status::fail(RNET_ERR_ARG, "null parameter buffer");
+  if (n != m->e->param_count())
+    return rnet_status::fail(RNET_ERR_ARG, "set_params_device: wrong parameter count");
+  RNET_TRY_CUDA(cudaMemcpyAsync(m->e->params(), d_params, n * sizeof(float),
+                                cudaMemcpyDeviceToDevice, m->e->stream()));
+  int rc = m->e->refresh_shadows();
+  if (rc) return rc;
+  RNET_TRY_CUDA(cudaStreamSynchronize(m->e->stream()));
+  return RNET_OK;
+}
 int rnet_model_get_params(rnet_model* m, float* host, size_t n) {
   CHECK_M(m);
   return m->e->get_params_host(host, n);
@@ -138,6 +150,11 @@ int rnet_model_set_precision(rnet_model* m, int precision) {
   if (precision != 0 && precision != 1)
     return rnet_status::fail(RNET_ERR_ARG, "rnet_model_set_precision: expected 0 (fp32) or 1 (bf16)");
   return m->e->set_precision(precision);
+}
+
+int rnet_model_set_recompute(rnet_model* m, int on) {
+  CHECK_M(m);
+  return m->e->set_recompute(on != 0);
 }
 
 int rnet_model_forward(rnet_model* m, const int* d_tokens, float* d_logits, int batch,

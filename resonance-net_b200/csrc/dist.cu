@@ -16,6 +16,7 @@
 #include <thread>
 
 #include "dist.h"
+#include "kernels.cuh"
 #include "status.h"
 
 namespace rnet_engine {
@@ -169,11 +170,24 @@ void dist_destroy(DistComm* d) {
 int dist_world(const DistComm* d) { return d ? d->world : 1; }
 int dist_rank(const DistComm* d) { return d ? d->rank : 0; }
 
-int dist_reduce_range(DistComm* d, float* buf, size_t count, cudaStream_t compute) {
+int dist_reduce_range(DistComm* d, float* buf, size_t count, cudaStream_t compute,
+                      __nv_bfloat16* scratch16) {
   if (!d || d->world <= 1 || count == 0) return RNET_OK;
   NcclApi& a = api();
   RNET_TRY_CUDA(cudaEventRecord(d->to_comm, compute));
   RNET_TRY_CUDA(cudaStreamWaitEvent(d->comm_stream, d->to_comm, 0));
+  if (scratch16) {
+    // bf16 on the wire: half the bytes; the summed bf16 values come back
+    // into the fp32 gradient (the comm stream orders the shared scratch)
+    RNET_TRY_CUDA(rnet_k::to_bf16(buf, scratch16, count, d->comm_stream));
+    ncclResult_t r = a.AllReduce(scratch16, scratch16, count, ncclBfloat16, ncclSum, d->comm,
+                                 d->comm_stream);
+    if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclAllReduce(bf16)");
+    int rc = d->settle("ncclAllReduce(bf16)");
+    if (rc) return rc;
+    RNET_TRY_CUDA(rnet_k::from_bf16(scratch16, buf, count, d->comm_stream));
+    return RNET_OK;
+  }
   ncclResult_t r = a.AllReduce(buf, buf, count, ncclFloat32, ncclSum, d->comm, d->comm_stream);
   if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclAllReduce");
   return d->settle("ncclAllReduce");

@@ -4,6 +4,7 @@
 // already loaded in the process, e.g. PyTorch's), so the library has no hard
 // link dependency and a missing NCCL is a clean RNET_ERR_NCCL.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -20,9 +21,11 @@ int dist_create(int rank, int world, int local_rank, const unsigned char uid[128
 void dist_destroy(DistComm* d);
 int dist_world(const DistComm* d);
 int dist_rank(const DistComm* d);
-// Enqueue an in-place fp32 sum all-reduce of buf[0:count] on the comm stream,
-// ordered after all work already queued on `compute`.
-int dist_reduce_range(DistComm* d, float* buf, size_t count, cudaStream_t compute);
+// Enqueue an in-place sum all-reduce of buf[0:count] on the comm stream,
+// ordered after all work already queued on `compute`: fp32 on the wire, or
+// bf16 when scratch16 (count bf16 elements) is given.
+int dist_reduce_range(DistComm* d, float* buf, size_t count, cudaStream_t compute,
+                      __nv_bfloat16* scratch16 = nullptr);
 // Make `compute` wait for every reduction enqueued so far.
 int dist_wait(DistComm* d, cudaStream_t compute);
 // Synchronous-order all-reduce on `stream` itself (drop-in dist_allreduce_sum).

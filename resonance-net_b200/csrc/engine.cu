@@ -73,6 +73,7 @@ Engine::~Engine() {
   cudaFree(VT_);
   cudaFree(params16_);
   cudaFree(KT16_);
+  cudaFree(comm16_);
   cudaFree(dKV_);
   for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
   cudaFree(scratch_);
@@ -244,11 +245,13 @@ int Engine::get_grads_host(float* h, size_t n) {
 
 int Engine::ensure_capacity(int N, bool with_caches) {
   const bool bf = precision == 1;
-  if (N <= cap_N_ && (cap_caches_ || !with_caches) && (cap_bf16_ || !bf)) return RNET_OK;
+  if (N <= cap_N_ && (cap_caches_ || !with_caches) && (cap_bf16_ || !bf) &&
+      cap_recompute_ == recompute_)
+    return RNET_OK;
   const size_t D = cfg_.d_model, F = cfg_.d_ff, S = cfg_.n_slots, V = cfg_.vocab_size;
   const size_t L = cfg_.n_layers, k = cfg_.slot_top_k;
   const size_t n = (size_t)N;
-  const size_t nact = with_caches ? L : 1;
+  const size_t nact = with_caches && !recompute_ ? L : 1;
   std::vector<std::pair<void**, size_t>> plan;  // (slot, bytes)
   act_.assign(nact, LayerAct{});
   auto f = [&](float** p, size_t cnt) { plan.push_back({(void**)p, cnt * sizeof(float)}); };
@@ -307,6 +310,7 @@ int Engine::ensure_capacity(int N, bool with_caches) {
   cap_N_ = N;
   cap_caches_ = with_caches;
   cap_bf16_ = bf;
+  cap_recompute_ = recompute_;
   have_cache_ = false;
   return RNET_OK;
 }
@@ -474,7 +478,7 @@ int Engine::forward(const int* d_tokens, float* d_logits, int B, int T) {
   for (int l = 0; l < cfg_.n_layers; ++l) {
     const float* Xl = caches ? X_ + (size_t)l * ND : X_ + (size_t)(l & 1) * ND;
     float* Xn = caches ? X_ + (size_t)(l + 1) * ND : X_ + (size_t)((l + 1) & 1) * ND;
-    rc = layer_forward(l, Xl, Xn, caches ? act_[l] : act_[0], B, T, caches);
+    rc = layer_forward(l, Xl, Xn, caches && !recompute_ ? act_[l] : act_[0], B, T, caches);
     if (rc) return rc;
   }
   const float* XL = caches ? X_ + (size_t)cfg_.n_layers * ND : X_ + (size_t)(cfg_.n_layers & 1) * ND;
@@ -510,7 +514,7 @@ int Engine::layer_backward(int l, int B, int T) {
   const int N = B * T, D = cfg_.d_model, F = cfg_.d_ff, S = cfg_.n_slots, k = cfg_.slot_top_k;
   const LayerParams& w = W_[l];
   const LayerParams& g = G_[l];
-  LayerAct& a = act_[l];
+  LayerAct& a = recompute_ ? act_[0] : act_[l];
   unsigned* err = rnet_status::device_error_word();
   cudaStream_t s = stream_;
   const float* Xl = X_ + (size_t)l * N * D;
@@ -602,11 +606,35 @@ int Engine::backward(const float* d_dlogits, const int* d_tokens, int B, int T) 
   const int N = B * T;
   int rc = head_backward(d_dlogits, N);
   if (rc) return rc;
+  const size_t ND = (size_t)N * cfg_.d_model;
+  // bf16 mode: gradient buckets travel as bf16 (one staging buffer of the
+  // largest bucket; the comm stream orders its reuse)
+  __nv_bfloat16* c16 = nullptr;
+  if (dist && precision == 1) {
+    const size_t need = std::max(G_[0].count, 2 * (size_t)cfg_.vocab_size * cfg_.d_model +
+                                                  (size_t)cfg_.d_model);
+    if (comm16_count_ < need) {
+      CK(cudaStreamSynchronize(stream_));
+      cudaFree(comm16_);
+      comm16_ = nullptr;
+      CK(cudaMalloc(&comm16_, need * sizeof(__nv_bfloat16)));
+      comm16_count_ = need;
+    }
+    c16 = comm16_;
+  }
   for (int l = cfg_.n_layers - 1; l >= 0; --l) {
+    // recompute mode: the caches in act_[0] are the last layer's after the
+    // forward; every other layer's are rebuilt from its kept input (the
+    // recomputed output X[l+1] equals the stored one: same kernels, same
+    // inputs, no atomics in the forward)
+    if (recompute_ && l != cfg_.n_layers - 1) {
+      rc = layer_forward(l, X_ + (size_t)l * ND, X_ + (size_t)(l + 1) * ND, act_[0], B, T, true);
+      if (rc) return rc;
+    }
     rc = layer_backward(l, B, T);
     if (rc) return rc;
     if (dist) {
-      rc = dist_reduce_range(dist, grads_ + G_[l].offset, G_[l].count, stream_);
+      rc = dist_reduce_range(dist, grads_ + G_[l].offset, G_[l].count, stream_, c16);
       if (rc) return rc;
     }
   }
@@ -614,7 +642,7 @@ int Engine::backward(const float* d_dlogits, const int* d_tokens, int B, int T) 
        rnet_k::embed_bwd(dX_, d_tokens, g_embed_, N, cfg_.vocab_size, cfg_.d_model, stream_));
   if (dist) {
     rc = dist_reduce_range(dist, grads_, 2 * (size_t)cfg_.vocab_size * cfg_.d_model + cfg_.d_model,
-                           stream_);
+                           stream_, c16);
     if (rc) return rc;
   }
   return RNET_OK;
@@ -812,9 +840,17 @@ int Engine::generate(Decoder* d, int n_steps, int* d_out, bool use_graph) {
   return RNET_OK;
 }
 
+int Engine::set_recompute(bool on) {
+  recompute_ = on;
+  have_cache_ = false;
+  return RNET_OK;
+}
+
 int Engine::topk(int layer, int** idx, float** w) {
   if (!have_cache_ || layer < 0 || layer >= cfg_.n_layers)
     return rnet_status::fail(RNET_ERR_ARG, "topk: no cached forward or bad layer");
+  if (recompute_)
+    return rnet_status::fail(RNET_ERR_ARG, "topk: selections are not kept with recompute on");
   *idx = act_[layer].idx;
   *w = act_[layer].w;
   return RNET_OK;

@@ -147,6 +147,12 @@ class Engine {
   // workspace capacity in tokens
   int ensure_capacity(int N, bool with_caches);
 
+  // Activation recompute: keep only the layer inputs X[0..L] from the
+  // forward and recompute each layer's caches right before its backward
+  // (one layer of caches in memory instead of L; one extra forward per step).
+  int set_recompute(bool on);
+  bool recompute() const { return recompute_; }
+
   // profiling
   void profile_enable(bool on) { prof_on_ = on; }
   int profile_read(ProfStats* out, bool reset);
@@ -205,6 +211,10 @@ class Engine {
   __nv_bfloat16 *nfh_ = nullptr, *dlogitsh_ = nullptr, *dXh_ = nullptr, *dGUh_ = nullptr,
                 *dqh_ = nullptr, *dPZHh_ = nullptr;
   bool cap_bf16_ = false;
+  bool recompute_ = false;
+  __nv_bfloat16* comm16_ = nullptr;  // bf16 all-reduce staging (bf16 mode, DP)
+  size_t comm16_count_ = 0;
+  bool cap_recompute_ = false;
   bool have_cache_ = false;
   int last_B_ = 0, last_T_ = 0;
 };

@@ -26,6 +26,8 @@ cudaError_t rms_norm_bwd(const float* dy, const float* x, const float* w, const 
                          __nv_bfloat16* dx16 = nullptr);
 // y = bf16(x), n elements (x, y 16-byte aligned when n % 8 == 0 is used).
 cudaError_t to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s);
+// y = float(x), n elements.
+cudaError_t from_bf16(const __nv_bfloat16* x, float* y, size_t n, cudaStream_t s);
 
 // ---- depthwise causal convolution (causal_conv.cu) -------------------------
 // c3/c7/c15 of x over each length-T sequence, S = c3 + c7 + c15.

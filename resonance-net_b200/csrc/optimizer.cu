@@ -107,6 +107,14 @@ __global__ void to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __res
     for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) y[i] = __float2bfloat16_rn(x[i]);
 }
 
+__global__ void from_bf16_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ y,
+                                 size_t n) {
+  rnet_dev::pdl_trigger();
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    y[i] = __bfloat162float(x[i]);
+}
+
 }  // namespace
 
 size_t sgd_scratch_floats() { return 2 * NORM_BLOCKS + 8; }
@@ -119,6 +127,14 @@ cudaError_t to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) 
   if (grid > 148 * 8) grid = 148 * 8;
   if (grid < 1) grid = 1;
   to_bf16_kernel<<<(unsigned)grid, 256, 0, s>>>(x, y, n);
+  return launched();
+}
+
+cudaError_t from_bf16(const __nv_bfloat16* x, float* y, size_t n, cudaStream_t s) {
+  if (!n) return cudaSuccess;
+  size_t grid = (n + 255) / 256;
+  if (grid > 148 * 8) grid = 148 * 8;
+  from_bf16_kernel<<<(unsigned)grid, 256, 0, s>>>(x, y, n);
   return launched();
 }
 

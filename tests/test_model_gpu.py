@@ -162,3 +162,35 @@ def test_train_step_host_matches_device_step(rnet, rdata, orc, cuda):
     assert abs(float(loss.item()) - lp) <= 1e-6 * abs(lp)
     a.close()
     b.close()
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_recompute_matches_cached_step(rnet, rdata, orc, cuda, bf16):
+    """Activation recompute (only layer inputs kept; each layer's caches
+    rebuilt before its backward) gives the same step as full caches: same
+    loss bit for bit, parameters within the atomic-order noise (1e-6)."""
+    torch = cuda
+    c = dict(CASES["cfg_small"])
+    cfg, params, tok, tgt = _make(orc, rdata, c)
+    rcfg = _rcfg(rnet, cfg)
+    B, T = c["B"], c["T"]
+    d_in = torch.from_numpy(tok.reshape(-1)).cuda()
+    d_tgt = torch.from_numpy(tgt.reshape(-1)).cuda()
+    outs = []
+    for rec in (False, True):
+        m = rnet.Model(rcfg, device=0, reference_init=False)
+        m.set_params(params)
+        m.set_precision(bf16)
+        m.set_recompute(rec)
+        loss = torch.zeros(1, device="cuda")
+        for _ in range(2):
+            m.train_step(d_in, d_tgt, B, T, 3e-4, 1.0, loss)
+        m.synchronize()
+        outs.append((float(loss.item()), m.get_grads(), m.get_params()))
+        if rec:
+            with pytest.raises(rnet.RnetError):
+                m.topk_host(0, B * T)
+        m.close()
+    assert abs(outs[0][0] - outs[1][0]) <= 1e-6 * abs(outs[0][0])
+    assert rel_err(outs[1][1], outs[0][1]) <= 1e-6
+    assert update_rel_err(params, outs[1][2], outs[0][2]) <= 1e-5
