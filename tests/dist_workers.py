@@ -104,6 +104,7 @@ def dp_engine(rank, world, port, out_dir, case):
                                 vocab=case["vocab"], seq_len=case["T"])
     m = rnet.Model(cfg, device=rank, reference_init=False)
     m.set_params(rdata.init_params_normal(cfg, seed=case["pseed"]))
+    m.set_precision(case.get("bf16", False))  # bf16 mode: bf16 gradient all-reduce
     uid = [rnet.Dist.unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
     d = rnet.Dist(rank, world, rank, uid[0])

@@ -21,13 +21,16 @@ def _port():
     return p
 
 
-def test_dp_two_gpus_matches_one(rnet, rdata, cuda, tmp_path):
+@pytest.mark.parametrize("bf16", [False, True])
+def test_dp_two_gpus_matches_one(rnet, rdata, cuda, tmp_path, bf16):
+    """bf16: bf16 GEMM operands on both sides and bf16 on the wire for the
+    two-GPU gradient all-reduce; compared at the bf16 tolerance (2e-2)."""
     torch = cuda
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     case = dict(d_model=64, n_layers=2, d_ff=128, n_slots=64, top_k=2, vocab=256, B=4, T=64,
-                pseed=1234, tseed=3, lr=3e-4, clip=1.0)
+                pseed=1234, tseed=3, lr=3e-4, clip=1.0, bf16=bf16)
     mp.spawn(dist_workers.dp_engine, args=(2, _port(), str(tmp_path), case), nprocs=2, join=True)
     dp = np.load(tmp_path / "dp_engine_params.npy").astype(np.float64)
     cfg = rnet.ModelConfig.make(d_model=case["d_model"], n_layers=case["n_layers"],
@@ -36,6 +39,7 @@ def test_dp_two_gpus_matches_one(rnet, rdata, cuda, tmp_path):
     m = rnet.Model(cfg, device=0, reference_init=False)
     params = rdata.init_params_normal(cfg, seed=case["pseed"])
     m.set_params(params)
+    m.set_precision(bf16)
     tok, tgt = rdata.uniform_tokens(case["B"], case["T"], seed=case["tseed"])
     d_in = torch.from_numpy(tok.reshape(-1)).cuda()
     d_tg = torch.from_numpy(tgt.reshape(-1)).cuda()
@@ -48,4 +52,5 @@ def test_dp_two_gpus_matches_one(rnet, rdata, cuda, tmp_path):
     rel = np.linalg.norm((dp - p64) - (one - p64)) / np.linalg.norm(one - p64)
     # both updates are fp32 parameters minus ~1e-6-sized steps: ~1e-3 of
     # rounding in the recovered updates, far below a wrong reduction (~1)
-    assert rel <= 5e-3, f"two-GPU step differs from the one-GPU step: {rel:.2e}"
+    tol = 2e-2 if bf16 else 5e-3
+    assert rel <= tol, f"two-GPU step differs from the one-GPU step: {rel:.2e}"
