@@ -61,7 +61,7 @@ def parse():
                     help="bf16 GEMM operands with fp32 accumulation (default: fp32-accurate)")
     # single-operation mode (profiling captures of one kernel class)
     ap.add_argument("--op", default=None,
-                    help="gemm | scan_fwd | scan_bwd | conv_fwd | conv_bwd | rms_fwd | rms_bwd")
+                    help="gemm | gemm16 | scan_fwd | scan_bwd | conv_fwd | conv_bwd | rms_fwd | rms_bwd")
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=512)
     ap.add_argument("--k", type=int, default=512)
@@ -69,6 +69,8 @@ def parse():
     ap.add_argument("--cg", type=int, default=0, help="--op: GEMM CTA group (0 auto, 1, 2)")
     ap.add_argument("--decode", action="store_true",
                     help="config 4: prefill + batched greedy decode instead of training")
+    ap.add_argument("--no-bf16", action="store_true",
+                    help="skip the bf16-mode object of the default (1-GPU) line")
     ap.add_argument("--no-decode", action="store_true",
                     help="skip the config-4 decode object of the default (1-GPU) line")
     ap.add_argument("--streams", type=int, default=256, help="--decode: streams over all GPUs")
@@ -385,11 +387,47 @@ def run_ours(args, rank, world, local):
     }
     if world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(importlib.import_module("resonance-net_b200.data"))
+    if world == 1 and not args.bf16 and args.model == "c2" and not args.no_bf16:
+        out["bf16"] = bf16_measure(model, rnet, torch, stream, d_in, d_tg, B, T, args, peaks)
     _finish(pg, model, dist_h)
     if world == 1 and not args.no_decode:
         out["decode"] = decode_measure(rnet, rdata, torch, None, 0, 1, local, args.streams,
                                        args.prompt, args.gen, args.warmup, args.steps)
     print(json.dumps(out), flush=True)
+
+
+def bf16_measure(model, rnet, torch, stream, d_in, d_tg, B, T, args, peaks):
+    """The same config-2 step with bf16 GEMM operands (rnet_model_set_precision
+    1): device-resident tok/s and the GEMM class against the bf16 peak."""
+    model.set_precision(True)
+    d_loss = torch.zeros(1, device="cuda")
+    for i in range(args.warmup):
+        model.train_step(d_in[i % POOL], d_tg[i % POOL], B, T, LR, CLIP, d_loss)
+    model.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        model.train_step(d_in[i % POOL], d_tg[i % POOL], B, T, LR, CLIP, d_loss)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    model.profile_enable(True)
+    model.profile_read(reset=True)
+    for i in range(args.steps):
+        model.train_step(d_in[i % POOL], d_tg[i % POOL], B, T, LR, CLIP, d_loss)
+    g = model.profile_read(reset=True)["gemm"]
+    model.profile_enable(False)
+    model.set_precision(False)
+    tf = g["flops"] / (g["ms"] * 1e-3) / 1e12 if g["ms"] > 0 else 0.0
+    return {"metric": METRIC + " with bf16 GEMM operands", "value":
+            round(B * T * args.steps / (ms * 1e-3), 1), "unit": UNIT,
+            "ms_per_step": round(ms / args.steps, 3),
+            "dtype": "bf16 GEMM operands (bf16 copies in memory), fp32 accumulate, fp32 master "
+                     "weights and non-GEMM work",
+            "gemm_ms_per_step": round(g["ms"] / args.steps, 3),
+            "roofline": {"bound": "tensor", "kernel": "gemm_tf32x3 MODE 2 (bf16 tiles)",
+                         "achieved": round(tf, 2), "peak": peaks["bf16_sust"],
+                         "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_sust"], 4)}}
 
 
 def _finish(pg, model, dist_h):
@@ -535,6 +573,17 @@ def run_op(args):
         fn = lambda: rnet.call("rnet_gemm_f32", M, Nn, K, p(A), lda, args.amn, p(Bm), ldb,
                                args.bmn, p(C), Nn, p(R), Nn, args.epi, F32(1.0), None)
         work = (f"gemm M={M} N={Nn} K={K} a_mn={args.amn} b_mn={args.bmn} cg={args.cg} "
+                f"epi={args.epi}")
+    elif args.op == "gemm16":
+        M, Nn, K = args.m, args.n, args.k
+        A = (rnd(K, M) if args.amn else rnd(M, K)).bfloat16()
+        Bm = (rnd(K, Nn) if args.bmn else rnd(Nn, K)).bfloat16()
+        C = z(M, Nn)
+        lda, ldb = (M if args.amn else K), (Nn if args.bmn else K)
+        R = rnd(M, Nn)
+        fn = lambda: rnet.call("rnet_gemm_bf16", M, Nn, K, p(A), lda, args.amn, p(Bm), ldb,
+                               args.bmn, p(C), Nn, p(R), Nn, args.epi, F32(1.0), None, None)
+        work = (f"gemm bf16 M={M} N={Nn} K={K} a_mn={args.amn} b_mn={args.bmn} cg={args.cg} "
                 f"epi={args.epi}")
     elif args.op in ("scan_fwd", "scan_bwd"):
         x = rnd(N, D)

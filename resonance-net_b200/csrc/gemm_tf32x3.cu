@@ -61,6 +61,12 @@ struct KParams {
   // split-K into a workspace: split ks stores its partial at epi.C + ks *
   // split_stride (0: no workspace split)
   long long split_stride;
+  // 1: store / accumulate / residual tiles go through the warp's shared-memory
+  // tile (coalesced 128-byte rows) instead of thread-per-row stores. Used with
+  // bf16 tiles, where the MMAs finish a tile fast enough that thread-per-row
+  // stores (32 lines per instruction) would bound the kernel, and no split
+  // warps compete for shared memory.
+  int stage_epi;
   Epilogue epi;
   unsigned* err;
 };
@@ -70,7 +76,7 @@ struct KParams {
 // ELEM = bytes per staged element (4: fp32 tiles; 2: bf16 tiles read straight
 // from bf16 operands), LO = a twin buffer per stage (the split warps' lo or
 // bf16 tiles).
-template <int BN, int BK, int CG, int ELEM = 4, bool LO = true>
+template <int BN, int BK, int CG, int ELEM = 4, bool LO = true, int NEPI = NUM_EPI_WARPS>
 struct Cfg {
   static constexpr int ROW_BYTES = BK * ELEM;         // K-major row (64 or 128 B)
   static constexpr int MN_ELEMS = 128 / ELEM;         // MN-major box width (one 128 B row)
@@ -80,10 +86,12 @@ struct Cfg {
   static constexpr int B_BYTES = B_ROWS * BK * ELEM;
   static constexpr int RAW_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGE_BYTES = LO ? 2 * RAW_BYTES : RAW_BYTES;  // raw (= hi) + lo
-  static constexpr int STAGES_FIT = SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int EPI_BYTES = NEPI * EPI_TILE_FLOATS * 4;
+  // more epilogue warps take their tiles out of the stage budget
+  static constexpr int STAGES_FIT =
+      (SMEM_BUDGET - (NEPI - NUM_EPI_WARPS) * EPI_TILE_FLOATS * 4) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int EPI_BYTES = NUM_EPI_WARPS * EPI_TILE_FLOATS * 4;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
   // UMMA smem-descriptor parameters
   static constexpr uint32_t K_LAYOUT = ROW_BYTES == 128 ? 2u : 4u;  // SWIZZLE_128B / _64B
@@ -267,14 +275,19 @@ struct Top2State {
 
 // One accumulator sub-tile (128 rows x BN columns); warp q handles rows
 // row0 = m0 + 32q .. +31, `st` is the warp's smem tile.
+// cfirst / cstep: this warp's share of the 32-column chunks when several
+// warps serve one TMEM lane quadrant (store / accumulate / residual kinds
+// only; the SwiGLU and top-2 kinds run on the cfirst == 0 warp).
 template <int BN>
 __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc, int row0,
                                                  int nt, bool last_sub, Top2State& st,
-                                                 float* tile, size_t c_off) {
+                                                 float* tile, size_t c_off, int cfirst = 0,
+                                                 int cstep = 1) {
   const Epilogue& e = p.epi;
   const int lane = threadIdx.x & 31;
   const int row = row0 + lane;
   float v[32];
+  if ((e.kind == EPI_SWIGLU_FWD || e.kind == EPI_TOP2) && cfirst != 0) return;
   if (e.kind == EPI_SWIGLU_FWD) {
     constexpr int HALF_CHUNKS = BN / 64;
 #pragma unroll 1
@@ -321,14 +334,27 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
     }
     return;
   }
+  if (p.stage_epi) {
+    const int op = e.kind == EPI_STORE ? 0 : (e.kind == EPI_ACCUM ? 1 : 2);
+#pragma unroll 1
+    for (int c = cfirst; c < BN / 32; c += cstep) {
+      tmem_ld_32cols(tacc + c * 32, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= e.alpha;
+      tile_out(tile, v, e.C + c_off, e.ldc, e.R, e.ldr, row0, nt * BN + c * 32, p.M, p.N, op,
+               op == 1 ? nullptr : e.C16);
+    }
+    return;
+  }
   // residual: this thread's 32-column slice of row `row` is one 128-byte
   // line; the next chunk's line is pulled into L1 while this one is stored
   const bool resid = e.kind == EPI_RESID && row < p.M;
   const float* rrow = e.R + (size_t)row * e.ldr + nt * BN;
-  if (resid && nt * BN < p.N) prefetch_l1(rrow);
+  if (resid && nt * BN + cfirst * 32 < p.N) prefetch_l1(rrow + cfirst * 32);
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
-    if (resid && c + 1 < BN / 32 && nt * BN + (c + 1) * 32 < p.N) prefetch_l1(rrow + (c + 1) * 32);
+  for (int c = cfirst; c < BN / 32; c += cstep) {
+    if (resid && c + cstep < BN / 32 && nt * BN + (c + cstep) * 32 < p.N)
+      prefetch_l1(rrow + (c + cstep) * 32);
     tmem_ld_32cols(tacc + c * 32, v);
     store_row_chunk(p, e.kind, row, nt * BN + c * 32, v, c_off);
   }
@@ -406,7 +432,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                        const __grid_constant__ CUtensorMap tmB, const KParams p) {
   rnet_dev::pdl_trigger();
   constexpr bool BF = MODE == 1;
-  using C = Cfg<BN, BK, CG, MODE == 2 ? 2 : 4, MODE != 2>;
+  // MODE 2: four of the idle split warps (6-9) become a second epilogue set
+  constexpr int NEPI = MODE == 2 ? 2 * NUM_EPI_WARPS : NUM_EPI_WARPS;
+  constexpr int RELAY_WARP = FIRST_SPLIT_WARP + NUM_SPLIT_WARPS - 1;
+  using C = Cfg<BN, BK, CG, MODE == 2 ? 2 : 4, MODE != 2, NEPI>;
   constexpr bool PAIR = CG == 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -436,7 +465,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], NUM_EPI_WARPS * CG);
+      mbar_init(&acce[b], NEPI * CG);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -568,12 +597,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       volatile int no_abort = 0;
       mbar_wait(drain, 0, p.err, &no_abort);
     }
-  } else if (warp >= FIRST_SPLIT_WARP) {
+  } else if (warp >= FIRST_SPLIT_WARP && !(MODE == 2 && warp < FIRST_SPLIT_WARP + 4)) {
    if constexpr (MODE == 2 && CG == 2) {
     // bf16 tiles need no split work, but the pair's MMA (issued by the even
     // CTA) reads both CTAs' tiles: one thread per CTA relays "this CTA's
     // tiles of stage s have landed" to the even CTA's split[s] barrier
-    if (warp == FIRST_SPLIT_WARP && lane == 0) {
+    if (warp == RELAY_WARP && lane == 0) {
       uint32_t it = 0;
       bool ok = true;
       for (int unit = group; unit < p.num_units && ok; unit += n_groups) {
@@ -663,8 +692,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
    }
-  } else {  // epilogue warps 0..3
-    const int q = warp;  // TMEM lane quadrant
+  } else {  // epilogue warps 0..3 (+ 6..9 in MODE 2)
+    const int q = warp & 3;  // TMEM lane quadrant (warp i may access lanes 32 (i % 4) + ...)
+    const int eset = warp < NUM_EPI_WARPS ? 0 : 1;
+    const int eslot = eset * NUM_EPI_WARPS + q;
     uint32_t tc = 0;
     bool ok = true;
     for (int unit = group; unit < p.num_units && ok; unit += n_groups) {
@@ -682,7 +713,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const size_t c_off =
             p.split_stride ? (size_t)p.split_stride * (size_t)(kb0 / p.kb_per_split) : 0;
         epilogue_subtile<BN>(p, tacc, row0, nt, nt == nt1 - 1, st,
-                             epi_tiles + q * EPI_TILE_FLOATS, c_off);
+                             epi_tiles + eslot * EPI_TILE_FLOATS, c_off, eset,
+                             NEPI / NUM_EPI_WARPS);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -774,7 +806,8 @@ int num_sms() {
 template <int BN, int BK, int CG, int MODE>
 static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
                           const KParams& kp) {
-  using C = Cfg<BN, BK, CG, MODE == 2 ? 2 : 4, MODE != 2>;
+  using C = Cfg<BN, BK, CG, MODE == 2 ? 2 : 4, MODE != 2,
+                MODE == 2 ? 2 * NUM_EPI_WARPS : NUM_EPI_WARPS>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BK, CG, MODE>,
@@ -983,6 +1016,7 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   kp.b_mn = B.mn_major ? 1 : 0;
   kp.epi = epi;
   kp.err = err_word;
+  kp.stage_epi = st16 ? 1 : 0;
 
   int splits = 1;
   if (ws_splits > 1) {
