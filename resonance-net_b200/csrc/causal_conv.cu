@@ -101,9 +101,12 @@ __device__ __forceinline__ void fwd_steps(const float (&win)[WIN], const float (
 // kernel K reads x[t - l] with l = K-1-k, so c7 + c15 = sum_l u[l] x[t - l],
 // u[l] = w15[14-l] + w7[6-l] (l <= 6): 15 multiply-adds instead of 22; then
 // S = c3 + u and Sq = S + u (= S + c7 + c15). Window row j = x[t0 + r0 - 14 + j].
-template <bool WQ, bool FULL>
+__device__ __forceinline__ void st_out(float* p, float v) { *p = v; }
+__device__ __forceinline__ void st_out(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+template <bool WQ, bool FULL, typename OT>
 __device__ __forceinline__ void fwd_steps_merged(const float (&win)[WIN], const float (&b3)[3],
-                                                 const float (&u)[15], float* pS, float* pQ,
+                                                 const float (&u)[15], OT* pS, OT* pQ,
                                                  int n, int D) {
 #pragma unroll
   for (int i = 0; i < STEPS; ++i) {
@@ -114,20 +117,22 @@ __device__ __forceinline__ void fwd_steps_merged(const float (&win)[WIN], const 
 #pragma unroll
     for (int l = 14; l >= 0; --l) su += win[i + HALO - l] * u[l];
     const float sum = s3 + su;
-    *pS = sum;
+    st_out(pS, sum);
     pS += D;
     if (WQ) {
-      *pQ = sum + su;
+      st_out(pQ, sum + su);
       pQ += D;
     }
   }
 }
 
-template <bool WQ, bool WC>
+// OT: output element type of S / Sq (float, or bf16 for the bf16 GEMM path,
+// which needs no fp32 copy of S); c7 / c15 outputs exist for OT = float only.
+template <bool WQ, bool WC, typename OT = float>
 __global__ void __launch_bounds__(NW * 32, 3)
     conv_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w3,
                     const float* __restrict__ w7, const float* __restrict__ w15,
-                    float* __restrict__ S, float* __restrict__ Sq, float* __restrict__ c7o,
+                    OT* __restrict__ S, OT* __restrict__ Sq, float* __restrict__ c7o,
                     float* __restrict__ c15o, int B, int T, int D, int nseg, int nparts) {
   rnet_dev::pdl_trigger();
   // persistent over tiles (b, segment) = p, p + nparts, ... of one channel
@@ -174,16 +179,16 @@ __global__ void __launch_bounds__(NW * 32, 3)
       const int tb = t0 + r0;
       const size_t o = ((size_t)b * T + tb) * D + d;
       const int n = T - tb < STEPS ? T - tb : STEPS;
-      if (WC) {  // layer-op caches need c7 and c15 separately
+      if constexpr (WC) {  // layer-op caches need c7 and c15 separately
         if (n == STEPS)
           fwd_steps<WQ, WC, true>(win, a3, a7, a15, S + o, Sq + o, c7o + o, c15o + o, STEPS, D);
         else if (n > 0)
           fwd_steps<WQ, WC, false>(win, a3, a7, a15, S + o, Sq + o, c7o + o, c15o + o, n, D);
       } else {
         if (n == STEPS)
-          fwd_steps_merged<WQ, true>(win, b3, u, S + o, Sq + o, STEPS, D);
+          fwd_steps_merged<WQ, true, OT>(win, b3, u, S + o, Sq + o, STEPS, D);
         else if (n > 0)
-          fwd_steps_merged<WQ, false>(win, b3, u, S + o, Sq + o, n, D);
+          fwd_steps_merged<WQ, false, OT>(win, b3, u, S + o, Sq + o, n, D);
       }
     }
     __syncthreads();  // buffer `buf` is restaged PIPE - 1 iterations on
@@ -603,6 +608,26 @@ cudaError_t conv_fwd(const float* x, const float* w3, const float* w7, const flo
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid(groups, np);
   kern<<<grid, NW * 32, smem, s>>>(x, w3, w7, w15, S, Sq, c7, c15, B, T, D, nseg, np);
+  return launched();
+}
+
+cudaError_t conv_fwd_bf16(const float* x, const float* w3, const float* w7, const float* w15,
+                          __nv_bfloat16* S16, __nv_bfloat16* Sq16, int B, int T, int D,
+                          cudaStream_t s) {
+  if (B <= 0 || T <= 0) return cudaSuccess;
+  if (D % 4 || !S16) return cudaErrorInvalidValue;
+  const int nseg = (T + TS - 1) / TS;
+  const int groups = (D + CW - 1) / CW;
+  int np = (148 * 3) / groups;
+  if (np > B * nseg) np = B * nseg;
+  if (np < 1) np = 1;
+  constexpr size_t smem = PIPE * ROWS * CW * sizeof(float);
+  auto kern = Sq16 ? conv_fwd_kernel<true, false, __nv_bfloat16>
+                   : conv_fwd_kernel<false, false, __nv_bfloat16>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(groups, np);
+  kern<<<grid, NW * 32, smem, s>>>(x, w3, w7, w15, S16, Sq16, nullptr, nullptr, B, T, D, nseg,
+                                   np);
   return launched();
 }
 

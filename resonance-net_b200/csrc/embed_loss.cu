@@ -164,9 +164,17 @@ __device__ __forceinline__ void swiglu_grad1(float dh, float g, float u, float& 
   du = dh * (g * sig);
 }
 
+__device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float4 v) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t*>(&a);
+  u.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
 __global__ void swiglu_bwd_pointwise_v4(float* __restrict__ dgu, int ld,
                                         const float* __restrict__ G, const float* __restrict__ U,
-                                        int N, int F) {
+                                        int N, int F, __nv_bfloat16* __restrict__ dgu16) {
   rnet_dev::pdl_trigger();
   const int F4 = F >> 2;
   const size_t n4 = (size_t)N * F4;
@@ -184,14 +192,19 @@ __global__ void swiglu_bwd_pointwise_v4(float* __restrict__ dgu, int ld,
     swiglu_grad1(dh.y, g.y, u.y, dg.y, du.y);
     swiglu_grad1(dh.z, g.z, u.z, dg.z, du.z);
     swiglu_grad1(dh.w, g.w, u.w, dg.w, du.w);
-    *pg = dg;
-    *pu = du;
+    if (dgu16) {
+      st_bf16x4(dgu16 + r * ld + c, dg);
+      st_bf16x4(dgu16 + r * ld + F + c, du);
+    } else {
+      *pg = dg;
+      *pu = du;
+    }
   }
 }
 
 __global__ void swiglu_bwd_pointwise_1(float* __restrict__ dgu, int ld,
                                        const float* __restrict__ G, const float* __restrict__ U,
-                                       int N, int F) {
+                                       int N, int F, __nv_bfloat16* __restrict__ dgu16) {
   rnet_dev::pdl_trigger();
   const size_t n = (size_t)N * F;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
@@ -200,8 +213,13 @@ __global__ void swiglu_bwd_pointwise_1(float* __restrict__ dgu, int ld,
     const int c = (int)(i - r * F);
     float dg, du;
     swiglu_grad1(dgu[r * ld + c], G[i], U[i], dg, du);
-    dgu[r * ld + c] = dg;
-    dgu[r * ld + F + c] = du;
+    if (dgu16) {
+      dgu16[r * ld + c] = __float2bfloat16_rn(dg);
+      dgu16[r * ld + F + c] = __float2bfloat16_rn(du);
+    } else {
+      dgu[r * ld + c] = dg;
+      dgu[r * ld + F + c] = du;
+    }
   }
 }
 
@@ -276,15 +294,16 @@ cudaError_t add3(const float* a, const float* b, const float* c, float* out, siz
 }
 
 cudaError_t swiglu_bwd_pointwise(float* dgu, int ld, const float* G, const float* U, int N, int F,
-                                 cudaStream_t s) {
+                                 cudaStream_t s, __nv_bfloat16* dgu16) {
   if (N <= 0 || F <= 0) return cudaSuccess;
   const bool v4 = (F % 4 == 0) && (ld % 4 == 0) &&
                   ((reinterpret_cast<uintptr_t>(dgu) | reinterpret_cast<uintptr_t>(G) |
-                    reinterpret_cast<uintptr_t>(U)) & 15) == 0;
+                    reinterpret_cast<uintptr_t>(U) | reinterpret_cast<uintptr_t>(dgu16)) & 15) == 0;
   if (v4)
-    swiglu_bwd_pointwise_v4<<<ew_grid((size_t)N * F / 4), 256, 0, s>>>(dgu, ld, G, U, N, F);
+    swiglu_bwd_pointwise_v4<<<ew_grid((size_t)N * F / 4), 256, 0, s>>>(dgu, ld, G, U, N, F,
+                                                                       dgu16);
   else
-    swiglu_bwd_pointwise_1<<<ew_grid((size_t)N * F), 256, 0, s>>>(dgu, ld, G, U, N, F);
+    swiglu_bwd_pointwise_1<<<ew_grid((size_t)N * F), 256, 0, s>>>(dgu, ld, G, U, N, F, dgu16);
   return launched();
 }
 

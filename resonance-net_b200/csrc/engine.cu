@@ -404,18 +404,22 @@ int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B,
   // into them (red.add: the same single rounding as R + acc, without the
   // epilogue's dependent residual loads).
   PROF(PK_RMS_FWD, 0, 3 * ND4, rnet_k::rms_norm_fwd(Xl, w.n1, a.n1, a.rinv1, N, D, eps, s, a.r1));
-  PROF(PK_CONV_FWD, 50.0 * N * D, (conv_quirk ? 3 : 2) * ND4,
-       rnet_k::conv_fwd(a.n1, w.c3, w.c7, w.c15, a.S, conv_quirk ? a.Sq : nullptr, nullptr,
-                        nullptr, B, T, D, s));
-  if (bf) {
-    PROF(PK_OTHER, 0, 6.0 * N * D, rnet_k::to_bf16(a.S, a.Sh, (size_t)N * D, s));
-    if (train && conv_quirk)
-      PROF(PK_OTHER, 0, 6.0 * N * D, rnet_k::to_bf16(a.Sq, a.Sqh, (size_t)N * D, s));
-  }
+  // bf16 mode: S (and the dmix operand Sq) only as the bf16 copies the
+  // GEMMs read; the fp32 ones would never be read
+  const double ND2 = 2.0 * N * D;
+  if (bf)
+    PROF(PK_CONV_FWD, 50.0 * N * D, ND4 + (train && conv_quirk ? 2 : 1) * ND2,
+         rnet_k::conv_fwd_bf16(a.n1, w.c3, w.c7, w.c15, a.Sh, train && conv_quirk ? a.Sqh : nullptr,
+                               B, T, D, s));
+  else
+    PROF(PK_CONV_FWD, 50.0 * N * D, (conv_quirk ? 3 : 2) * ND4,
+         rnet_k::conv_fwd(a.n1, w.c3, w.c7, w.c15, a.S, conv_quirk ? a.Sq : nullptr, nullptr,
+                          nullptr, B, T, D, s));
   MM_RES(N, D, D, kop(bf, a.S, a.Sh, D), kop(bf, w.mix, bf ? h16(w.mix) : nullptr, D), a.r1);
   // 2. MinGRU (:301-313): P = n2 [Wz;Wh]^T, fused gate + scan + residual
-  PROF(PK_RMS_FWD, 0, 2 * ND4,
-       rnet_k::rms_norm_fwd(a.r1, w.n2, a.n2, a.rinv2, N, D, eps, s, nullptr, a.n2h));
+  PROF(PK_RMS_FWD, 0, ND4 + (bf ? ND2 : ND4),
+       rnet_k::rms_norm_fwd(a.r1, w.n2, bf ? nullptr : a.n2, a.rinv2, N, D, eps, s, nullptr,
+                            a.n2h));
   MM(N, 2 * D, D, kop(bf, a.n2, a.n2h, D), kop(bf, w.Wz, bf ? h16(w.Wz) : nullptr, D),
      epi_store(a.P, 2 * D), 0);
   // training keeps e = h~ - h_prev (all the backward needs), prefill keeps h
@@ -423,8 +427,9 @@ int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B,
        rnet_k::gru_scan_fwd(a.P, a.P + D, 2 * D, w.bz, w.bh, a.z, a.h, nullptr, a.r1, a.r2, B, T,
                             D, s, train, a.r3));
   // 3. slot memory (:315-330)
-  PROF(PK_RMS_FWD, 0, 2 * ND4,
-       rnet_k::rms_norm_fwd(a.r2, w.n3, a.n3, a.rinv3, N, D, eps, s, nullptr, a.n3h));
+  PROF(PK_RMS_FWD, 0, ND4 + (bf ? ND2 : ND4),
+       rnet_k::rms_norm_fwd(a.r2, w.n3, bf ? nullptr : a.n3, a.rinv3, N, D, eps, s, nullptr,
+                            a.n3h));
   {
     Epilogue e = epi_store(a.q, D);
     e.C16 = bf ? a.qh : nullptr;
@@ -441,19 +446,18 @@ int Engine::layer_forward(int l, const float* Xl, float* Xn, LayerAct& a, int B,
     MM(N, S, D, kmaj(a.q, D), kmaj(KT, D), epi_store(scores_, S), 0);
     PROF(PK_OTHER, 0, 4.0 * N * S, rnet_k::topk_rows(scores_, a.idx, a.w, N, S, k, s));
   }
-  PROF(PK_SLOT_GATHER, 2.0 * k * N * D, (1 + k) * ND4,
-       rnet_k::slot_gather(a.idx, a.w, VT, a.r, N, D, S, k, err, s));
-  if (bf) PROF(PK_OTHER, 0, 6.0 * N * D, rnet_k::to_bf16(a.r, a.rh, (size_t)N * D, s));
+  PROF(PK_SLOT_GATHER, 2.0 * k * N * D, k * ND4 + (bf ? ND2 : ND4),
+       rnet_k::slot_gather(a.idx, a.w, VT, bf ? nullptr : a.r, N, D, S, k, err, s, a.rh));
   MM_RES(N, D, D, kop(bf, a.r, a.rh, D), kop(bf, w.pout, bf ? h16(w.pout) : nullptr, D), a.r3);
   // 4. SwiGLU FFN (:332-342): paired gate|up tiles, SiLU*up in the epilogue
-  PROF(PK_RMS_FWD, 0, 3 * ND4,
-       rnet_k::rms_norm_fwd(a.r3, w.n4, a.n4, a.rinv4, N, D, eps, s, Xn, a.n4h));
+  PROF(PK_RMS_FWD, 0, 2 * ND4 + (bf ? ND2 : ND4),
+       rnet_k::rms_norm_fwd(a.r3, w.n4, bf ? nullptr : a.n4, a.rinv4, N, D, eps, s, Xn, a.n4h));
   {
     Epilogue e;
     e.kind = EPI_SWIGLU_FWD;
     e.G = a.G;
     e.U = a.U;
-    e.H = a.H;
+    e.H = bf ? nullptr : a.H;  // bf16 mode: H only as the bf16 copy
     e.H16 = bf ? a.Hh : nullptr;
     e.ldf = F;
     MM(N, F, D, kop(bf, a.n4, a.n4h, D), kop(bf, w.gate, bf ? h16(w.gate) : nullptr, D), e,
@@ -483,8 +487,9 @@ int Engine::forward(const int* d_tokens, float* d_logits, int B, int T) {
   }
   const float* XL = caches ? X_ + (size_t)cfg_.n_layers * ND : X_ + (size_t)(cfg_.n_layers & 1) * ND;
   const bool bf = precision == 1;
-  PROF(PK_RMS_FWD, 0, 8.0 * ND,
-       rnet_k::rms_norm_fwd(XL, fnorm_, nf_, rinvf_, N, D, cfg_.rms_eps, s, nullptr, nfh_));
+  PROF(PK_RMS_FWD, 0, (bf ? 6.0 : 8.0) * ND,
+       rnet_k::rms_norm_fwd(XL, fnorm_, bf ? nullptr : nf_, rinvf_, N, D, cfg_.rms_eps, s, nullptr,
+                            nfh_));
   MM(N, V, D, kop(bf, nf_, nfh_, D), kop(bf, outw_, bf ? h16(outw_) : nullptr, D),
      epi_store(d_logits, V), 0);
   have_cache_ = caches;
@@ -544,9 +549,9 @@ int Engine::layer_backward(int l, int B, int T) {
   CK(fork());
   MM_W(D, F, N, mop(bf, dX_, dXh_, D), mop(bf, a.H, a.Hh, F), epi_accum(g.down, F));
   MM(N, F, D, kop(bf, dX_, dXh_, D), mop(bf, w.down, W16(w.down), F), epi_store(dGU_, 2 * F), 0);
-  PROF(PK_OTHER, 0, 5.0 * 4 * N * F,
-       rnet_k::swiglu_bwd_pointwise(dGU_, 2 * F, a.G, a.U, N, F, s));
-  if (bf) PROF(PK_OTHER, 0, 12.0 * N * F, rnet_k::to_bf16(dGU_, dGUh_, 2 * (size_t)N * F, s));
+  // bf16 mode: dG | dU written only as the bf16 copy the GEMMs read
+  PROF(PK_OTHER, 0, (bf ? 16.0 : 20.0) * N * F,
+       rnet_k::swiglu_bwd_pointwise(dGU_, 2 * F, a.G, a.U, N, F, s, bf ? dGUh_ : nullptr));
   CK(fork());
   MM_W(2 * F, D, N, mop(bf, dGU_, dGUh_, 2 * F), mop(bf, a.n4, a.n4h, D), epi_accum(g.gate, D));
   MM(N, D, 2 * F, kop(bf, dGU_, dGUh_, 2 * F), mop(bf, w.gate, W16(w.gate), D),
@@ -559,10 +564,9 @@ int Engine::layer_backward(int l, int B, int T) {
   MM_W(D, D, N, mop(bf, dX_, dXh_, D), mop(bf, a.r, a.rh, D), epi_accum(g.pout, D));
   MM(N, D, D, kop(bf, dX_, dXh_, D), mop(bf, w.pout, W16(w.pout), D), epi_store(dr_, D), 0);
   CK(cudaMemsetAsync(dKT, 0, 2 * (size_t)S * D * sizeof(float), s));  // dKT and dVT
-  PROF(PK_SLOT_SPARSE_BWD, 8.0 * k * N * D, (3 + 4 * k) * ND4,
+  PROF(PK_SLOT_SPARSE_BWD, 8.0 * k * N * D, (2 + 4 * k) * ND4 + (bf ? 2.0 : 4.0) * N * D,
        rnet_k::slot_sparse_bwd(dr_, a.idx, a.w, VT_ + (size_t)l * S * D, KT_ + (size_t)l * S * D,
-                               a.q, dq_, dVT, dKT, N, D, S, k, err, s));
-  if (bf) PROF(PK_OTHER, 0, 6.0 * N * D, rnet_k::to_bf16(dq_, dqh_, (size_t)N * D, s));
+                               a.q, bf ? nullptr : dq_, dVT, dKT, N, D, S, k, err, s, dqh_));
   CK(fork());
   MM_W(D, D, N, mop(bf, dq_, dqh_, D), mop(bf, a.n3, a.n3h, D), epi_accum(g.pq, D));
   // dKT, dVT are adjacent [S, D] blocks of consecutive layers: both into
@@ -574,10 +578,9 @@ int Engine::layer_backward(int l, int B, int T) {
   PROF(PK_RMS_BWD, 0, 4 * ND4,
        rnet_k::rms_norm_bwd(dsub_, a.r2, w.n3, a.rinv3, dX_, g.n3, N, D, 1, s, dXh_));
   // 2. MinGRU (:512-528, src/min_gru.cu:128-191)
-  PROF(PK_SCAN_BWD, 0, 5 * ND4,
+  PROF(PK_SCAN_BWD, 0, 3 * ND4 + (bf ? 2.0 : 4.0) * 2 * N * D,
        rnet_k::gru_scan_bwd(dX_, a.z, a.h, nullptr, 0, nullptr, dPZH_, dPZH_ + D, 2 * D, g.bz,
-                            g.bh, B, T, D, s));
-  if (bf) PROF(PK_OTHER, 0, 12.0 * N * D, rnet_k::to_bf16(dPZH_, dPZHh_, 2 * (size_t)N * D, s));
+                            g.bh, B, T, D, s, bf ? dPZHh_ : nullptr));
   CK(fork());
   MM_W(2 * D, D, N, mop(bf, dPZH_, dPZHh_, 2 * D), mop(bf, a.n2, a.n2h, D), epi_accum(g.Wz, D));
   MM(N, D, 2 * D, kop(bf, dPZH_, dPZHh_, 2 * D), mop(bf, w.Wz, W16(w.Wz), D),

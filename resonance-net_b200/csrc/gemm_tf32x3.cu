@@ -157,7 +157,7 @@ __device__ __forceinline__ void tile_out(float* st, const float (&v)[32], float*
             const float4 r = *reinterpret_cast<const float4*>(R + (size_t)row * ldr + col);
             x.x += r.x; x.y += r.y; x.z += r.z; x.w += r.w;
           }
-          *reinterpret_cast<float4*>(g) = x;
+          if (dst) *reinterpret_cast<float4*>(g) = x;
           if (dst16) {
             const __nv_bfloat162 lo = __floats2bfloat162_rn(x.x, x.y);
             const __nv_bfloat162 hi = __floats2bfloat162_rn(x.z, x.w);
@@ -173,8 +173,9 @@ __device__ __forceinline__ void tile_out(float* st, const float (&v)[32], float*
           if (op == 1) {
             atomicAdd(g + q, xs[q]);
           } else {
-            g[q] = xs[q] + (op == 2 ? R[(size_t)row * ldr + col + q] : 0.f);
-            if (dst16) dst16[(size_t)row * ld + col + q] = __float2bfloat16_rn(g[q]);
+            const float o = xs[q] + (op == 2 ? R[(size_t)row * ldr + col + q] : 0.f);
+            if (dst) g[q] = o;
+            if (dst16) dst16[(size_t)row * ld + col + q] = __float2bfloat16_rn(o);
           }
         }
       }

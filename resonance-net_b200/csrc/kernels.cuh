@@ -36,6 +36,10 @@ cudaError_t from_bf16(const __nv_bfloat16* x, float* y, size_t n, cudaStream_t s
 cudaError_t conv_fwd(const float* x, const float* w3, const float* w7, const float* w15,
                      float* S, float* Sq, float* c7, float* c15, int B, int T, int D,
                      cudaStream_t s);
+// Model path with bf16 outputs: S16 (and Sq16 if given) only.
+cudaError_t conv_fwd_bf16(const float* x, const float* w3, const float* w7, const float* w15,
+                          __nv_bfloat16* S16, __nv_bfloat16* Sq16, int B, int T, int D,
+                          cudaStream_t s);
 // dx (+)= sum_K conv_K^T(dS); dw_K[k] += sum x[t-(K-1)+k] dS[t].
 // accumulate: 0 -> dx = ..., 1 -> dx += ...
 // `partials` is scratch of conv_bwd_partials_floats(B, T, D) floats.
@@ -60,9 +64,12 @@ cudaError_t gru_scan_fwd(const float* pz, const float* ph, int ldp, const float*
 // bh is not read.
 // Writes dz/dh~ with row stride ldd (dh~ at column offset `dht_off`),
 // dbz += sum dz, dbh += sum dh~.
+// dzh16 (optional): dz / dh~ as bf16 into dzh16 (same row stride ldd, dh~ at
+// the same column offset as dht - dz); dz, dht are then not written.
 cudaError_t gru_scan_bwd(const float* dy, const float* z, const float* h, const float* ph,
                          int ldp, const float* bh, float* dz, float* dht, int ldd, float* dbz,
-                         float* dbh, int B, int T, int D, cudaStream_t s);
+                         float* dbh, int B, int T, int D, cudaStream_t s,
+                         __nv_bfloat16* dzh16 = nullptr);
 
 // ---- slot memory (slot_memory.cu) -----------------------------------------
 // out[j*R + i] = in[i*C + j] (+ accumulate into out if acc)
@@ -73,15 +80,17 @@ cudaError_t transpose(const float* in, float* out, int R, int C, int acc, cudaSt
 cudaError_t transpose_pairs(const float* in, size_t in_stride1, size_t in_stride2, float* out0,
                             float* out1, size_t out_stride, int pairs, int R, int C, int acc,
                             cudaStream_t s);
-// r[n,:] = sum_j w[n,j] VT[idx[n,j], :]
+// r[n,:] = sum_j w[n,j] VT[idx[n,j], :]   (r16: bf16 copy; r may be null then)
 cudaError_t slot_gather(const int* idx, const float* w, const float* VT, float* r, int N,
-                        int D, int S, int k, unsigned* err, cudaStream_t s);
+                        int D, int S, int k, unsigned* err, cudaStream_t s,
+                        __nv_bfloat16* r16 = nullptr);
 // Sparse backward through top-k + softmax + gather (one warp per token):
 //   dwj = <dr, VT[idx_j]>, dsc_j = w_j (dwj - sum w dw), dq = sum dsc_j KT[idx_j]
-//   dVT[idx_j] += w_j dr, dKT[idx_j] += dsc_j q
+//   dVT[idx_j] += w_j dr, dKT[idx_j] += dsc_j q   (dq16: bf16 dq; dq may be null then)
 cudaError_t slot_sparse_bwd(const float* dr, const int* idx, const float* w, const float* VT,
                             const float* KT, const float* q, float* dq, float* dVT, float* dKT,
-                            int N, int D, int S, int k, unsigned* err, cudaStream_t s);
+                            int N, int D, int S, int k, unsigned* err, cudaStream_t s,
+                            __nv_bfloat16* dq16 = nullptr);
 // Top-k (k <= 8) over a materialised score matrix, reference order semantics,
 // + softmax (used by the per-op API for k != 2).
 cudaError_t topk_rows(const float* scores, int* idx, float* w, int N, int S, int k,
@@ -106,8 +115,10 @@ cudaError_t add3(const float* a, const float* b, const float* c, float* out, siz
 cudaError_t silu_mul(const float* g, const float* u, float* h, size_t n, cudaStream_t s);
 // In place over dgu = [dG | dU] ([N, 2F], row stride ld) holding dH in its
 // dG half: dG = dH * u * silu'(g), dU = dH * silu(g) (G, U: [N, F] caches).
+// dgu16 (optional): [dG | dU] written as bf16 there (row stride ld) instead
+// of in place.
 cudaError_t swiglu_bwd_pointwise(float* dgu, int ld, const float* G, const float* U, int N, int F,
-                                 cudaStream_t s);
+                                 cudaStream_t s, __nv_bfloat16* dgu16 = nullptr);
 
 // ---- recurrent decode (decode.cu) -----------------------------------------
 // h[r, f] = silu(gu[r, f]) * gu[r, F + f] over rows of width 2F.

@@ -153,7 +153,8 @@ __global__ void __launch_bounds__(W * 32)
                     const float* __restrict__ h, const float* __restrict__ ph, int ldp,
                     const float* __restrict__ bh, float* __restrict__ dz,
                     float* __restrict__ dht, int ldd, float* __restrict__ dbz,
-                    float* __restrict__ dbh, int T, int D) {
+                    float* __restrict__ dbh, int T, int D, __nv_bfloat16* __restrict__ dz16,
+                    __nv_bfloat16* __restrict__ dht16) {
   rnet_dev::pdl_trigger();
   extern __shared__ float smem[];
   float* sZ = smem;
@@ -214,8 +215,13 @@ __global__ void __launch_bounds__(W * 32)
         }
         const float vz = dh * e * zv * (1.f - zv);
         const float vh = dh * zv;
-        dz[od] = vz;
-        dht[od] = vh;
+        if (dz16) {
+          dz16[od] = __float2bfloat16_rn(vz);
+          dht16[od] = __float2bfloat16_rn(vh);
+        } else {
+          dz[od] = vz;
+          dht[od] = vh;
+        }
         accz += vz;
         acch += vh;
       }
@@ -287,13 +293,15 @@ cudaError_t gru_scan_fwd(const float* pz, const float* ph, int ldp, const float*
 
 cudaError_t gru_scan_bwd(const float* dy, const float* z, const float* h, const float* ph,
                          int ldp, const float* bh, float* dz, float* dht, int ldd, float* dbz,
-                         float* dbh, int B, int T, int D, cudaStream_t s) {
+                         float* dbh, int B, int T, int D, cudaStream_t s, __nv_bfloat16* dzh16) {
   if (B <= 0 || T <= 0) return cudaSuccess;
   if (D % 4 || ldp % 4) return cudaErrorInvalidValue;
   const size_t smem = (size_t)3 * TILE * sizeof(float);
   allow_smem(scan_bwd_kernel, smem);
   const int grid = B * ((D + CW - 1) / CW);
-  scan_bwd_kernel<<<grid, W * 32, smem, s>>>(dy, z, h, ph, ldp, bh, dz, dht, ldd, dbz, dbh, T, D);
+  __nv_bfloat16* dht16 = dzh16 ? dzh16 + (dht - dz) : nullptr;
+  scan_bwd_kernel<<<grid, W * 32, smem, s>>>(dy, z, h, ph, ldp, bh, dz, dht, ldd, dbz, dbh, T, D,
+                                             dzh16, dht16);
   return launched();
 }
 

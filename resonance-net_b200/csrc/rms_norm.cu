@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     ss = warp_sum(ss);
     const float ri = rsqrtf(ss / (float)D + eps);
     if (lane == 0 && rinv) rinv[row] = ri;
-    if (y) {
+    if (y || y16) {
       float4* yr = reinterpret_cast<float4*>(y + (size_t)row * D);
 #pragma unroll
       for (int j = 0; j < VPL; ++j) {
@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(WARPS * 32)
           const float4 g = w4[c];
           const float4 o = make_float4(v[j].x * ri * g.x, v[j].y * ri * g.y, v[j].z * ri * g.z,
                                        v[j].w * ri * g.w);
-          yr[c] = o;
+          if (y) yr[c] = o;
           if (y16) st_bf16x4(y16 + (size_t)row * D + 4 * c, o);
         }
       }

@@ -41,9 +41,18 @@ __global__ void transpose_kernel(const float* __restrict__ in, float* __restrict
 }
 
 // One warp per token; lane covers 4 consecutive features per 128-wide step.
+__device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float4 v) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t*>(&a);
+  u.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+// r16 / dq16 (optional): bf16 outputs; the fp32 one is skipped when null.
 __global__ void gather_kernel(const int* __restrict__ idx, const float* __restrict__ w,
                               const float* __restrict__ VT, float* __restrict__ r, int N, int D,
-                              int S, int k, unsigned* err) {
+                              int S, int k, unsigned* err, __nv_bfloat16* __restrict__ r16) {
   rnet_dev::pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= N) return;
@@ -64,7 +73,8 @@ __global__ void gather_kernel(const int* __restrict__ idx, const float* __restri
       const float4 v = *reinterpret_cast<const float4*>(VT + (size_t)id[j] * D + c);
       acc.x += ww[j] * v.x; acc.y += ww[j] * v.y; acc.z += ww[j] * v.z; acc.w += ww[j] * v.w;
     }
-    *reinterpret_cast<float4*>(r + (size_t)warp * D + c) = acc;
+    if (r) *reinterpret_cast<float4*>(r + (size_t)warp * D + c) = acc;
+    if (r16) st_bf16x4(r16 + (size_t)warp * D + c, acc);
   }
 }
 
@@ -73,7 +83,7 @@ __global__ void sparse_bwd_kernel(const float* __restrict__ dr, const int* __res
                                   const float* __restrict__ KT, const float* __restrict__ q,
                                   float* __restrict__ dq, float* __restrict__ dVT,
                                   float* __restrict__ dKT, int N, int D, int S, int k,
-                                  unsigned* err) {
+                                  unsigned* err, __nv_bfloat16* __restrict__ dq16) {
   rnet_dev::pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= N) return;
@@ -117,7 +127,8 @@ __global__ void sparse_bwd_kernel(const float* __restrict__ dr, const int* __res
       red_add_v4(dKT + (size_t)id[j] * D + c, dsc[j] * qq.x, dsc[j] * qq.y, dsc[j] * qq.z,
                  dsc[j] * qq.w);
     }
-    *reinterpret_cast<float4*>(dq + (size_t)warp * D + c) = acc;
+    if (dq) *reinterpret_cast<float4*>(dq + (size_t)warp * D + c) = acc;
+    if (dq16) st_bf16x4(dq16 + (size_t)warp * D + c, acc);
   }
 }
 
@@ -171,20 +182,21 @@ cudaError_t transpose_pairs(const float* in, size_t in_stride1, size_t in_stride
 }
 
 cudaError_t slot_gather(const int* idx, const float* w, const float* VT, float* r, int N, int D,
-                        int S, int k, unsigned* err, cudaStream_t s) {
+                        int S, int k, unsigned* err, cudaStream_t s, __nv_bfloat16* r16) {
   if (N <= 0) return cudaSuccess;
   if (k < 1 || k > 8 || D % 4) return cudaErrorInvalidValue;
-  gather_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(idx, w, VT, r, N, D, S, k, err);
+  gather_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(idx, w, VT, r, N, D, S, k, err, r16);
   return launched();
 }
 
 cudaError_t slot_sparse_bwd(const float* dr, const int* idx, const float* w, const float* VT,
                             const float* KT, const float* q, float* dq, float* dVT, float* dKT,
-                            int N, int D, int S, int k, unsigned* err, cudaStream_t s) {
+                            int N, int D, int S, int k, unsigned* err, cudaStream_t s,
+                            __nv_bfloat16* dq16) {
   if (N <= 0) return cudaSuccess;
   if (k < 1 || k > 8 || D % 4) return cudaErrorInvalidValue;
   sparse_bwd_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dr, idx, w, VT, KT, q, dq, dVT, dKT, N,
-                                                         D, S, k, err);
+                                                         D, S, k, err, dq16);
   return launched();
 }
 
