@@ -164,6 +164,23 @@ int rnet_cross_entropy_forward_noalloc(const float* logits, const int* targets, 
 int rnet_residual_add(float* x, const float* y, size_t n, void* stream);
 int rnet_scale_grads(float* grads, float scale, size_t n, void* stream);
 
+/* ------------------------------------------------------------------ data
+ * Training batches of the reference's DataLoader (src/data_loader.cpp:31-52
+ * as driven by src/main.cpp:117-133) with the corpus resident on the GPU.
+ * rnet_data_create uploads n corpus bytes once (n = 0: the reference's
+ * synthetic tokens); seed seeds the std::mt19937 the reference's training
+ * loop passes to get_batch (42 + rank * 10007 there). rnet_data_batch makes
+ * the reference's draws on the host (window starts, 8 bytes per sequence)
+ * and gathers the windows into device int32 inputs / targets [batch *
+ * seq_len] on `stream`, asynchronously; the batches equal the reference
+ * loader's byte for byte. Not thread-safe per handle. */
+typedef struct rnet_data rnet_data;
+int rnet_data_create(const unsigned char* host_bytes, size_t n, int device, unsigned seed,
+                     rnet_data** out);
+int rnet_data_destroy(rnet_data* d);
+int rnet_data_batch(rnet_data* d, int batch, int seq_len, int* d_inputs, int* d_targets,
+                    void* stream);
+
 /* ------------------------------------------------------------------ model
  * The reference's ResonanceNet class (include/resonance_net.h:56-130).
  * Parameters and gradients are single flat fp32 device buffers in checkpoint
@@ -234,6 +251,16 @@ int rnet_model_topk(rnet_model* m, int layer, const int** d_idx, const float** d
 /* Host copies of the same ([batch*seq_len*top_k] each; waits for the stream). */
 int rnet_model_topk_host(rnet_model* m, int layer, int* h_idx, float* h_w, size_t n);
 int rnet_model_save(rnet_model* m, const char* path);
+/* Checkpoint without stalling training (no counterpart in the reference,
+ * whose save() blocks on a device-to-host copy): the parameters are
+ * snapshotted on the model stream (a device copy ordered after all queued
+ * work, so a later SGD step cannot change what is saved), then copied to
+ * pinned host memory on a side stream and written by a host thread in the
+ * reference byte layout. rnet_model_save_wait joins the write and returns
+ * its status; a second save_async first waits for the previous one. Costs
+ * one parameter-sized device buffer and one pinned host buffer. */
+int rnet_model_save_async(rnet_model* m, const char* path);
+int rnet_model_save_wait(rnet_model* m);
 int rnet_model_load_weights(rnet_model* m, const char* path);
 /* Wait for the model stream and report any device error word bits. */
 int rnet_model_synchronize(rnet_model* m);

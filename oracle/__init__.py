@@ -171,6 +171,7 @@ def ref_lib() -> ctypes.CDLL:
         _ref.ref_model_save.argtypes = [_P, ctypes.c_char_p]
         _ref.ref_model_load_into.argtypes = [_P, ctypes.c_char_p]
         _ref.ref_get_scores.argtypes = [_P, _I, _P, _I]
+        _ref.ref_loader_batches.argtypes = [ctypes.c_char_p, ctypes.c_uint, _I, _I, _I, _P, _P]
     return _ref
 
 
@@ -240,6 +241,15 @@ class RefModel:
         if self.h:
             self.lib.ref_model_destroy(self.h)
             self.h = None
+
+
+def ref_loader_batches(path: str, seed: int, B: int, T: int, steps: int):
+    """Batches of the reference's own DataLoader ([steps, B*T] inputs, targets)."""
+    inp = np.zeros((steps, B * T), np.int32)
+    tgt = np.zeros((steps, B * T), np.int32)
+    assert ref_lib().ref_loader_batches((path or "").encode(), seed, B, T, steps, ptr(inp),
+                                        ptr(tgt)) == 1
+    return inp, tgt
 
 
 def margins_from_scores(scores: np.ndarray, k: int = 2) -> np.ndarray:

@@ -19,6 +19,7 @@
 #undef private
 #include "dist.h"
 #include "layers.h"
+#include "data_loader.cpp"  // the reference's DataLoader (src/data_loader.cpp), unmodified
 
 using namespace rnet;
 
@@ -214,6 +215,23 @@ void ref_get_scores(void* hp, int layer, float* host, int BS) {
   Handle* h = (Handle*)hp;
   cudaMemcpy(host, h->model.cache_[layer].scores_cache,
              sizeof(float) * (size_t)BS * h->model.cfg_.n_slots, cudaMemcpyDeviceToHost);
+}
+
+}  // extern "C"
+
+extern "C" {
+
+// `steps` batches from the reference's DataLoader (src/data_loader.cpp:31-52)
+// seeded like src/main.cpp:117; path = corpus file, or "" for its synthetic
+// tokens. inputs / targets: [steps][B*T]. Returns 1 on success.
+int ref_loader_batches(const char* path, unsigned seed, int B, int T, int steps, int* inputs,
+                       int* targets) {
+  DataLoader dl;
+  if (path && path[0] && !dl.load(path)) return 0;
+  std::mt19937 rng(seed);
+  for (int s = 0; s < steps; ++s)
+    dl.get_batch(inputs + (size_t)s * B * T, targets + (size_t)s * B * T, B, T, rng);
+  return 1;
 }
 
 }  // extern "C"

@@ -92,6 +92,8 @@ _SIGS = {
     "rnet_model_topk_host": [_P, _I, _P, _P, _SZ],
     "rnet_model_save": [_P, ctypes.c_char_p],
     "rnet_model_load_weights": [_P, ctypes.c_char_p],
+    "rnet_model_save_async": [_P, ctypes.c_char_p],
+    "rnet_model_save_wait": [_P],
     "rnet_model_synchronize": [_P],
     "rnet_model_profile_enable": [_P, _I],
     "rnet_model_profile_read": [_P, _P, _P, _P, _P, _I, _I],
@@ -114,6 +116,9 @@ _SIGS = {
     "rnet_dist_uid_file_write": [ctypes.c_char_p, ctypes.c_char_p],
     "rnet_dist_uid_file_read": [ctypes.c_char_p, _I, ctypes.c_char_p],
     "rnet_model_set_dist": [_P, _P],
+    "rnet_data_create": [_P, _SZ, _I, ctypes.c_uint, ctypes.POINTER(_P)],
+    "rnet_data_destroy": [_P],
+    "rnet_data_batch": [_P, _I, _I, _P, _P, _P],
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -285,6 +290,12 @@ class Model:
     def save(self, path: str) -> None:
         check(lib().rnet_model_save(self._h, path.encode()))
 
+    def save_async(self, path: str) -> None:
+        check(lib().rnet_model_save_async(self._h, path.encode()))
+
+    def save_wait(self) -> None:
+        check(lib().rnet_model_save_wait(self._h))
+
     def load_weights(self, path: str) -> None:
         check(lib().rnet_model_load_weights(self._h, path.encode()))
 
@@ -387,8 +398,35 @@ class Dist:
             self.handle = _P()
 
 
+class DataLoader:
+    """The reference's batch sampler with the corpus resident on the GPU
+    (rnet_data_*): same batches as src/data_loader.cpp for the same seed."""
+
+    def __init__(self, corpus: Optional[bytes], device: int = 0, seed: int = 42):
+        self.handle = _P()
+        buf = corpus or b""
+        check(lib().rnet_data_create(buf if buf else None, len(buf), device, seed,
+                                     ctypes.byref(self.handle)))
+
+    def batch(self, batch: int, seq_len: int, d_inputs, d_targets, stream=None) -> None:
+        check(lib().rnet_data_batch(self.handle, batch, seq_len, _ptr(d_inputs), _ptr(d_targets),
+                                    _ptr(stream)))
+
+    def close(self) -> None:
+        if self.handle:
+            lib().rnet_data_destroy(self.handle)
+            self.handle = _P()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 PROFILE_KINDS = ("gemm", "scan_fwd", "scan_bwd", "conv_fwd", "conv_bwd", "rms_fwd", "rms_bwd",
-                 "slot_gather", "slot_sparse_bwd", "embed", "cross_entropy", "sgd", "other")
+                 "slot_gather", "slot_sparse_bwd", "embed", "cross_entropy", "sgd", "other",
+                 "comm_wait")
 
 
 def kernel_launches() -> int:

@@ -239,6 +239,15 @@ int rnet_model_save(rnet_model* m, const char* path) {
   if (!path) return rnet_status::fail(RNET_ERR_ARG, "null path");
   return m->e->save(path);
 }
+int rnet_model_save_async(rnet_model* m, const char* path) {
+  CHECK_M(m);
+  if (!path) return rnet_status::fail(RNET_ERR_ARG, "null path");
+  return m->e->save_async(path);
+}
+int rnet_model_save_wait(rnet_model* m) {
+  CHECK_M(m);
+  return m->e->save_wait();
+}
 int rnet_model_load_weights(rnet_model* m, const char* path) {
   CHECK_M(m);
   if (!path) return rnet_status::fail(RNET_ERR_ARG, "null path");

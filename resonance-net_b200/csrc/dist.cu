@@ -10,6 +10,7 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -135,6 +136,16 @@ int dist_create(int rank, int world, int local_rank, const unsigned char uid[128
   std::memcpy(&id, uid, 128);
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
+  // Cap on the SMs NCCL's kernels occupy while backward runs beside them
+  // (the GEMM and conv-backward grids are persistent, one CTA per SM):
+  // RNET_NCCL_MAX_CTAS, default NCCL's own choice.
+  if (const char* e = getenv("RNET_NCCL_MAX_CTAS")) {
+    const int v = atoi(e);
+    if (v > 0) {
+      cfg.maxCTAs = v;
+      if (cfg.minCTAs > v || cfg.minCTAs == NCCL_CONFIG_UNDEF_INT) cfg.minCTAs = 1;
+    }
+  }
   ncclResult_t r = a.CommInitRankConfig(&d->comm, world, id, rank, &cfg);
   if (r != ncclSuccess && r != ncclInProgress) {
     delete d;

@@ -4,11 +4,13 @@
 // :218-343 (forward with caches), :346-408 (inference forward), :411-548
 // (backward), :551-697 (step, zero_grad), :743-824 (checkpoint).
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <algorithm>
 #include <cstring>
 #include <random>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "dist.h"
@@ -66,6 +68,12 @@ Engine::Engine(const rnet_model_config& c) : cfg_(c) {}
 
 Engine::~Engine() {
   if (device_ >= 0) cudaSetDevice(device_);
+  save_wait();
+  cudaFree(snap_);
+  if (snap_host_) cudaFreeHost(snap_host_);
+  if (snap_ready_) cudaEventDestroy(snap_ready_);
+  if (host_ready_) cudaEventDestroy(host_ready_);
+  if (save_stream_) cudaStreamDestroy(save_stream_);
   if (stream_) cudaStreamSynchronize(stream_);
   cudaFree(params_);
   cudaFree(grads_);
@@ -610,11 +618,23 @@ int Engine::backward(const float* d_dlogits, const int* d_tokens, int B, int T) 
   int rc = head_backward(d_dlogits, N);
   if (rc) return rc;
   const size_t ND = (size_t)N * cfg_.d_model;
+  // Gradient buckets: contiguous ranges of the flat gradient buffer, a layer
+  // at a time from the last layer down, merged until a bucket holds at least
+  // bucket_bytes_ (25 MB by default, RNET_DP_BUCKET_MB overrides), then
+  // all-reduced on the comm stream while the backward goes on.
+  if (bucket_bytes_ == 0) {
+    const char* e = getenv("RNET_DP_BUCKET_MB");
+    const double mb = e ? atof(e) : 25.0;
+    bucket_bytes_ = (size_t)((mb > 0 ? mb : 25.0) * 1e6);
+  }
   // bf16 mode: gradient buckets travel as bf16 (one staging buffer of the
   // largest bucket; the comm stream orders its reuse)
   __nv_bfloat16* c16 = nullptr;
   if (dist && precision == 1) {
-    const size_t need = std::max(G_[0].count, 2 * (size_t)cfg_.vocab_size * cfg_.d_model +
+    // a bucket stops growing once it reaches bucket_bytes_: at most that plus
+    // one layer (or the head)
+    const size_t need = bucket_bytes_ / sizeof(float) +
+                        std::max(G_[0].count, 2 * (size_t)cfg_.vocab_size * cfg_.d_model +
                                                   (size_t)cfg_.d_model);
     if (comm16_count_ < need) {
       CK(cudaStreamSynchronize(stream_));
@@ -625,6 +645,14 @@ int Engine::backward(const float* d_dlogits, const int* d_tokens, int B, int T) 
     }
     c16 = comm16_;
   }
+  size_t pend_lo = 0, pend_hi = 0;  // pending bucket [lo, hi) in floats
+  auto flush = [&](bool force) -> int {
+    if (!dist || pend_hi == pend_lo) return RNET_OK;
+    if (!force && (pend_hi - pend_lo) * sizeof(float) < bucket_bytes_) return RNET_OK;
+    const int r = dist_reduce_range(dist, grads_ + pend_lo, pend_hi - pend_lo, stream_, c16);
+    pend_lo = pend_hi = 0;
+    return r;
+  };
   for (int l = cfg_.n_layers - 1; l >= 0; --l) {
     // recompute mode: the caches in act_[0] are the last layer's after the
     // forward; every other layer's are rebuilt from its kept input (the
@@ -637,15 +665,20 @@ int Engine::backward(const float* d_dlogits, const int* d_tokens, int B, int T) 
     rc = layer_backward(l, B, T);
     if (rc) return rc;
     if (dist) {
-      rc = dist_reduce_range(dist, grads_ + G_[l].offset, G_[l].count, stream_, c16);
+      // layer l sits directly below the pending range (layer l + 1, ...)
+      pend_hi = pend_hi == pend_lo ? G_[l].offset + G_[l].count : pend_hi;
+      pend_lo = G_[l].offset;
+      rc = flush(false);
       if (rc) return rc;
     }
   }
   PROF(PK_EMBED, 0, 4.0 * N * cfg_.d_model,
        rnet_k::embed_bwd(dX_, d_tokens, g_embed_, N, cfg_.vocab_size, cfg_.d_model, stream_));
   if (dist) {
-    rc = dist_reduce_range(dist, grads_, 2 * (size_t)cfg_.vocab_size * cfg_.d_model + cfg_.d_model,
-                           stream_, c16);
+    // the head (embedding, output, final norm) sits below layer 0
+    if (pend_hi == pend_lo) pend_hi = G_[0].offset;
+    pend_lo = 0;
+    rc = flush(true);
     if (rc) return rc;
   }
   return RNET_OK;
@@ -658,8 +691,11 @@ int Engine::zero_grad() {
 int Engine::step(float lr, float clip) {
   int world = 1;
   if (dist) {
+    cudaEvent_t pa = nullptr;
+    if (prof_on_) prof_begin(&pa);
     int rc = dist_wait(dist, stream_);
     if (rc) return rc;
+    if (prof_on_) prof_end(pa, PK_COMM_WAIT, 0, 0);
     world = dist_world(dist);
   }
   const bool bf = precision == 1;
@@ -873,6 +909,61 @@ int Engine::save(const char* path) {
   ok = ok && fwrite(h.data(), sizeof(float), P_, f) == P_;
   ok = (fclose(f) == 0) && ok;
   if (!ok) return rnet_status::fail(RNET_ERR_IO, std::string("short write: ") + path);
+  return RNET_OK;
+}
+
+int Engine::save_async(const char* path) {
+  int rc = save_wait();
+  if (rc) return rc;
+  if (!snap_) {
+    CK(cudaMalloc(&snap_, P_ * sizeof(float)));
+    CK(cudaMallocHost(&snap_host_, P_ * sizeof(float)));
+    CK(cudaStreamCreateWithFlags(&save_stream_, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&snap_ready_, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&host_ready_, cudaEventDisableTiming));
+  }
+  // the snapshot is ordered on the model stream: the next SGD update cannot
+  // overtake it
+  CK(cudaMemcpyAsync(snap_, params_, P_ * sizeof(float), cudaMemcpyDeviceToDevice, stream_));
+  CK(cudaEventRecord(snap_ready_, stream_));
+  CK(cudaStreamWaitEvent(save_stream_, snap_ready_, 0));
+  CK(cudaMemcpyAsync(snap_host_, snap_, P_ * sizeof(float), cudaMemcpyDeviceToHost,
+                     save_stream_));
+  CK(cudaEventRecord(host_ready_, save_stream_));
+  const std::string file(path);
+  const rnet_model_config cfg = cfg_;
+  save_status_ = RNET_OK;
+  save_msg_.clear();
+  save_thread_ = new std::thread([this, file, cfg]() {
+    if (cudaEventSynchronize(host_ready_) != cudaSuccess) {
+      save_status_ = RNET_ERR_CUDA;
+      save_msg_ = "save_async: snapshot copy failed";
+      return;
+    }
+    FILE* f = fopen(file.c_str(), "wb");
+    if (!f) {
+      save_status_ = RNET_ERR_IO;
+      save_msg_ = "cannot open for write: " + file;
+      return;
+    }
+    bool ok = fwrite(&cfg, sizeof(cfg), 1, f) == 1;
+    ok = ok && fwrite(snap_host_, sizeof(float), P_, f) == P_;
+    ok = (fclose(f) == 0) && ok;
+    if (!ok) {
+      save_status_ = RNET_ERR_IO;
+      save_msg_ = "short write: " + file;
+    }
+  });
+  return RNET_OK;
+}
+
+int Engine::save_wait() {
+  if (!save_thread_) return RNET_OK;
+  std::thread* t = static_cast<std::thread*>(save_thread_);
+  t->join();
+  delete t;
+  save_thread_ = nullptr;
+  if (save_status_) return rnet_status::fail(save_status_, save_msg_);
   return RNET_OK;
 }
 

@@ -57,6 +57,7 @@ enum ProfKind {
   PK_CE,
   PK_SGD,
   PK_OTHER,
+  PK_COMM_WAIT,  // data parallel: compute stream stalled on the last all-reduce
   PK_COUNT
 };
 
@@ -127,6 +128,12 @@ class Engine {
                  float* d_loss_sum);
 
   int save(const char* path);
+  // Checkpoint without stalling training: the parameters are snapshotted on
+  // the model stream (device copy, ordered after everything queued so far),
+  // then copied to pinned host memory on a side stream and written by a host
+  // thread. save_wait() joins it and returns its status. One save in flight.
+  int save_async(const char* path);
+  int save_wait();
   int load_weights(const char* path);  // config in file must match
 
   int topk(int layer, int** idx, float** w);
@@ -212,6 +219,15 @@ class Engine {
                 *dqh_ = nullptr, *dPZHh_ = nullptr;
   bool cap_bf16_ = false;
   bool recompute_ = false;
+  // asynchronous save
+  float* snap_ = nullptr;   // device snapshot of params_
+  float* snap_host_ = nullptr;  // pinned
+  cudaStream_t save_stream_ = nullptr;
+  cudaEvent_t snap_ready_ = nullptr, host_ready_ = nullptr;
+  void* save_thread_ = nullptr;  // std::thread*
+  int save_status_ = 0;
+  std::string save_msg_;
+  size_t bucket_bytes_ = 0;  // data-parallel bucket size (0: read RNET_DP_BUCKET_MB, default 25)
   __nv_bfloat16* comm16_ = nullptr;  // bf16 all-reduce staging (bf16 mode, DP)
   size_t comm16_count_ = 0;
   bool cap_recompute_ = false;

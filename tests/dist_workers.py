@@ -95,6 +95,8 @@ def dp_engine(rank, world, port, out_dir, case):
     the batch with the NCCL gradient all-reduce (rnet.Dist); rank 0 writes the
     updated parameters."""
     import torch
+    if case.get("bucket_mb"):
+        os.environ["RNET_DP_BUCKET_MB"] = str(case["bucket_mb"])
     dist = _init(rank, world, port)
     rnet = importlib.import_module("resonance-net_b200")
     rdata = importlib.import_module("resonance-net_b200.data")

@@ -120,3 +120,29 @@ def test_reference_main_program_drop_in(ref_ok, orc, rdata, tmp_path):
     for (s, la), (_, lb) in zip(a, b):
         assert abs(la - lb) <= 2e-4, f"step {s}: reference {la} vs library {lb}"
     assert a[-1][1] < a[0][1], "the loss did not fall: the run is not training"
+
+
+def test_async_save_snapshots_params_at_call(rnet, rdata, cuda, tmp_path):
+    """rnet_model_save_async writes the parameters as they were when it was
+    called, although training steps run while the file is written; the file
+    is the synchronous save() of those parameters byte for byte."""
+    torch = cuda
+    cfg = rnet.ModelConfig.make(d_model=64, n_layers=2, d_ff=128, n_slots=64, seq_len=32)
+    m = rnet.Model(cfg, device=0, reference_init=False)
+    m.set_params(rdata.init_params_normal(cfg, seed=2))
+    tok, tgt = rdata.uniform_tokens(2, 32, seed=4)
+    d_in = torch.from_numpy(tok.reshape(-1)).cuda()
+    d_tg = torch.from_numpy(tgt.reshape(-1)).cuda()
+    m.train_step(d_in, d_tg, 2, 32)
+    sync_path = str(tmp_path / "sync.bin")
+    m.save(sync_path)
+    at_call = m.get_params()
+    async_path = str(tmp_path / "async.bin")
+    m.save_async(async_path)
+    for _ in range(5):  # training goes on while the file is written
+        m.train_step(d_in, d_tg, 2, 32)
+    m.save_wait()
+    assert not np.array_equal(m.get_params(), at_call)
+    with open(sync_path, "rb") as a, open(async_path, "rb") as b:
+        assert a.read() == b.read()
+    m.close()

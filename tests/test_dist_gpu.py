@@ -21,16 +21,19 @@ def _port():
     return p
 
 
-@pytest.mark.parametrize("bf16", [False, True])
-def test_dp_two_gpus_matches_one(rnet, rdata, cuda, tmp_path, bf16):
+@pytest.mark.parametrize("bf16,bucket_mb", [(False, 0), (True, 0), (False, 0.01)],
+                         ids=["fp32-25MB", "bf16-25MB", "fp32-per-layer"])
+def test_dp_two_gpus_matches_one(rnet, rdata, cuda, tmp_path, bf16, bucket_mb):
     """bf16: bf16 GEMM operands on both sides and bf16 on the wire for the
-    two-GPU gradient all-reduce; compared at the bf16 tolerance (2e-2)."""
+    two-GPU gradient all-reduce; compared at the bf16 tolerance (2e-2).
+    Buckets: the default 25 MB (the whole small model in one bucket) and
+    10 KB (every layer its own bucket, the head in the last one)."""
     torch = cuda
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     case = dict(d_model=64, n_layers=2, d_ff=128, n_slots=64, top_k=2, vocab=256, B=4, T=64,
-                pseed=1234, tseed=3, lr=3e-4, clip=1.0, bf16=bf16)
+                pseed=1234, tseed=3, lr=3e-4, clip=1.0, bf16=bf16, bucket_mb=bucket_mb)
     mp.spawn(dist_workers.dp_engine, args=(2, _port(), str(tmp_path), case), nprocs=2, join=True)
     dp = np.load(tmp_path / "dp_engine_params.npy").astype(np.float64)
     cfg = rnet.ModelConfig.make(d_model=case["d_model"], n_layers=case["n_layers"],
