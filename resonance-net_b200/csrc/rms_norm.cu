@@ -143,6 +143,91 @@ __global__ void __launch_bounds__(WARPS * 32)
   }
 }
 
+// Backward for wide rows (D > 512, e.g. 2048): a row per CTA of RB_THREADS
+// threads (VPT float4 per thread) instead of a row per warp, which would
+// need 16 float4 per lane per array and spill. The row's dot product is a
+// block reduction through a double-buffered shared array (one barrier per
+// row); each thread keeps the dw partial of its fixed columns in registers
+// over all rows of the CTA and flushes it once with atomics.
+constexpr int RB_THREADS = 128;
+
+template <int VPT>
+__global__ void __launch_bounds__(RB_THREADS)
+    rms_bwd_rowblock_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                            const float* __restrict__ w, const float* __restrict__ rinv,
+                            float* __restrict__ dx, float* __restrict__ dw, int rows, int D,
+                            int mode, __nv_bfloat16* __restrict__ dx16) {
+  rnet_dev::pdl_trigger();
+  __shared__ float red[2][RB_THREADS / 32];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int nv = D >> 2;
+  const float invD = 1.0f / (float)D;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4 wv[VPT], acc[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int c = t + RB_THREADS * j;
+    wv[j] = c < nv ? w4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  int par = 0;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x, par ^= 1) {
+    const float4* dyr = reinterpret_cast<const float4*>(dy + (size_t)row * D);
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * D);
+    float4* dxr = reinterpret_cast<float4*>(dx + (size_t)row * D);
+    const float ri = rinv[row];
+    float4 g[VPT], xh[VPT], prev[VPT];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = t + RB_THREADS * j;
+      if (c < nv) {
+        const float4 a = dyr[c], b = xr[c], ww = wv[j];
+        prev[j] = mode == 1 ? dxr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        g[j] = a;
+        xh[j] = make_float4(b.x * ri, b.y * ri, b.z * ri, b.w * ri);
+        dot += a.x * ww.x * xh[j].x + a.y * ww.y * xh[j].y + a.z * ww.z * xh[j].z +
+               a.w * ww.w * xh[j].w;
+      }
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) red[par][warp] = dot;
+    __syncthreads();
+    dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < RB_THREADS / 32; ++k) dot += red[par][k];
+    dot *= invD;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = t + RB_THREADS * j;
+      if (c < nv) {
+        const float4 ww = wv[j];
+        float4 o = make_float4(ri * (g[j].x * ww.x - xh[j].x * dot),
+                               ri * (g[j].y * ww.y - xh[j].y * dot),
+                               ri * (g[j].z * ww.z - xh[j].z * dot),
+                               ri * (g[j].w * ww.w - xh[j].w * dot));
+        o.x += prev[j].x; o.y += prev[j].y; o.z += prev[j].z; o.w += prev[j].w;
+        dxr[c] = o;
+        if (dx16) st_bf16x4(dx16 + (size_t)row * D + 4 * c, o);
+        acc[j].x += g[j].x * xh[j].x;
+        acc[j].y += g[j].y * xh[j].y;
+        acc[j].z += g[j].z * xh[j].z;
+        acc[j].w += g[j].w * xh[j].w;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int c = t + RB_THREADS * j;
+    if (c < nv) {
+      atomicAdd(&dw[4 * c], acc[j].x);
+      atomicAdd(&dw[4 * c + 1], acc[j].y);
+      atomicAdd(&dw[4 * c + 2], acc[j].z);
+      atomicAdd(&dw[4 * c + 3], acc[j].w);
+    }
+  }
+}
+
 // Backward for D <= STAGED_MAX_D: persistent CTAs walk groups of WARPS rows
 // (one row per warp); the dy / x (/ dx when accumulating) rows of the next
 // group are copied global -> shared while the current group is computed, so
@@ -330,6 +415,15 @@ cudaError_t bwd_t(const float* dy, const float* x, const float* w, const float* 
                                                               mode,
                                                               rnet_status::device_error_word(),
                                                               dx16);
+    return launched();
+  }
+  if constexpr (VPL >= 8) {
+    // wide rows: a row per 128-thread CTA (VPL / 4 float4 per thread)
+    constexpr int VPT = VPL / 4;
+    int grid = sm_count() * 4;
+    if (grid > rows) grid = rows;
+    rms_bwd_rowblock_kernel<VPT><<<grid, RB_THREADS, 0, s>>>(dy, x, w, rinv, dx, dw, rows, D,
+                                                             mode, dx16);
     return launched();
   }
   // >= 4 rows per warp so the dw partial flush is amortised

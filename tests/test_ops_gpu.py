@@ -43,7 +43,8 @@ def cta_group(request, rnet):
 
 
 # (1003, 256) and (13, 512): staged backward with a last 8-row group of 3 and 5 rows
-@pytest.mark.parametrize("N,D", [(64, 64), (1000, 512), (7, 2048), (1003, 256), (13, 512)])
+@pytest.mark.parametrize("N,D", [(64, 64), (1000, 512), (7, 2048), (1003, 256), (13, 512),
+                                 (3000, 2048), (999, 1024)])
 def test_rms_norm(rnet, orc, cuda, N, D):
     torch = cuda
     r = _rng(N + D)
