@@ -229,6 +229,15 @@ int rnet_model_set_precision(rnet_model* m, int precision);
  * the cost of one more forward per step); results are unchanged. With it on,
  * rnet_model_topk is unavailable. Default 0. */
 int rnet_model_set_recompute(rnet_model* m, int on);
+/* Optimizer extensions (no counterpart in the reference, whose step is plain
+ * SGD with global-norm clipping; all three default to off, which keeps that
+ * step): momentum (v = momentum * v + g, p -= lr * v), weight decay (wd * p
+ * added to the clipped gradient) and a linear learning-rate warmup
+ * (lr * min(1, (t + 1) / warmup_steps) at the t-th step after this call; the
+ * reference parses TrainConfig::warmup_steps but never applies it). Resets
+ * the step count and the velocity. */
+int rnet_model_set_optimizer(rnet_model* m, float momentum, float weight_decay,
+                             int warmup_steps);
 int rnet_model_forward(rnet_model* m, const int* d_tokens, float* d_logits, int batch,
                        int seq_len);
 int rnet_model_backward(rnet_model* m, const float* d_dlogits, const int* d_tokens, int batch,

@@ -82,6 +82,7 @@ _SIGS = {
     "rnet_model_set_conv_quirk": [_P, _I],
     "rnet_model_set_precision": [_P, _I],
     "rnet_model_set_recompute": [_P, _I],
+    "rnet_model_set_optimizer": [_P, _F, _F, _I],
     "rnet_model_forward": [_P, _P, _P, _I, _I],
     "rnet_model_backward": [_P, _P, _P, _I, _I],
     "rnet_model_zero_grad": [_P],
@@ -245,6 +246,10 @@ class Model:
     def set_precision(self, bf16: bool) -> None:
         """GEMM arithmetic: fp32-accurate (default) or bf16 operands / fp32 accumulation."""
         check(lib().rnet_model_set_precision(self._h, int(bool(bf16))))
+
+    def set_optimizer(self, momentum: float = 0.0, weight_decay: float = 0.0,
+                      warmup_steps: int = 0) -> None:
+        check(lib().rnet_model_set_optimizer(self._h, momentum, weight_decay, warmup_steps))
 
     def set_recompute(self, on: bool) -> None:
         """Keep only layer inputs and recompute each layer's caches in backward."""

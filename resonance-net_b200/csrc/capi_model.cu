@@ -152,6 +152,12 @@ int rnet_model_set_precision(rnet_model* m, int precision) {
   return m->e->set_precision(precision);
 }
 
+int rnet_model_set_optimizer(rnet_model* m, float momentum, float weight_decay,
+                             int warmup_steps) {
+  CHECK_M(m);
+  return m->e->set_optimizer(momentum, weight_decay, warmup_steps);
+}
+
 int rnet_model_set_recompute(rnet_model* m, int on) {
   CHECK_M(m);
   return m->e->set_recompute(on != 0);

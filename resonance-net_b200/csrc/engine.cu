@@ -81,6 +81,7 @@ Engine::~Engine() {
   cudaFree(VT_);
   cudaFree(params16_);
   cudaFree(KT16_);
+  cudaFree(velocity_);
   cudaFree(comm16_);
   cudaFree(dKV_);
   for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
@@ -699,9 +700,14 @@ int Engine::step(float lr, float clip) {
     world = dist_world(dist);
   }
   const bool bf = precision == 1;
-  PROF(PK_SGD, 2.0 * P_, (bf ? 18.0 : 16.0) * P_,
+  if (warmup_ > 0) {
+    const double f = (double)(step_count_ + 1) / warmup_;
+    if (f < 1.0) lr = (float)(lr * f);
+  }
+  ++step_count_;
+  PROF(PK_SGD, 2.0 * P_, (bf ? 18.0 : 16.0) * P_ + (velocity_ ? 8.0 * P_ : 0.0),
        rnet_k::sgd_clip_step(params_, grads_, P_, lr, clip, world, scratch_, norm_dev_, stream_,
-                             bf ? params16_ : nullptr));
+                             bf ? params16_ : nullptr, velocity_, momentum_, weight_decay_));
   cudaEvent_t pa = nullptr;
   if (prof_on_) prof_begin(&pa);
   int rc = refresh_shadows_impl(bf);
@@ -875,6 +881,26 @@ int Engine::generate(Decoder* d, int n_steps, int* d_out, bool use_graph) {
     if (d_out)
       CK(cudaMemcpyAsync(d_out + (size_t)i * d->M, d->tok, d->M * sizeof(int),
                          cudaMemcpyDeviceToDevice, s));
+  }
+  return RNET_OK;
+}
+
+int Engine::set_optimizer(float momentum, float weight_decay, int warmup_steps) {
+  if (!(momentum >= 0.0f && momentum < 1.0f) || !(weight_decay >= 0.0f) || warmup_steps < 0)
+    return rnet_status::fail(RNET_ERR_ARG,
+                             "set_optimizer: need 0 <= momentum < 1, weight_decay >= 0, "
+                             "warmup_steps >= 0");
+  momentum_ = momentum;
+  weight_decay_ = weight_decay;
+  warmup_ = warmup_steps;
+  step_count_ = 0;
+  CK(cudaStreamSynchronize(stream_));
+  if (momentum > 0.0f) {
+    if (!velocity_) CK(cudaMalloc(&velocity_, P_ * sizeof(float)));
+    CK(cudaMemsetAsync(velocity_, 0, P_ * sizeof(float), stream_));
+  } else {
+    cudaFree(velocity_);
+    velocity_ = nullptr;
   }
   return RNET_OK;
 }

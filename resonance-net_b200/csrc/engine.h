@@ -127,6 +127,13 @@ class Engine {
   int train_step(const int* d_in, const int* d_tgt, int B, int T, float lr, float clip,
                  float* d_loss_sum);
 
+  // Optimizer extensions (off by default: the reference's plain SGD with
+  // clipping, src/resonance_net.cpp:551-663): momentum, weight decay added
+  // after clipping, and a linear learning-rate warmup over warmup_steps
+  // (lr * min(1, (t + 1) / warmup) at step t; the reference parses
+  // TrainConfig::warmup_steps but never applies it). Resets the step count
+  // and the velocity.
+  int set_optimizer(float momentum, float weight_decay, int warmup_steps);
   int save(const char* path);
   // Checkpoint without stalling training: the parameters are snapshotted on
   // the model stream (device copy, ordered after everything queued so far),
@@ -219,6 +226,10 @@ class Engine {
                 *dqh_ = nullptr, *dPZHh_ = nullptr;
   bool cap_bf16_ = false;
   bool recompute_ = false;
+  float momentum_ = 0.0f, weight_decay_ = 0.0f;
+  int warmup_ = 0;
+  long long step_count_ = 0;
+  float* velocity_ = nullptr;
   // asynchronous save
   float* snap_ = nullptr;   // device snapshot of params_
   float* snap_host_ = nullptr;  // pinned

@@ -151,9 +151,13 @@ cudaError_t sample_rows(const float* logits, int M, int V, float temperature, fl
 //   p -= lr_eff * g
 // `scratch` = sgd_scratch_floats() floats. norm_out (optional) gets ||g||.
 // params16 (optional): the updated parameters rounded to bf16 as well.
+// Extensions (defaults = the reference's plain SGD): weight_decay adds
+// wd * p to the gradient after clipping; velocity (n floats) turns on
+// momentum: v = momentum * v + g (+ wd * p), p -= lr_eff * v.
 size_t sgd_scratch_floats();
 cudaError_t sgd_clip_step(float* params, const float* grads, size_t n, float lr, float clip,
                           int world, float* scratch, float* norm_out, cudaStream_t s,
-                          __nv_bfloat16* params16 = nullptr);
+                          __nv_bfloat16* params16 = nullptr, float* velocity = nullptr,
+                          float momentum = 0.0f, float weight_decay = 0.0f);
 
 }  // namespace rnet_k

@@ -61,18 +61,42 @@ __global__ void finalize_kernel(const double* __restrict__ part, int nparts, flo
   }
 }
 
+// Optional extensions (off by default, so the step is the reference's plain
+// SGD): weight decay wd adds wd * p to the gradient; momentum mu keeps a
+// velocity v = mu * v + g (+ wd * p) and steps along it.
+__device__ __forceinline__ float upd1(float p, float g, float* v, float neg, float mu, float wd) {
+  float d = g + wd * p;
+  if (v) {
+    d += mu * *v;
+    *v = d;
+  }
+  return p + neg * d;
+}
+
 __global__ void update_kernel(float* __restrict__ p, const float* __restrict__ g, size_t n,
-                              const float* __restrict__ lr_ptr, __nv_bfloat16* __restrict__ p16) {
+                              const float* __restrict__ lr_ptr, __nv_bfloat16* __restrict__ p16,
+                              float* __restrict__ vel, float mu, float wd) {
   rnet_dev::pdl_trigger();
   const float neg = -*lr_ptr;
   const size_t n4 = n / 4;
   float4* p4 = reinterpret_cast<float4*>(p);
   const float4* g4 = reinterpret_cast<const float4*>(g);
+  float4* v4 = reinterpret_cast<float4*>(vel);
+  const bool plain = vel == nullptr && wd == 0.0f;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
        i += (size_t)gridDim.x * blockDim.x) {
     float4 a = p4[i];
     const float4 b = g4[i];
-    a.x += neg * b.x; a.y += neg * b.y; a.z += neg * b.z; a.w += neg * b.w;
+    if (plain) {
+      a.x += neg * b.x; a.y += neg * b.y; a.z += neg * b.z; a.w += neg * b.w;
+    } else {
+      float4 v = vel ? v4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      a.x = upd1(a.x, b.x, vel ? &v.x : nullptr, neg, mu, wd);
+      a.y = upd1(a.y, b.y, vel ? &v.y : nullptr, neg, mu, wd);
+      a.z = upd1(a.z, b.z, vel ? &v.z : nullptr, neg, mu, wd);
+      a.w = upd1(a.w, b.w, vel ? &v.w : nullptr, neg, mu, wd);
+      if (vel) v4[i] = v;
+    }
     p4[i] = a;
     if (p16) {
       const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
@@ -84,7 +108,7 @@ __global__ void update_kernel(float* __restrict__ p, const float* __restrict__ g
   }
   if (blockIdx.x == 0)
     for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) {
-      p[i] += neg * g[i];
+      p[i] = upd1(p[i], g[i], vel ? vel + i : nullptr, neg, mu, wd);
       if (p16) p16[i] = __float2bfloat16_rn(p[i]);
     }
 }
@@ -140,7 +164,8 @@ cudaError_t from_bf16(const __nv_bfloat16* x, float* y, size_t n, cudaStream_t s
 
 cudaError_t sgd_clip_step(float* params, const float* grads, size_t n, float lr, float clip,
                           int world, float* scratch, float* norm_out, cudaStream_t s,
-                          __nv_bfloat16* params16) {
+                          __nv_bfloat16* params16, float* velocity, float momentum,
+                          float weight_decay) {
   if (!n) return cudaSuccess;
   if ((reinterpret_cast<uintptr_t>(params) | reinterpret_cast<uintptr_t>(grads)) & 15)
     return cudaErrorInvalidValue;
@@ -148,7 +173,8 @@ cudaError_t sgd_clip_step(float* params, const float* grads, size_t n, float lr,
   float* lr_dev = scratch + 2 * NORM_BLOCKS;
   sumsq_kernel<<<NORM_BLOCKS, 256, 0, s>>>(grads, n, part);
   finalize_kernel<<<1, 256, 0, s>>>(part, NORM_BLOCKS, lr, clip, world, lr_dev, norm_out);
-  update_kernel<<<148 * 8, 256, 0, s>>>(params, grads, n, lr_dev, params16);
+  update_kernel<<<148 * 8, 256, 0, s>>>(params, grads, n, lr_dev, params16, velocity, momentum,
+                                        weight_decay);
   return launched(3);
 }
 

@@ -194,3 +194,38 @@ def test_recompute_matches_cached_step(rnet, rdata, orc, cuda, bf16):
     assert abs(outs[0][0] - outs[1][0]) <= 1e-6 * abs(outs[0][0])
     assert rel_err(outs[1][1], outs[0][1]) <= 1e-6
     assert update_rel_err(params, outs[1][2], outs[0][2]) <= 1e-5
+
+
+def test_optimizer_extensions(rnet, rdata, orc, cuda):
+    """Momentum, weight decay and linear warmup (rnet_model_set_optimizer)
+    against a numpy restatement of the rule, step by step, using the step's
+    own gradients (still in the gradient buffer after the step): clip on the
+    raw gradient norm, lr_t = lr * min(1, (t+1)/warmup) * min(1, clip/||g||),
+    v = mu v + g + wd p, p -= lr_t v. With all three off the step is the
+    reference's SGD (checked against the oracle elsewhere)."""
+    torch = cuda
+    c = dict(CASES["cfg_tiny"])
+    cfg, params, tok, tgt = _make(orc, rdata, c)
+    rcfg = _rcfg(rnet, cfg)
+    B, T = c["B"], c["T"]
+    m = rnet.Model(rcfg, device=0, reference_init=False)
+    m.set_params(params)
+    mu, wd, warm, lr, clip = 0.9, 0.01, 3, 3e-3, 1.0
+    m.set_optimizer(mu, wd, warm)
+    d_in = torch.from_numpy(tok.reshape(-1)).cuda()
+    d_tgt = torch.from_numpy(tgt.reshape(-1)).cuda()
+    p = params.astype(np.float64)
+    v = np.zeros_like(p)
+    for t in range(5):
+        m.train_step(d_in, d_tgt, B, T, lr, clip)
+        g = m.get_grads().astype(np.float64)
+        norm = np.linalg.norm(g)
+        lr_t = lr * min(1.0, (t + 1) / warm) * (min(1.0, clip / norm) if norm > 0 else 1.0)
+        v = mu * v + g + wd * p
+        want = p - lr_t * v
+        got = m.get_params().astype(np.float64)
+        assert rel_err(got - p, want - p) <= 1e-4, f"step {t}"
+        p = got  # continue from the library's fp32 parameters
+    with pytest.raises(rnet.RnetError):
+        m.set_optimizer(1.5, 0.0, 0)
+    m.close()
