@@ -224,7 +224,8 @@ def test_optimizer_extensions(rnet, rdata, orc, cuda):
         v = mu * v + g + wd * p
         want = p - lr_t * v
         got = m.get_params().astype(np.float64)
-        assert rel_err(got - p, want - p) <= 1e-4, f"step {t}"
+        # one-ulp differences of the fp32 parameters are rounding, not the rule
+        assert update_rel_err(p, got, want) <= 1e-4, f"step {t}"
         p = got  # continue from the library's fp32 parameters
     with pytest.raises(rnet.RnetError):
         m.set_optimizer(1.5, 0.0, 0)
