@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(WARPS * 32)
 // block reduction through a double-buffered shared array (one barrier per
 // row); each thread keeps the dw partial of its fixed columns in registers
 // over all rows of the CTA and flushes it once with atomics.
-constexpr int RB_THREADS = 128;
+constexpr int RB_THREADS = 256;
 
 template <int VPT>
 __global__ void __launch_bounds__(RB_THREADS)
@@ -418,8 +418,8 @@ cudaError_t bwd_t(const float* dy, const float* x, const float* w, const float* 
     return launched();
   }
   if constexpr (VPL >= 8) {
-    // wide rows: a row per 128-thread CTA (VPL / 4 float4 per thread)
-    constexpr int VPT = VPL / 4;
+    // wide rows: a row per 256-thread CTA (VPL / 8 float4 per thread)
+    constexpr int VPT = VPL / 8;
     int grid = sm_count() * 4;
     if (grid > rows) grid = rows;
     rms_bwd_rowblock_kernel<VPT><<<grid, RB_THREADS, 0, s>>>(dy, x, w, rinv, dx, dw, rows, D,
