@@ -42,6 +42,12 @@ CFG = dict(d_model=512, n_layers=8, d_ff=1024, n_slots=1024, top_k=2, vocab=256,
 CFG5 = dict(d_model=2048, n_layers=24, d_ff=5632, n_slots=8192, top_k=2, vocab=256, seq_len=2048)
 METRIC5 = "train tok/s (d2048 L24 F5632 S8192, B16 T2048 per GPU, bf16)"
 LR, CLIP = 3e-4, 1.0
+# Algorithmic bytes per [N, D] element of one launch (fp32): scan fwd reads
+# pz, ph, writes h, z; scan bwd reads dy, z, h, h~, writes dz, dh~; conv fwd
+# reads x, writes S; conv bwd reads dS, x, writes dx; RMSNorm fwd reads x,
+# writes y; RMSNorm bwd reads dy, x, writes dx.
+ALG_BYTES_PER_ELEM = {"scan_fwd": 16, "scan_bwd": 24, "conv_fwd": 8, "conv_bwd": 12,
+                      "rms_fwd": 8, "rms_bwd": 12}
 POOL = 8
 
 
@@ -352,6 +358,13 @@ def run_ours(args, rank, world, local):
             if v["ms"] > 0 and v["bytes"] > 0 and k != "gemm":
                 kernels[k]["GBps"] = round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1)
                 kernels[k]["hbm_frac"] = round(kernels[k]["GBps"] / peaks["hbm"], 3)
+            # the same time against the survey's algorithmic bytes per [N, D]
+            # element (the kernels' own extra outputs, e.g. the scan's saved
+            # e and second residual copy, not counted as work)
+            if k in ALG_BYTES_PER_ELEM and v["ms"] > 0:
+                alg = ALG_BYTES_PER_ELEM[k] * B * T * C["d_model"] * v["launches"]
+                kernels[k]["alg_GBps"] = round(alg / (v["ms"] * 1e-3) / 1e9, 1)
+                kernels[k]["alg_hbm_frac"] = round(kernels[k]["alg_GBps"] / peaks["hbm"], 3)
     out = {
         "metric": METRIC5 if c5 else METRIC, "value": round(tokens / (ms * 1e-3), 1), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
