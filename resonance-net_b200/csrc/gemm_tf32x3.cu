@@ -27,6 +27,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -49,7 +51,10 @@ constexpr int NUM_SPLIT_WARPS = 8;
 constexpr int NUM_THREADS = 32 * (FIRST_SPLIT_WARP + NUM_SPLIT_WARPS);
 constexpr int SMEM_BUDGET = 200 * 1024;  // pipeline stages (barriers etc. extra)
 constexpr int TILE_LD = 33;              // epilogue transpose tile: 32 x 33 floats per warp
-constexpr int EPI_TILE_FLOATS = 32 * TILE_LD;
+// per-warp epilogue slot: a 32 x 33 transpose tile, or a 32 x 32 fp32 tile in
+// the SWIZZLE_128B layout a TMA store reads (slots 1024-byte aligned)
+constexpr int EPI_TILE_FLOATS = 1280;
+static_assert(EPI_TILE_FLOATS >= 32 * TILE_LD && (EPI_TILE_FLOATS * 4) % 1024 == 0, "epi slot");
 
 struct KParams {
   int M, N, K;
@@ -67,6 +72,10 @@ struct KParams {
   // stores (32 lines per instruction) would bound the kernel, and no split
   // warps compete for shared memory.
   int stage_epi;
+  // 1: store / accumulate tiles leave through TMA (bulk tensor store or
+  // reduce-add of each warp's 32 x 32 tile from shared memory), the store
+  // map being the kernel's tmC
+  int tma_out;
   Epilogue epi;
   unsigned* err;
 };
@@ -269,6 +278,29 @@ __device__ __forceinline__ void prefetch_epilogue_inputs(const KParams& p, int r
   }
 }
 
+// Bulk tensor store / reduce-add of one 32 x 32 fp32 tile (SWIZZLE_128B in
+// shared memory) to (x = col, y = row) of the map; bulk-group completion.
+__device__ __forceinline__ void tma_store_tile(const void* map, const void* smem, int x, int y,
+                                               bool reduce_add) {
+  if (reduce_add)
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], "
+        "[%3];" ::"l"(map), "r"(x), "r"(y), "r"(smem_u32(smem))
+        : "memory");
+  else
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map),
+        "r"(x), "r"(y), "r"(smem_u32(smem))
+        : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 struct Top2State {
   float h0, h1;
   int i0, i1;
@@ -283,7 +315,7 @@ template <int BN>
 __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc, int row0,
                                                  int nt, bool last_sub, Top2State& st,
                                                  float* tile, size_t c_off, int cfirst = 0,
-                                                 int cstep = 1) {
+                                                 int cstep = 1, const void* tmC = nullptr) {
   const Epilogue& e = p.epi;
   const int lane = threadIdx.x & 31;
   const int row = row0 + lane;
@@ -337,13 +369,32 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
   }
   if (p.stage_epi) {
     const int op = e.kind == EPI_STORE ? 0 : (e.kind == EPI_ACCUM ? 1 : 2);
+    const bool tma = p.tma_out && ((op == 0 && e.C16 == nullptr) || op == 1);
 #pragma unroll 1
     for (int c = cfirst; c < BN / 32; c += cstep) {
       tmem_ld_32cols(tacc + c * 32, v);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] *= e.alpha;
-      tile_out(tile, v, e.C + c_off, e.ldc, e.R, e.ldr, row0, nt * BN + c * 32, p.M, p.N, op,
-               op == 1 ? nullptr : e.C16);
+      if (tma) {
+        // the previous chunk's bulk copy has finished reading the slot
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        float4* t4 = reinterpret_cast<float4*>(tile);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          t4[lane * 8 + (j ^ (lane & 7))] =
+              make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tma_store_tile(tmC, tile, nt * BN + c * 32, row0, op == 1);
+      } else {
+        tile_out(tile, v, e.C + c_off, e.ldc, e.R, e.ldr, row0, nt * BN + c * 32, p.M, p.N, op,
+                 op == 1 ? nullptr : e.C16);
+      }
+    }
+    if (tma) {
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
     }
     return;
   }
@@ -430,7 +481,8 @@ __device__ __forceinline__ void load_b(uint8_t* sb, const void* map, uint64_t* b
 template <int BN, int BK, int CG, int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
-                       const __grid_constant__ CUtensorMap tmB, const KParams p) {
+                       const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ CUtensorMap tmC, const KParams p) {
   rnet_dev::pdl_trigger();
   constexpr bool BF = MODE == 1;
   // MODE 2: four of the idle split warps (6-9) become a second epilogue set
@@ -715,7 +767,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             p.split_stride ? (size_t)p.split_stride * (size_t)(kb0 / p.kb_per_split) : 0;
         epilogue_subtile<BN>(p, tacc, row0, nt, nt == nt1 - 1, st,
                              epi_tiles + eslot * EPI_TILE_FLOATS, c_off, eset,
-                             NEPI / NUM_EPI_WARPS);
+                             NEPI / NUM_EPI_WARPS, &tmC);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -723,6 +775,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+    // the warp's bulk stores have completed before the CTA exits
+    if (p.tma_out && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -791,6 +845,11 @@ static cudaError_t reject(const char* why) {
 
 // Test hook: force the CTA group (0 = automatic).
 static int g_force_cg = 0;
+// RNET_GEMM_TMA_OUT=0 keeps the bf16 path's stores on the warps (A/B timing)
+static const bool g_tma_out = [] {
+  const char* e = getenv("RNET_GEMM_TMA_OUT");
+  return !(e && e[0] == '0');
+}();
 void set_force_cta_group(int cg) { g_force_cg = (cg == 1 || cg == 2) ? cg : 0; }
 
 int num_sms() {
@@ -806,7 +865,7 @@ int num_sms() {
 
 template <int BN, int BK, int CG, int MODE>
 static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
-                          const KParams& kp) {
+                          const CUtensorMap& tc, const KParams& kp) {
   using C = Cfg<BN, BK, CG, MODE == 2 ? 2 : 4, MODE != 2,
                 MODE == 2 ? 2 * NUM_EPI_WARPS : NUM_EPI_WARPS>;
   static bool configured = false;
@@ -857,7 +916,8 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
   }
   const int groups = kp.num_units < max_groups ? kp.num_units : max_groups;
   cfg.gridDim = dim3(groups * CG);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, BK, CG, MODE>, ta, tb, kp);
+  cudaError_t e =
+      cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, BK, CG, MODE>, ta, tb, tc, kp);
   if (e != cudaSuccess) {
     g_reason = "kernel launch";
     return e;
@@ -1070,32 +1130,43 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
     return !B.mn_major ? make_map(m, base, (uint64_t)K, b_rows, B.ld, BK, b_box, kswz, st16)
                        : make_map(m, base, b_rows, (uint64_t)K, B.ld, mn_box, BK, mswz, st16);
   };
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;
   if (!map_a(&ta, A.p)) return reject("tensor map of A rejected");
   if (!map_b(&tb, B.p)) return reject("tensor map of B rejected");
+  // bf16 tiles: plain stores / accumulations leave through TMA when C allows
+  // a tensor map (16-byte aligned base and row pitch)
+  std::memset(&tc, 0, sizeof(tc));
+  kp.tma_out = 0;
+  if (st16 && kp.split_stride == 0 && g_tma_out &&
+      ((epi.kind == EPI_STORE && epi.C16 == nullptr) || epi.kind == EPI_ACCUM) &&
+      (reinterpret_cast<uintptr_t>(epi.C) & 15) == 0 &&
+      epi.ldc % 4 == 0 && epi.ldc >= N &&
+      make_map(&tc, epi.C, (uint64_t)N, (uint64_t)M, epi.ldc, 32, 32,
+               CU_TENSOR_MAP_SWIZZLE_128B))
+    kp.tma_out = 1;
 
   cudaError_t e;
   if (st16) {
     if (CG == 2)
-      e = BN == 128 ? launch<128, 64, 2, 2>(stream, ta, tb, kp)
-                    : launch<256, 64, 2, 2>(stream, ta, tb, kp);
+      e = BN == 128 ? launch<128, 64, 2, 2>(stream, ta, tb, tc, kp)
+                    : launch<256, 64, 2, 2>(stream, ta, tb, tc, kp);
     else
-      e = BN == 128 ? launch<128, 64, 1, 2>(stream, ta, tb, kp)
-                    : launch<256, 64, 1, 2>(stream, ta, tb, kp);
+      e = BN == 128 ? launch<128, 64, 1, 2>(stream, ta, tb, tc, kp)
+                    : launch<256, 64, 1, 2>(stream, ta, tb, tc, kp);
   } else if (bf) {
     if (CG == 2)
-      e = BN == 128 ? launch<128, 16, 2, 1>(stream, ta, tb, kp)
-                    : launch<256, 16, 2, 1>(stream, ta, tb, kp);
+      e = BN == 128 ? launch<128, 16, 2, 1>(stream, ta, tb, tc, kp)
+                    : launch<256, 16, 2, 1>(stream, ta, tb, tc, kp);
     else
-      e = BN == 128 ? launch<128, 16, 1, 1>(stream, ta, tb, kp)
-                    : launch<256, 16, 1, 1>(stream, ta, tb, kp);
+      e = BN == 128 ? launch<128, 16, 1, 1>(stream, ta, tb, tc, kp)
+                    : launch<256, 16, 1, 1>(stream, ta, tb, tc, kp);
   } else {
     if (CG == 2)
-      e = BN == 128 ? launch<128, 16, 2, 0>(stream, ta, tb, kp)
-                    : launch<256, 16, 2, 0>(stream, ta, tb, kp);
+      e = BN == 128 ? launch<128, 16, 2, 0>(stream, ta, tb, tc, kp)
+                    : launch<256, 16, 2, 0>(stream, ta, tb, tc, kp);
     else
-      e = BN == 128 ? launch<128, 16, 1, 0>(stream, ta, tb, kp)
-                    : launch<256, 16, 1, 0>(stream, ta, tb, kp);
+      e = BN == 128 ? launch<128, 16, 1, 0>(stream, ta, tb, tc, kp)
+                    : launch<256, 16, 1, 0>(stream, ta, tb, tc, kp);
   }
   if (e != cudaSuccess || kp.split_stride == 0) return e;
   // fixed-order sum of the partials + the caller's epilogue
