@@ -621,12 +621,12 @@ int Engine::backward(const float* d_dlogits, const int* d_tokens, int B, int T) 
   const size_t ND = (size_t)N * cfg_.d_model;
   // Gradient buckets: contiguous ranges of the flat gradient buffer, a layer
   // at a time from the last layer down, merged until a bucket holds at least
-  // bucket_bytes_ (25 MB by default, RNET_DP_BUCKET_MB overrides), then
+  // bucket_bytes_ (4 MB by default, RNET_DP_BUCKET_MB overrides), then
   // all-reduced on the comm stream while the backward goes on.
   if (bucket_bytes_ == 0) {
     const char* e = getenv("RNET_DP_BUCKET_MB");
-    const double mb = e ? atof(e) : 25.0;
-    bucket_bytes_ = (size_t)((mb > 0 ? mb : 25.0) * 1e6);
+    const double mb = e ? atof(e) : 4.0;
+    bucket_bytes_ = (size_t)((mb > 0 ? mb : 4.0) * 1e6);
   }
   // bf16 mode: gradient buckets travel as bf16 (one staging buffer of the
   // largest bucket; the comm stream orders its reuse)

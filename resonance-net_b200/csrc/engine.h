@@ -238,7 +238,7 @@ class Engine {
   void* save_thread_ = nullptr;  // std::thread*
   int save_status_ = 0;
   std::string save_msg_;
-  size_t bucket_bytes_ = 0;  // data-parallel bucket size (0: read RNET_DP_BUCKET_MB, default 25)
+  size_t bucket_bytes_ = 0;  // data-parallel bucket size (0: read RNET_DP_BUCKET_MB, default 4)
   __nv_bfloat16* comm16_ = nullptr;  // bf16 all-reduce staging (bf16 mode, DP)
   size_t comm16_count_ = 0;
   bool cap_recompute_ = false;
