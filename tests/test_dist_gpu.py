@@ -22,11 +22,11 @@ def _port():
 
 
 @pytest.mark.parametrize("bf16,bucket_mb", [(False, 0), (True, 0), (False, 0.01)],
-                         ids=["fp32-25MB", "bf16-25MB", "fp32-per-layer"])
+                         ids=["fp32-default", "bf16-default", "fp32-10KB"])
 def test_dp_two_gpus_matches_one(rnet, rdata, cuda, tmp_path, bf16, bucket_mb):
     """bf16: bf16 GEMM operands on both sides and bf16 on the wire for the
     two-GPU gradient all-reduce; compared at the bf16 tolerance (2e-2).
-    Buckets: the default 25 MB (the whole small model in one bucket) and
+    Buckets: the default 4 MB (the whole small model in one bucket) and
     10 KB (every layer its own bucket, the head in the last one)."""
     torch = cuda
     if torch.cuda.device_count() < 2:
