@@ -76,6 +76,9 @@ struct KParams {
   // reduce-add of each warp's 32 x 32 tile from shared memory), the store
   // map being the kernel's tmC
   int tma_out;
+  // SwiGLU forward: 2 or 3 when G, U (and H) are planes of one 3-D tensor
+  // map (tmC: [planes][M][ldf]) that TMA stores; 0 = warp stores
+  int swiglu_planes;
   Epilogue epi;
   unsigned* err;
 };
@@ -294,6 +297,16 @@ __device__ __forceinline__ void tma_store_tile(const void* map, const void* smem
         : "memory");
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
+// 3-D form (z = plane) for the SwiGLU outputs.
+__device__ __forceinline__ void tma_store_tile3(const void* map, const void* smem, int x, int y,
+                                                int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+          map),
+      "r"(x), "r"(y), "r"(z), "r"(smem_u32(smem))
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
@@ -320,20 +333,51 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
   const int lane = threadIdx.x & 31;
   const int row = row0 + lane;
   float v[32];
-  if ((e.kind == EPI_SWIGLU_FWD || e.kind == EPI_TOP2) && cfirst != 0) return;
+  if (e.kind == EPI_TOP2 && cfirst != 0) return;
   if (e.kind == EPI_SWIGLU_FWD) {
     constexpr int HALF_CHUNKS = BN / 64;
+    // one 32 x 32 tile through TMA: swizzled into the warp's slot, stored
+    // as plane z (the slot is free again once the copy has read it)
+    auto tma_plane = [&](const float (&x)[32], int f0, int z) {
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+      float4* t4 = reinterpret_cast<float4*>(tile);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        t4[lane * 8 + (j ^ (lane & 7))] =
+            make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tma_store_tile3(tmC, tile, f0, row0, z);
+    };
 #pragma unroll 1
-    for (int c = 0; c < HALF_CHUNKS; ++c) {
+    for (int c = cfirst; c < HALF_CHUNKS; c += cstep) {
       float g[32];
       tmem_ld_32cols(tacc + c * 32, g);
       tmem_ld_32cols(tacc + (c + HALF_CHUNKS) * 32, v);
       const int f0 = nt * (BN / 2) + c * 32;
-      tile_out(tile, g, e.G, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0);
-      tile_out(tile, v, e.U, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0);
+      if (p.swiglu_planes) {
+        tma_plane(g, f0, 0);
+        tma_plane(v, f0, 1);
+      } else {
+        tile_out(tile, g, e.G, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0);
+        tile_out(tile, v, e.U, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0);
+      }
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = silu_fast(g[i]) * v[i];
-      tile_out(tile, v, e.H, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0, e.H16);
+      if (p.swiglu_planes == 3) {
+        tma_plane(v, f0, 2);
+      } else {
+        if (p.swiglu_planes) {
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+        }
+        tile_out(tile, v, e.H, e.ldf, nullptr, 0, row0, f0, p.M, p.N, 0, e.H16);
+      }
+    }
+    if (p.swiglu_planes) {
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
     }
     return;
   }
@@ -776,7 +820,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     // the warp's bulk stores have completed before the CTA exits
-    if (p.tma_out && lane == 0) bulk_wait_all();
+    if ((p.tma_out || p.swiglu_planes) && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -1145,6 +1189,30 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
       make_map(&tc, epi.C, (uint64_t)N, (uint64_t)M, epi.ldc, 32, 32,
                CU_TENSOR_MAP_SWIZZLE_128B))
     kp.tma_out = 1;
+  // SwiGLU forward: G, U (and H) through one 3-D map when they are
+  // equally spaced planes (the engine allocates them back to back)
+  kp.swiglu_planes = 0;
+  if (epi.kind == EPI_SWIGLU_FWD && kp.split_stride == 0 && g_tma_out && epi.G && epi.U &&
+      epi.U > epi.G && epi.ldf % 4 == 0 && epi.ldf >= N &&
+      ((reinterpret_cast<uintptr_t>(epi.G) & 15) == 0)) {
+    const size_t plane = (size_t)(epi.U - epi.G);
+    const bool h_adj = epi.H && epi.H16 == nullptr && (size_t)(epi.H - epi.U) == plane;
+    const int planes = h_adj ? 3 : 2;
+    if (plane % 4 == 0 && plane >= (size_t)M * epi.ldf) {
+      const uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)planes};
+      const uint64_t strides[2] = {(uint64_t)epi.ldf * 4, (uint64_t)plane * 4};
+      const uint32_t box[3] = {32, 32, 1};
+      auto enc = get_encode_fn();
+      cuuint64_t d[3] = {dims[0], dims[1], dims[2]}, st[2] = {strides[0], strides[1]};
+      cuuint32_t bx[3] = {box[0], box[1], box[2]}, es[3] = {1, 1, 1};
+      if (enc &&
+          enc(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(epi.G), d, st, bx, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+        kp.swiglu_planes = planes;
+    }
+  }
   // fp32 tiles: the staged path only pays with TMA stores (split-K partial
   // planes and residual epilogues keep thread-per-row stores, which leave
   // shared memory to the split warps)
