@@ -430,7 +430,12 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
               make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) tma_store_tile(tmC, tile, nt * BN + c * 32, row0, op == 1);
+        if (lane == 0) {
+          if (p.tma_out == 2)  // split-K partial: plane = split index
+            tma_store_tile3(tmC, tile, nt * BN + c * 32, row0, (int)(c_off / p.split_stride));
+          else
+            tma_store_tile(tmC, tile, nt * BN + c * 32, row0, op == 1);
+        }
       } else {
         tile_out(tile, v, e.C + c_off, e.ldc, e.R, e.ldr, row0, nt * BN + c * 32, p.M, p.N, op,
                  op == 1 ? nullptr : e.C16);
@@ -1189,6 +1194,18 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
       make_map(&tc, epi.C, (uint64_t)N, (uint64_t)M, epi.ldc, 32, 32,
                CU_TENSOR_MAP_SWIZZLE_128B))
     kp.tma_out = 1;
+  // split-K partial planes: one 3-D map over the workspace, z = split index
+  if (kp.split_stride != 0 && g_tma_out && N % 4 == 0) {
+    auto enc = get_encode_fn();
+    cuuint64_t d[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)kp.k_splits};
+    cuuint64_t st[2] = {(cuuint64_t)N * 4, (cuuint64_t)M * N * 4};
+    cuuint32_t bx[3] = {32, 32, 1}, es[3] = {1, 1, 1};
+    if (enc && enc(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, kp.epi.C, d, st, bx, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      kp.tma_out = 2;
+  }
   // SwiGLU forward: G, U (and H) through one 3-D map when they are
   // equally spaced planes (the engine allocates them back to back)
   kp.swiglu_planes = 0;
