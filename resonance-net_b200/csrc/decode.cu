@@ -252,8 +252,11 @@ __device__ __forceinline__ void top2_merge(float& a1, float& a2, float b1, float
   a2 = m2;
 }
 
+// VT / r (optional): the warp also gathers r[row] = w0 VT[i0] + w1 VT[i1]
+// (the slot_gather of the selected pair, same arithmetic), saving a launch.
 __global__ void topk2_rows_kernel(const float* __restrict__ scores, int* __restrict__ idx,
-                                  float* __restrict__ w, int M, int S) {
+                                  float* __restrict__ w, int M, int S,
+                                  const float* __restrict__ VT, float* __restrict__ r, int D) {
   rnet_dev::pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -315,14 +318,27 @@ __global__ void topk2_rows_kernel(const float* __restrict__ scores, int* __restr
       i1 = __shfl_sync(0xffffffffu, i1, src);
     }
   }
+  const float mx = fmaxf(h0, h1);
+  const float e0 = __expf(h0 - mx), e1 = __expf(h1 - mx);
+  const float sum = e0 + e1;
+  const float w0 = e0 / sum, w1 = e1 / sum;
   if (lane == 0) {
-    const float mx = fmaxf(h0, h1);
-    const float e0 = __expf(h0 - mx), e1 = __expf(h1 - mx);
-    const float sum = e0 + e1;
     idx[2 * (size_t)row] = i0;
     idx[2 * (size_t)row + 1] = i1;
-    w[2 * (size_t)row] = e0 / sum;
-    w[2 * (size_t)row + 1] = e1 / sum;
+    w[2 * (size_t)row] = w0;
+    w[2 * (size_t)row + 1] = w1;
+  }
+  if (r) {
+    const int id[2] = {i0, i1};
+    const float ww[2] = {w0, w1};
+    for (int c = lane * 4; c < D; c += 128) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < 2; ++j) {
+        const float4 v = *reinterpret_cast<const float4*>(VT + (size_t)id[j] * D + c);
+        acc.x += ww[j] * v.x; acc.y += ww[j] * v.y; acc.z += ww[j] * v.z; acc.w += ww[j] * v.w;
+      }
+      *reinterpret_cast<float4*>(r + (size_t)row * D + c) = acc;
+    }
   }
 }
 
@@ -337,9 +353,11 @@ cudaError_t silu_mul_rows(const float* gu, float* h, int M, int F, cudaStream_t 
   return launched();
 }
 
-cudaError_t topk2_rows(const float* scores, int* idx, float* w, int M, int S, cudaStream_t s) {
+cudaError_t topk2_rows(const float* scores, int* idx, float* w, int M, int S, cudaStream_t s,
+                       const float* VT, float* r, int D) {
   if (M <= 0) return cudaSuccess;
-  topk2_rows_kernel<<<(M + 7) / 8, 256, 0, s>>>(scores, idx, w, M, S);
+  if (r && (D % 4 || !VT)) return cudaErrorInvalidValue;
+  topk2_rows_kernel<<<(M + 7) / 8, 256, 0, s>>>(scores, idx, w, M, S, VT, r, D);
   return launched();
 }
 

@@ -824,20 +824,37 @@ int Engine::decode_step(Decoder* d, const int* d_tokens) {
     CK(rnet_k::decode_conv(d->n, ring, d->pos, w.c3, w.c7, w.c15, d->S, M, D, s));
     MM_RES(M, D, D, kmaj(d->S, D), kmaj(w.mix, D), d->x);
     CK(rnet_k::rms_norm_fwd(d->x, w.n2, d->n, nullptr, M, D, eps, s));
-    MM(M, 2 * D, D, kmaj(d->n, D), kmaj(w.Wz, D), epi_store(d->P, 2 * D), 0);
-    CK(rnet_k::decode_gru(d->P, w.bz, w.bh, h, d->x, M, D, s));
+    {
+      // gate pre-activations -> GRU state update + residual where the
+      // split-K partials are summed (one launch fewer)
+      Epilogue e;
+      e.kind = EPI_PAIR_GRU;
+      e.C = d->P;
+      e.ldf = D;
+      e.b0 = w.bz;
+      e.b1 = w.bh;
+      e.state = h;
+      e.xres = d->x;
+      MM(M, 2 * D, D, kmaj(d->n, D), kmaj(w.Wz, D), e, 0);
+    }
     CK(rnet_k::rms_norm_fwd(d->x, w.n3, d->n, nullptr, M, D, eps, s));
     MM(M, D, D, kmaj(d->n, D), kmaj(w.pq, D), epi_store(d->q, D), 0);
     // short M: scores through the split-K GEMM, then a warp-per-row top-2
     // (the row-owner top-2 epilogue would run on M / 128 CTAs)
     MM(M, S, D, kmaj(d->q, D), kmaj(KT_ + (size_t)l * S * D, D), epi_store(d->scores, S), 0);
-    CK(rnet_k::topk2_rows(d->scores, d->idx, d->w, M, S, s));
-    CK(rnet_k::slot_gather(d->idx, d->w, VT_ + (size_t)l * S * D, d->r, M, D, S, 2, err, s));
+    // top-2 + softmax + value gather in one warp-per-row launch
+    CK(rnet_k::topk2_rows(d->scores, d->idx, d->w, M, S, s, VT_ + (size_t)l * S * D, d->r, D));
     MM_RES(M, D, D, kmaj(d->r, D), kmaj(w.pout, D), d->x);
     CK(rnet_k::rms_norm_fwd(d->x, w.n4, d->n, nullptr, M, D, eps, s));
     // gate|up as one [2F, D] operand (adjacent in the parameter buffer)
-    MM(M, 2 * F, D, kmaj(d->n, D), kmaj(w.gate, D), epi_store(d->GU, 2 * F), 0);
-    CK(rnet_k::silu_mul_rows(d->GU, d->H, M, F, s));
+    {
+      Epilogue e;  // gate|up -> silu(gate) * up where the partials are summed
+      e.kind = EPI_PAIR_SILU;
+      e.C = d->GU;
+      e.H = d->H;
+      e.ldf = F;
+      MM(M, 2 * F, D, kmaj(d->n, D), kmaj(w.gate, D), e, 0);
+    }
     MM_RES(M, D, F, kmaj(d->H, F), kmaj(w.down, F), d->x);
   }
   CK(rnet_k::rms_norm_fwd(d->x, fnorm_, d->n, nullptr, M, D, eps, s));

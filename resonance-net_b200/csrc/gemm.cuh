@@ -36,6 +36,12 @@ enum EpiKind : int {
   EPI_RESID = 2,       // C = R + alpha*acc
   EPI_SWIGLU_FWD = 3,  // paired B: G = acc[gate], U = acc[up], H = silu(G)*U
   EPI_TOP2 = 5,        // row-owner: running top-2 over N, softmax, idx/w (+optional C)
+  // Paired-column epilogues of a plain GEMM whose N = 2 * ldf columns are
+  // two halves [a | b]; applied where the split-K partials are summed (no
+  // extra launch), or after a plain store into C when K is not split.
+  EPI_PAIR_SILU = 6,   // H[r, f] = silu(a) * b          (C: [M, 2 ldf] scratch)
+  EPI_PAIR_GRU = 7,    // z = sigmoid(a + b0), h~ = b + b1, state = (1 - z) state + z h~,
+                       // xres += state                  (state, xres: [M, ldf])
 };
 
 struct Epilogue {
@@ -58,6 +64,11 @@ struct Epilogue {
   // EPI_STORE / EPI_RESID, H16 with EPI_SWIGLU_FWD
   __nv_bfloat16* C16 = nullptr;
   __nv_bfloat16* H16 = nullptr;
+  // EPI_PAIR_GRU: biases of the two halves, recurrent state, residual stream
+  const float* b0 = nullptr;
+  const float* b1 = nullptr;
+  float* state = nullptr;
+  float* xres = nullptr;
 };
 
 // Launch. Both operands fp32 (3xTF32 or bf16-rounded per `precision`) or

@@ -979,6 +979,47 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
 // fill the GPU. Their K range is split over extra CTAs that store partial
 // tiles into a workspace; splitk_reduce sums the partials in split order (so
 // results do not depend on scheduling) and applies the epilogue.
+// Paired-column rules over S partial planes [M, 2h] (S = 1: a stored C):
+// a = sum of column f, b = sum of column h + f, summed in split order.
+// Same formulas as the decode step's separate kernels (silu_mul_rows,
+// decode_gru), so the results do not depend on the fusion.
+__global__ void __launch_bounds__(256)
+    splitk_pair_kernel(const float* __restrict__ ws, int S, int M, int h, Epilogue e) {
+  rnet_dev::pdl_trigger();
+  const size_t plane = (size_t)M * 2 * h;
+  const int h4 = h >> 2;
+  const size_t n4 = (size_t)M * h4;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / h4;
+    const int c = (int)(i - r * h4) * 4;
+    const float* src = ws + r * 2 * h + c;
+    float4 a = *reinterpret_cast<const float4*>(src);
+    float4 b = *reinterpret_cast<const float4*>(src + h);
+    for (int k = 1; k < S; ++k) {
+      const float4 pa = *reinterpret_cast<const float4*>(src + k * plane);
+      const float4 pb = *reinterpret_cast<const float4*>(src + k * plane + h);
+      a.x += pa.x; a.y += pa.y; a.z += pa.z; a.w += pa.w;
+      b.x += pb.x; b.y += pb.y; b.z += pb.z; b.w += pb.w;
+    }
+    const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+    const size_t o = r * e.ldf + c;
+    if (e.kind == EPI_PAIR_SILU) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) e.H[o + j] = av[j] / (1.0f + __expf(-av[j])) * bv[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float z = 1.0f / (1.0f + __expf(-(av[j] + e.b0[c + j])));
+        const float ht = bv[j] + e.b1[c + j];
+        const float hn = (1.f - z) * e.state[o + j] + z * ht;
+        e.state[o + j] = hn;
+        e.xres[o + j] += hn;
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256)
     splitk_reduce_kernel(const float* __restrict__ ws, int S, int M, int N, Epilogue e) {
   rnet_dev::pdl_trigger();
@@ -1065,10 +1106,21 @@ cudaError_t reserve_workspace(cudaStream_t stream, size_t floats) {
 }
 
 cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand& A,
-                        const Operand& B, const Epilogue& epi, int b_pair_off, int k_splits,
+                        const Operand& B, const Epilogue& epi_in, int b_pair_off, int k_splits,
                         unsigned* err_word, int precision) {
   if (M <= 0 || N <= 0) return cudaSuccess;
   g_reason = "";
+  // paired-column epilogues: the GEMM itself stores (into the workspace
+  // planes or C), the pair rule runs where the result is read back
+  const bool pair = epi_in.kind == EPI_PAIR_SILU || epi_in.kind == EPI_PAIR_GRU;
+  if (pair && (N != 2 * epi_in.ldf || epi_in.ldf % 4 || b_pair_off || epi_in.C == nullptr))
+    return reject("paired epilogue: N must be 2 * ldf (ldf % 4 == 0) with C as scratch");
+  Epilogue epi = epi_in;
+  if (pair) {
+    epi.kind = EPI_STORE;
+    epi.ldc = N;
+    epi.alpha = 1.0f;
+  }
   if (K <= 0 || A.p == nullptr || B.p == nullptr) return reject("K <= 0 or null operand");
   if (A.bf16 != B.bf16) return reject("one bf16 and one fp32 operand");
   const bool st16 = A.bf16;  // bf16 storage: MODE 2
@@ -1258,7 +1310,19 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
       e = BN == 128 ? launch<128, 16, 1, 0>(stream, ta, tb, tc, kp)
                     : launch<256, 16, 1, 0>(stream, ta, tb, tc, kp);
   }
-  if (e != cudaSuccess || kp.split_stride == 0) return e;
+  if (e != cudaSuccess) return e;
+  if (pair) {
+    // fixed-order sum of the partials (or the stored C) + the pair rule
+    const float* src = kp.split_stride ? kp.epi.C : epi.C;
+    const int S = kp.split_stride ? kp.k_splits : 1;
+    const size_t work = (size_t)M * (N / 2) / 4;
+    size_t grid = (work + 255) / 256;
+    if (grid > (size_t)num_sms() * 8) grid = (size_t)num_sms() * 8;
+    if (grid < 1) grid = 1;
+    splitk_pair_kernel<<<(unsigned)grid, 256, 0, stream>>>(src, S, M, N / 2, epi_in);
+    return rnet_k::launched();
+  }
+  if (kp.split_stride == 0) return e;
   // fixed-order sum of the partials + the caller's epilogue
   const size_t work = (N % 4 == 0) ? (size_t)M * N / 4 : (size_t)M * N;
   size_t grid = (work + 255) / 256;

@@ -125,7 +125,9 @@ cudaError_t swiglu_bwd_pointwise(float* dgu, int ld, const float* G, const float
 cudaError_t silu_mul_rows(const float* gu, float* h, int M, int F, cudaStream_t s);
 // Top-2 slots of each score row ([M, S]) by the reference's sequential rule,
 // softmax weights over the pair; same results as the GEMM's top-2 epilogue.
-cudaError_t topk2_rows(const float* scores, int* idx, float* w, int M, int S, cudaStream_t s);
+// VT / r (optional): also gather r = sum_j w_j VT[idx_j] (as slot_gather).
+cudaError_t topk2_rows(const float* scores, int* idx, float* w, int M, int S, cudaStream_t s,
+                       const float* VT = nullptr, float* r = nullptr, int D = 0);
 // ring: [M][14][D] last conv inputs indexed by position mod 14; *pos = index
 // of the current token (device scalar, advanced by argmax_rows).
 cudaError_t decode_conv(const float* n, float* ring, const int* pos, const float* w3,
