@@ -252,24 +252,21 @@ __device__ __forceinline__ void top2_merge(float& a1, float& a2, float b1, float
   a2 = m2;
 }
 
-// VT / r (optional): the warp also gathers r[row] = w0 VT[i0] + w1 VT[i1]
-// (the slot_gather of the selected pair, same arithmetic), saving a launch.
-__global__ void topk2_rows_kernel(const float* __restrict__ scores, int* __restrict__ idx,
-                                  float* __restrict__ w, int M, int S,
-                                  const float* __restrict__ VT, float* __restrict__ r, int D) {
-  rnet_dev::pdl_trigger();
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= M) return;
-  const float* sr = scores + (size_t)row * S;
+// The scan itself, for one warp: ld(s) gives the score of slot s. Leaves the
+// held pair (values h0, h1 at positions i0, i1) uniform across the warp.
+template <class Load>
+__device__ __forceinline__ void top2_scan_warp(Load ld, int S, int lane, float& h0, float& h1,
+                                               int& i0, int& i1) {
   const float NEG = -1e30f;  // the reference's initial held value
-  float h0 = NEG, h1 = NEG;  // held pair (positions 0, 1), uniform across the warp
-  int i0 = 0, i1 = 0;
+  h0 = NEG;
+  h1 = NEG;
+  i0 = 0;
+  i1 = 0;
   for (int base = 0; base < S; base += 32 * 32) {
     const int s0 = base + lane * 32;
     float v[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = s0 + j < S ? sr[s0 + j] : NEG;
+    for (int j = 0; j < 32; ++j) v[j] = s0 + j < S ? ld(s0 + j) : NEG;
     // chunk top-2 (values)
     float c1 = NEG, c2 = NEG;
 #pragma unroll
@@ -318,6 +315,21 @@ __global__ void topk2_rows_kernel(const float* __restrict__ scores, int* __restr
       i1 = __shfl_sync(0xffffffffu, i1, src);
     }
   }
+}
+
+// VT / r (optional): the warp also gathers r[row] = w0 VT[i0] + w1 VT[i1]
+// (the slot_gather of the selected pair, same arithmetic), saving a launch.
+__global__ void topk2_rows_kernel(const float* __restrict__ scores, int* __restrict__ idx,
+                                  float* __restrict__ w, int M, int S,
+                                  const float* __restrict__ VT, float* __restrict__ r, int D) {
+  rnet_dev::pdl_trigger();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float* sr = scores + (size_t)row * S;
+  float h0, h1;
+  int i0, i1;
+  top2_scan_warp([&](int j) { return sr[j]; }, S, lane, h0, h1, i0, i1);
   const float mx = fmaxf(h0, h1);
   const float e0 = __expf(h0 - mx), e1 = __expf(h1 - mx);
   const float sum = e0 + e1;
@@ -342,6 +354,135 @@ __global__ void topk2_rows_kernel(const float* __restrict__ scores, int* __restr
   }
 }
 
+// The decode step's slot sublayer after the score GEMM, one 256-thread CTA
+// per row:
+//  1. all threads sum the score GEMM's partial planes in plane order (the
+//     split-K sum's order, so the same values), float4-coalesced, into shared
+//     memory padded by one word per 32 (slot s at s + s / 32, so the scan's
+//     lane-strided reads are free of bank conflicts);
+//  2. warp 0 runs the sequential top-2 scan and the pair softmax;
+//  3. all threads add w0 VP[i0] + w1 VP[i1] (VP = V * proj_out^T, the slot
+//     sublayer's output) into the residual row, then write its RMSNorm.
+constexpr int SLOT_ROW_THREADS = 256;
+
+__global__ void __launch_bounds__(SLOT_ROW_THREADS)
+    slot_row_kernel(const float* __restrict__ planes, int n_planes, int* __restrict__ idx,
+                    float* __restrict__ w, int M, int S, const float* __restrict__ VP,
+                    float* __restrict__ x, int D, const float* __restrict__ nw,
+                    float* __restrict__ ny, float eps) {
+  rnet_dev::pdl_trigger();
+  extern __shared__ float sc[];  // S + S / 32 floats
+  __shared__ float red[SLOT_ROW_THREADS / 32];
+  __shared__ float pick_w[2];
+  __shared__ int pick_i[2];
+  const size_t row = blockIdx.x;
+  const size_t plane = (size_t)M * S;
+  const float* src = planes + row * S;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int q = tid; q < (S >> 2); q += SLOT_ROW_THREADS) {
+    float4 a = *reinterpret_cast<const float4*>(src + 4 * q);
+    for (int k0 = 1; k0 < n_planes; k0 += 8) {
+      float4 b[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (k0 + j < n_planes) b[j] = *reinterpret_cast<const float4*>(src + (k0 + j) * plane + 4 * q);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (k0 + j < n_planes) { a.x += b[j].x; a.y += b[j].y; a.z += b[j].z; a.w += b[j].w; }
+    }
+    const int s0 = 4 * q, p = s0 + (s0 >> 5);  // the 4 slots share one 32-slot group
+    sc[p] = a.x;
+    sc[p + 1] = a.y;
+    sc[p + 2] = a.z;
+    sc[p + 3] = a.w;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float h0, h1;
+    int i0, i1;
+    top2_scan_warp([&](int j) { return sc[j + (j >> 5)]; }, S, lane, h0, h1, i0, i1);
+    const float mx = fmaxf(h0, h1);
+    const float e0 = __expf(h0 - mx), e1 = __expf(h1 - mx);
+    const float sum = e0 + e1;
+    if (lane == 0) {
+      const float w0 = e0 / sum, w1 = e1 / sum;
+      pick_w[0] = w0;
+      pick_w[1] = w1;
+      pick_i[0] = i0;
+      pick_i[1] = i1;
+      idx[2 * row] = i0;
+      idx[2 * row + 1] = i1;
+      w[2 * row] = w0;
+      w[2 * row + 1] = w1;
+    }
+  }
+  __syncthreads();
+  const int id[2] = {pick_i[0], pick_i[1]};
+  const float ww[2] = {pick_w[0], pick_w[1]};
+  float* xr = x + row * D;
+  float ss = 0.f;
+  for (int c = tid * 4; c < D; c += SLOT_ROW_THREADS * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < 2; ++j) {
+      const float4 v = *reinterpret_cast<const float4*>(VP + (size_t)id[j] * D + c);
+      acc.x += ww[j] * v.x; acc.y += ww[j] * v.y; acc.z += ww[j] * v.z; acc.w += ww[j] * v.w;
+    }
+    float4 xv = *reinterpret_cast<const float4*>(xr + c);
+    xv.x += acc.x; xv.y += acc.y; xv.z += acc.z; xv.w += acc.w;
+    *reinterpret_cast<float4*>(xr + c) = xv;
+    ss += xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w;
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int k = 0; k < SLOT_ROW_THREADS / 32; ++k) t += red[k];
+  const float ri = rsqrtf(t / (float)D + eps);
+  float* yr = ny + row * D;
+  for (int c = tid * 4; c < D; c += SLOT_ROW_THREADS * 4) {
+    const float4 xv = *reinterpret_cast<const float4*>(xr + c);
+    const float4 g = *reinterpret_cast<const float4*>(nw + c);
+    *reinterpret_cast<float4*>(yr + c) =
+        make_float4(xv.x * ri * g.x, xv.y * ri * g.y, xv.z * ri * g.z, xv.w * ri * g.w);
+  }
+}
+
+// out[s, j] = sum_d A[s, d] * B[d * bd + j * bj] over d < K, accumulated in
+// double (A: [R, K] rows, out: [R, J] rows). 32 x 32 output tiles, 256
+// threads, 4 outputs per thread; K staged 32 at a time through shared memory.
+__global__ void __launch_bounds__(256) fold_kernel(const float* __restrict__ A,
+                                                   const float* __restrict__ B, size_t bd,
+                                                   size_t bj, float* __restrict__ out, int R,
+                                                   int J, int K) {
+  __shared__ float As[32][33];
+  __shared__ float Bs[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // ty: 0..7
+  const int r0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  for (int k0 = 0; k0 < K; k0 += 32) {
+    for (int i = ty; i < 32; i += 8) {
+      const int rr = r0 + i, kk = k0 + tx;
+      As[i][tx] = (rr < R && kk < K) ? A[(size_t)rr * K + kk] : 0.f;
+      const int dd = k0 + i, jj = j0 + tx;
+      Bs[i][tx] = (dd < K && jj < J) ? B[dd * bd + jj * bj] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < 32; ++kk) {
+      const double b = (double)Bs[kk][tx];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] += (double)As[ty + 8 * q][kk] * b;
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int rr = r0 + ty + 8 * q, jj = j0 + tx;
+    if (rr < R && jj < J) out[(size_t)rr * J + jj] = (float)acc[q];
+  }
+}
+
 }  // namespace
 
 cudaError_t silu_mul_rows(const float* gu, float* h, int M, int F, cudaStream_t s) {
@@ -358,6 +499,33 @@ cudaError_t topk2_rows(const float* scores, int* idx, float* w, int M, int S, cu
   if (M <= 0) return cudaSuccess;
   if (r && (D % 4 || !VT)) return cudaErrorInvalidValue;
   topk2_rows_kernel<<<(M + 7) / 8, 256, 0, s>>>(scores, idx, w, M, S, VT, r, D);
+  return launched();
+}
+
+cudaError_t topk2_gather_residual_norm(const float* planes, int n_planes, int* idx, float* w,
+                                       int M, int S, const float* VP, float* x, int D,
+                                       const float* nw, float* ny, float eps, cudaStream_t s) {
+  if (M <= 0) return cudaSuccess;
+  if (D % 4 || S % 4 || !VP || !x || !nw || !ny || n_planes < 1) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)(S + S / 32 + 1) * sizeof(float);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  static int smem_set = 0;  // opt in above 48 KB once (largest size asked so far)
+  if ((int)smem > 48 * 1024 && (int)smem > smem_set) {
+    cudaError_t e = cudaFuncSetAttribute(slot_row_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    smem_set = (int)smem;
+  }
+  slot_row_kernel<<<M, SLOT_ROW_THREADS, smem, s>>>(planes, n_planes, idx, w, M, S, VP, x, D, nw,
+                                                    ny, eps);
+  return launched();
+}
+
+cudaError_t fold_rows(const float* A, const float* B, size_t bd, size_t bj, float* out, int R,
+                      int J, int K, cudaStream_t s) {
+  if (R <= 0 || J <= 0) return cudaSuccess;
+  dim3 grid((J + 31) / 32, (R + 31) / 32);
+  fold_kernel<<<grid, 256, 0, s>>>(A, B, bd, bj, out, R, J, K);
   return launched();
 }
 

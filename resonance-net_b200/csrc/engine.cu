@@ -741,6 +741,8 @@ int Engine::decoder_init(Decoder* d, int M) {
   const size_t D = cfg_.d_model, F = cfg_.d_ff, V = cfg_.vocab_size, L = cfg_.n_layers;
   const size_t k = cfg_.slot_top_k, m = M;
   if (k != 2) return rnet_status::fail(RNET_ERR_UNSUPPORTED, "decoder: slot_top_k must be 2");
+  if (cfg_.n_slots % 4 || D % 4)
+    return rnet_status::fail(RNET_ERR_UNSUPPORTED, "decoder: n_slots and d_model must be % 4");
   d->M = M;
   d->floats_per_layer = m * 15 * D;
   std::vector<std::pair<void**, size_t>> plan;
@@ -750,6 +752,8 @@ int Engine::decoder_init(Decoder* d, int M) {
   f(&d->r, m * D); f(&d->G, m * F); f(&d->U, m * F); f(&d->H, m * F); f(&d->logits, m * V);
   f(&d->GU, m * 2 * F); f(&d->scores, m * (size_t)cfg_.n_slots);
   f(&d->w, m * k);
+  f(&d->KqT, L * cfg_.n_slots * D);
+  f(&d->VP, L * cfg_.n_slots * D);
   plan.push_back({(void**)&d->idx, m * k * sizeof(int)});
   plan.push_back({(void**)&d->tok, m * sizeof(int)});
   plan.push_back({(void**)&d->pos, sizeof(int)});
@@ -798,6 +802,14 @@ int Engine::prefill(Decoder* d, const int* d_tokens, int T) {
                                     s));
   }
   have_cache_ = false;
+  // fold the slot path's fixed projections for the decode steps:
+  // KqT[s, e] = sum_d KT[s, d] proj_q[d, e], VP[s, j] = sum_d VT[s, d] proj_out[j, d]
+  const int S = cfg_.n_slots;
+  for (int l = 0; l < cfg_.n_layers; ++l) {
+    const size_t o = (size_t)l * S * D;
+    CK(rnet_k::fold_rows(KT_ + o, W_[l].pq, (size_t)D, 1, d->KqT + o, S, D, D, s));
+    CK(rnet_k::fold_rows(VT_ + o, W_[l].pout, 1, (size_t)D, d->VP + o, S, D, D, s));
+  }
   const float* XL = X_ + (size_t)(cfg_.n_layers & 1) * ND;
   CK(rnet_k::last_rows(XL, d->x, M, T, D, s));
   CK(rnet_k::rms_norm_fwd(d->x, fnorm_, d->n, nullptr, M, D, cfg_.rms_eps, s));
@@ -811,22 +823,32 @@ int Engine::prefill(Decoder* d, const int* d_tokens, int T) {
 
 int Engine::decode_step(Decoder* d, const int* d_tokens) {
   const int M = d->M, D = cfg_.d_model, F = cfg_.d_ff, S = cfg_.n_slots, V = cfg_.vocab_size;
+  const int L = cfg_.n_layers;
   const float eps = cfg_.rms_eps;
   cudaStream_t s = stream_;
   unsigned* err = rnet_status::device_error_word();
   if (d_tokens) CK(cudaMemcpyAsync(d->tok, d_tokens, M * sizeof(int), cudaMemcpyDeviceToDevice, s));
   CK(rnet_k::embed_fwd(d->tok, embed_, d->x, M, V, D, err, s));
-  for (int l = 0; l < cfg_.n_layers; ++l) {
+  CK(rnet_k::rms_norm_fwd(d->x, W_[0].n1, d->n, nullptr, M, D, eps, s));
+  // Every residual update also writes the next sublayer's RMSNorm of x into
+  // d->n (in the kernel that sums the split-K partials), so no norm has a
+  // launch of its own after the first.
+  auto with_norm = [&](Epilogue e, const float* nw) {
+    e.nw = nw;
+    e.ny = d->n;
+    e.eps = eps;
+    return e;
+  };
+  for (int l = 0; l < L; ++l) {
     const LayerParams& w = W_[l];
     float* ring = d->state + (size_t)l * d->floats_per_layer;
     float* h = ring + (size_t)M * 14 * D;
-    CK(rnet_k::rms_norm_fwd(d->x, w.n1, d->n, nullptr, M, D, eps, s));
+    const size_t so = (size_t)l * S * D;
     CK(rnet_k::decode_conv(d->n, ring, d->pos, w.c3, w.c7, w.c15, d->S, M, D, s));
-    MM_RES(M, D, D, kmaj(d->S, D), kmaj(w.mix, D), d->x);
-    CK(rnet_k::rms_norm_fwd(d->x, w.n2, d->n, nullptr, M, D, eps, s));
+    MMS(M, D, D, kmaj(d->S, D), kmaj(w.mix, D), with_norm(epi_accum(d->x, D), w.n2), 0, 1);
     {
-      // gate pre-activations -> GRU state update + residual where the
-      // split-K partials are summed (one launch fewer)
+      // gate pre-activations -> GRU state update + residual (+ norm 3) where
+      // the split-K partials are summed
       Epilogue e;
       e.kind = EPI_PAIR_GRU;
       e.C = d->P;
@@ -835,17 +857,20 @@ int Engine::decode_step(Decoder* d, const int* d_tokens) {
       e.b1 = w.bh;
       e.state = h;
       e.xres = d->x;
-      MM(M, 2 * D, D, kmaj(d->n, D), kmaj(w.Wz, D), e, 0);
+      MM(M, 2 * D, D, kmaj(d->n, D), kmaj(w.Wz, D), with_norm(e, w.n3), 0);
     }
-    CK(rnet_k::rms_norm_fwd(d->x, w.n3, d->n, nullptr, M, D, eps, s));
-    MM(M, D, D, kmaj(d->n, D), kmaj(w.pq, D), epi_store(d->q, D), 0);
-    // short M: scores through the split-K GEMM, then a warp-per-row top-2
-    // (the row-owner top-2 epilogue would run on M / 128 CTAs)
-    MM(M, S, D, kmaj(d->q, D), kmaj(KT_ + (size_t)l * S * D, D), epi_store(d->scores, S), 0);
-    // top-2 + softmax + value gather in one warp-per-row launch
-    CK(rnet_k::topk2_rows(d->scores, d->idx, d->w, M, S, s, VT_ + (size_t)l * S * D, d->r, D));
-    MM_RES(M, D, D, kmaj(d->r, D), kmaj(w.pout, D), d->x);
-    CK(rnet_k::rms_norm_fwd(d->x, w.n4, d->n, nullptr, M, D, eps, s));
+    {
+      // scores = n . (K proj_q)^T: the partial planes go straight to the
+      // top-2 kernel, which also gathers the folded values into x (+ norm 4)
+      int planes = 1;
+      const float* pl = nullptr;
+      Epilogue e = epi_store(d->scores, S);
+      e.splits_out = &planes;
+      e.planes_out = &pl;
+      MM(M, S, D, kmaj(d->n, D), kmaj(d->KqT + so, D), e, 0);
+      CK(rnet_k::topk2_gather_residual_norm(pl, planes, d->idx, d->w, M, S, d->VP + so, d->x, D,
+                                            w.n4, d->n, eps, s));
+    }
     // gate|up as one [2F, D] operand (adjacent in the parameter buffer)
     {
       Epilogue e;  // gate|up -> silu(gate) * up where the partials are summed
@@ -855,9 +880,9 @@ int Engine::decode_step(Decoder* d, const int* d_tokens) {
       e.ldf = F;
       MM(M, 2 * F, D, kmaj(d->n, D), kmaj(w.gate, D), e, 0);
     }
-    MM_RES(M, D, F, kmaj(d->H, F), kmaj(w.down, F), d->x);
+    const float* next_w = l + 1 < L ? W_[l + 1].n1 : fnorm_;
+    MMS(M, D, F, kmaj(d->H, F), kmaj(w.down, F), with_norm(epi_accum(d->x, D), next_w), 0, 1);
   }
-  CK(rnet_k::rms_norm_fwd(d->x, fnorm_, d->n, nullptr, M, D, eps, s));
   MM(M, V, D, kmaj(d->n, D), kmaj(outw_, D), epi_store(d->logits, V), 0);
   CK(rnet_k::sample_rows(d->logits, M, V, d->temperature, d->top_p, d->seed, d->tok, d->pos, 1,
                          s));

@@ -75,6 +75,10 @@ struct Decoder {
   size_t floats_per_layer = 0;
   float *x, *n, *S, *P, *q, *r, *G, *U, *H, *logits;
   float *GU, *scores;  // [M, 2F] gate|up pre-activations, [M, S] slot scores
+  // per layer [S, D]: keys folded with proj_q (scores = n . KqT[s]) and
+  // values folded with proj_out (slot output = sum_j w_j VP[i_j]), made at
+  // prefill from the weights of that moment
+  float *KqT, *VP;
   int* idx;
   float* w;
   int* tok;  // current / next token per stream

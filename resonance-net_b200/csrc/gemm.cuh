@@ -69,6 +69,19 @@ struct Epilogue {
   const float* b1 = nullptr;
   float* state = nullptr;
   float* xres = nullptr;
+  // RMSNorm of the finished rows (EPI_ACCUM / EPI_RESID / EPI_STORE, and
+  // EPI_PAIR_GRU on its residual stream): ny = x * rsqrt(mean(x^2) + eps) * nw,
+  // written by the kernel that sums the split-K partials (one CTA per row),
+  // so the next sublayer's normalisation costs no launch of its own
+  const float* nw = nullptr;
+  float* ny = nullptr;
+  float eps = 0.0f;
+  // EPI_STORE only: leave the split-K partial planes unsummed for the
+  // caller's own kernel. On return *planes_out holds the first plane
+  // ([M, ldc] each, M * N floats apart, summed in index order) and
+  // *splits_out their count; 1 means C itself holds the result.
+  int* splits_out = nullptr;
+  const float** planes_out = nullptr;
 };
 
 // Launch. Both operands fp32 (3xTF32 or bf16-rounded per `precision`) or

@@ -1068,6 +1068,108 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Row-owner forms of the two sums above, for epilogues that also normalise
+// the finished rows (Epilogue::ny): one CTA per row, threads owning columns
+// c = 4 * tid + 4 * blockDim.x * j. Pass 1 sums in split order, applies the
+// epilogue, stores the row and accumulates its sum of squares; pass 2
+// re-reads the thread's own stores and writes y = x * rsqrt(ms + eps) * w
+// (the RMSNorm forward's formula). S = 0: the GEMM stored the row already.
+__device__ __forceinline__ float block_sum_128(float v, float* red) {
+  v = rnet_dev::warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  const float t = red[0] + red[1] + red[2] + red[3];
+  return t;
+}
+
+__device__ __forceinline__ void norm_row_pass(const float* x, const float* w, float* y, int n,
+                                              float ri) {
+  for (int c = threadIdx.x * 4; c < n; c += blockDim.x * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(x + c);
+    const float4 g = *reinterpret_cast<const float4*>(w + c);
+    *reinterpret_cast<float4*>(y + c) =
+        make_float4(v.x * ri * g.x, v.y * ri * g.y, v.z * ri * g.z, v.w * ri * g.w);
+  }
+}
+
+constexpr int NORM_THREADS = 128;
+
+__global__ void __launch_bounds__(NORM_THREADS)
+    splitk_reduce_norm_kernel(const float* __restrict__ ws, int S, int M, int N, Epilogue e) {
+  rnet_dev::pdl_trigger();
+  __shared__ float red[NORM_THREADS / 32];
+  const size_t r = blockIdx.x;
+  const size_t plane = (size_t)M * N;
+  float* dst = e.C + r * e.ldc;
+  float ss = 0.f;
+  for (int c = threadIdx.x * 4; c < N; c += blockDim.x * 4) {
+    float4 o;
+    if (S > 0) {
+      const float* src = ws + r * N + c;
+      float4 a = *reinterpret_cast<const float4*>(src);
+      for (int k0 = 1; k0 < S; k0 += 8) {
+        float4 b[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (k0 + j < S) b[j] = *reinterpret_cast<const float4*>(src + (k0 + j) * plane);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (k0 + j < S) { a.x += b[j].x; a.y += b[j].y; a.z += b[j].z; a.w += b[j].w; }
+      }
+      const float al = e.alpha;
+      o = make_float4(al * a.x, al * a.y, al * a.z, al * a.w);
+      if (e.kind == EPI_ACCUM || e.kind == EPI_RESID) {
+        const float* base = e.kind == EPI_ACCUM ? dst + c : e.R + r * e.ldr + c;
+        o.x += base[0]; o.y += base[1]; o.z += base[2]; o.w += base[3];
+      }
+      *reinterpret_cast<float4*>(dst + c) = o;
+    } else {
+      o = *reinterpret_cast<const float4*>(dst + c);
+    }
+    ss += o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
+  }
+  ss = block_sum_128(ss, red);
+  const float ri = rsqrtf(ss / (float)N + e.eps);
+  norm_row_pass(dst, e.nw, e.ny + r * e.ldc, N, ri);
+}
+
+// EPI_PAIR_GRU with the norm: the same update as splitk_pair_kernel, then the
+// RMSNorm of the updated residual row.
+__global__ void __launch_bounds__(NORM_THREADS)
+    splitk_pair_gru_norm_kernel(const float* __restrict__ ws, int S, int M, int h, Epilogue e) {
+  rnet_dev::pdl_trigger();
+  __shared__ float red[NORM_THREADS / 32];
+  const size_t r = blockIdx.x;
+  const size_t plane = (size_t)M * 2 * h;
+  float ss = 0.f;
+  for (int c = threadIdx.x * 4; c < h; c += blockDim.x * 4) {
+    const float* src = ws + r * 2 * h + c;
+    float4 a = *reinterpret_cast<const float4*>(src);
+    float4 b = *reinterpret_cast<const float4*>(src + h);
+    for (int k = 1; k < S; ++k) {
+      const float4 pa = *reinterpret_cast<const float4*>(src + k * plane);
+      const float4 pb = *reinterpret_cast<const float4*>(src + k * plane + h);
+      a.x += pa.x; a.y += pa.y; a.z += pa.z; a.w += pa.w;
+      b.x += pb.x; b.y += pb.y; b.z += pb.z; b.w += pb.w;
+    }
+    const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+    const size_t o = r * e.ldf + c;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float z = 1.0f / (1.0f + __expf(-(av[j] + e.b0[c + j])));
+      const float ht = bv[j] + e.b1[c + j];
+      const float hn = (1.f - z) * e.state[o + j] + z * ht;
+      e.state[o + j] = hn;
+      const float xn = e.xres[o + j] + hn;
+      e.xres[o + j] = xn;
+      ss += xn * xn;
+    }
+  }
+  ss = block_sum_128(ss, red);
+  const float ri = rsqrtf(ss / (float)h + e.eps);
+  norm_row_pass(e.xres + r * e.ldf, e.nw, e.ny + r * e.ldf, h, ri);
+}
+
 struct Workspace {
   float* p = nullptr;
   size_t floats = 0;
@@ -1115,7 +1217,23 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   const bool pair = epi_in.kind == EPI_PAIR_SILU || epi_in.kind == EPI_PAIR_GRU;
   if (pair && (N != 2 * epi_in.ldf || epi_in.ldf % 4 || b_pair_off || epi_in.C == nullptr))
     return reject("paired epilogue: N must be 2 * ldf (ldf % 4 == 0) with C as scratch");
+  const bool norm = epi_in.ny != nullptr;
+  if (norm) {
+    const bool ok_kind = epi_in.kind == EPI_PAIR_GRU || epi_in.kind == EPI_STORE ||
+                         epi_in.kind == EPI_ACCUM || epi_in.kind == EPI_RESID;
+    const int width = pair ? epi_in.ldf : N;
+    const int pitch = pair ? epi_in.ldf : epi_in.ldc;
+    if (!ok_kind || !epi_in.nw || width % 4 || pitch % 4 || epi_in.C16 || b_pair_off ||
+        epi_in.splits_out)
+      return reject("row norm: store / residual / GRU-pair epilogue, width % 4 == 0, weights");
+  }
+  if (epi_in.splits_out && (epi_in.kind != EPI_STORE || !epi_in.planes_out ||
+                            epi_in.ldc != N || epi_in.C16 || b_pair_off))
+    return reject("deferred split-K sum: EPI_STORE with ldc == N and both outputs");
   Epilogue epi = epi_in;
+  epi.ny = nullptr;  // the GEMM kernel itself never normalises
+  epi.splits_out = nullptr;
+  epi.planes_out = nullptr;
   if (pair) {
     epi.kind = EPI_STORE;
     epi.ldc = N;
@@ -1143,7 +1261,11 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
     const int kb = (K + BK - 1) / BK;
     int sp = num_sms() / tiles;
     if (sp > kb / 2) sp = kb / 2;  // >= 2 k-blocks per split
-    if (sp > 32) sp = 32;
+    static const int sp_max = [] {
+      const char* v = getenv("RNET_SPLITK_MAX");
+      return v && atoi(v) >= 2 ? atoi(v) : 32;
+    }();
+    if (sp > sp_max) sp = sp_max;
     if (sp >= 2) {
       const size_t need = (size_t)sp * M * N;
       Workspace* w = workspace_for(stream);
@@ -1319,7 +1441,24 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
     size_t grid = (work + 255) / 256;
     if (grid > (size_t)num_sms() * 8) grid = (size_t)num_sms() * 8;
     if (grid < 1) grid = 1;
-    splitk_pair_kernel<<<(unsigned)grid, 256, 0, stream>>>(src, S, M, N / 2, epi_in);
+    if (norm)
+      splitk_pair_gru_norm_kernel<<<(unsigned)M, NORM_THREADS, 0, stream>>>(src, S, M, N / 2,
+                                                                            epi_in);
+    else
+      splitk_pair_kernel<<<(unsigned)grid, 256, 0, stream>>>(src, S, M, N / 2, epi_in);
+    return rnet_k::launched();
+  }
+  if (epi_in.splits_out) {
+    // the caller's kernel sums the planes (or reads C when unsplit)
+    *epi_in.splits_out = kp.split_stride ? kp.k_splits : 1;
+    *epi_in.planes_out = kp.split_stride ? kp.epi.C : epi_in.C;
+    return e;
+  }
+  if (norm) {
+    // fixed-order sum (none when unsplit) + epilogue + RMSNorm, a CTA per row
+    const int S = kp.split_stride ? kp.k_splits : 0;
+    splitk_reduce_norm_kernel<<<(unsigned)M, NORM_THREADS, 0, stream>>>(kp.epi.C, S, M, N,
+                                                                        epi_in);
     return rnet_k::launched();
   }
   if (kp.split_stride == 0) return e;

@@ -128,6 +128,19 @@ cudaError_t silu_mul_rows(const float* gu, float* h, int M, int F, cudaStream_t 
 // VT / r (optional): also gather r = sum_j w_j VT[idx_j] (as slot_gather).
 cudaError_t topk2_rows(const float* scores, int* idx, float* w, int M, int S, cudaStream_t s,
                        const float* VT = nullptr, float* r = nullptr, int D = 0);
+// The decode step's slot sublayer after the score GEMM, in one launch:
+// top-2 over the scores (the sum of n_planes split-K partial planes [M, S],
+// M * S floats apart, in plane order; 1 = plain scores), then
+// x[row] += w0 VP[i0] + w1 VP[i1] with VP = V * proj_out^T ([S, D], see
+// fold_rows) and ny[row] = RMSNorm(x[row]) * nw. S % 4 == 0, D % 4 == 0.
+cudaError_t topk2_gather_residual_norm(const float* planes, int n_planes, int* idx, float* w,
+                                       int M, int S, const float* VP, float* x, int D,
+                                       const float* nw, float* ny, float eps, cudaStream_t s);
+// out[R, J] = A[R, K] * B, B(d, j) = B[d * bd + j * bj], accumulated in double:
+// folds two fixed projections into one matrix (decode: keys with proj_q,
+// values with proj_out).
+cudaError_t fold_rows(const float* A, const float* B, size_t bd, size_t bj, float* out, int R,
+                      int J, int K, cudaStream_t s);
 // ring: [M][14][D] last conv inputs indexed by position mod 14; *pos = index
 // of the current token (device scalar, advanced by argmax_rows).
 cudaError_t decode_conv(const float* n, float* ring, const int* pos, const float* w3,
