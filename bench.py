@@ -727,8 +727,11 @@ def decode_measure(rnet, rdata, torch, pg, rank, world, local, streams, T, G, wa
     n0 = rnet.kernel_launches()
     clocks = ClockSampler(local) if rank == 0 else ClockSampler(None)
     clocks.start()
-    clocks.mark(True)
     ms_prefill = timed(lambda: dec.prefill(d_tok, T), reps)
+    # untimed decode steps first: the power cap's running average (and the
+    # clocks it sets) then reflect the decode steps, not the prefill before
+    dec.generate(G, d_out, True)
+    clocks.mark(True)  # the clocks reported are the decode steps' own
     ms_decode = timed(lambda: dec.generate(G, d_out, True), 1)
     clocks.mark(False)
     ck = clocks.stop()

@@ -41,8 +41,10 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // preceding kernel drains, then block in pdl_wait() until that kernel has
 // completed and its memory is visible. Only GEMMs are launched that way: they
 // read their operands through TMA (L2) and their engine epilogues only store.
-// Every kernel calls pdl_trigger() on entry so a following GEMM may launch
-// once all of its CTAs have started. Both are no-ops without the attribute.
+// (Chaining the small kernels as well measured slower: their early CTAs
+// crowd the persistent GEMM grid.) Every kernel calls pdl_trigger() on entry
+// so a following GEMM may launch once all of its CTAs have started. Both are
+// no-ops without the attribute.
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }

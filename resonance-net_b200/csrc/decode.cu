@@ -6,6 +6,7 @@
 // single-token step exact is, per layer and stream: the last 14 inputs of the
 // causal convolutions (a ring indexed by position mod 14) and the MinGRU h.
 #include "common.cuh"
+#include "conv_step.cuh"
 #include "kernels.cuh"
 
 namespace rnet_k {
@@ -13,41 +14,24 @@ using namespace rnet_dev;
 
 namespace {
 
-constexpr int RING = 14;
+constexpr int RING = rnet_dev::CONV_RING;
 
 // S = c3 + c7 + c15 of the current input row n[m] and the ring of the 14
-// previous rows; then the current row is written into the ring at pos % 14.
-// Positions before the start of the sequence contribute zero (the ring is
-// zero-initialised / filled by prefill).
+// previous rows (conv_step4); then the current row is written into the ring
+// at pos % 14. Positions before the start of the sequence contribute zero
+// (the ring is zero-initialised / filled by prefill). A thread per 4 channels.
 __global__ void decode_conv_kernel(const float* __restrict__ n, float* __restrict__ ring,
                                    const int* __restrict__ pos_ptr, const float* __restrict__ w3,
                                    const float* __restrict__ w7, const float* __restrict__ w15,
                                    float* __restrict__ S, int M, int D) {
   rnet_dev::pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= M * D) return;
-  const int m = i / D, d = i % D;
-  const int pos = *pos_ptr;
-  float* rg = ring + (size_t)m * RING * D + d;
-  // win[o] = x[pos - o], o = 0..14
-  float win[RING + 1];
-  win[0] = n[i];
-#pragma unroll
-  for (int o = 1; o <= RING; ++o) {
-    const int t = pos - o;
-    win[o] = t >= 0 ? rg[(size_t)(t % RING) * D] : 0.f;
-  }
-  // same per-scale order as the training kernel: sum over taps k ascending,
-  // tap k reads x[t - (K-1) + k] = win[K-1-k]
-  float s3 = 0.f, s7 = 0.f, s15 = 0.f;
-#pragma unroll
-  for (int k = 0; k < 3; ++k) s3 += win[2 - k] * w3[k * D + d];
-#pragma unroll
-  for (int k = 0; k < 7; ++k) s7 += win[6 - k] * w7[k * D + d];
-#pragma unroll
-  for (int k = 0; k < 15; ++k) s15 += win[14 - k] * w15[k * D + d];
-  S[i] = s3 + s7 + s15;
-  rg[(size_t)(pos % RING) * D] = win[0];
+  const int D4 = D >> 2;
+  if (i >= M * D4) return;
+  const int m = i / D4, d = (i % D4) * 4;
+  const float4 x = *reinterpret_cast<const float4*>(n + (size_t)m * D + d);
+  *reinterpret_cast<float4*>(S + (size_t)m * D + d) =
+      rnet_dev::conv_step4(x, ring + (size_t)m * RING * D, *pos_ptr, w3, w7, w15, d, D);
 }
 
 // h = (1 - z) h + z h~, z = sigmoid(pz + bz), h~ = ph + bh; x += h.
@@ -385,7 +369,8 @@ __global__ void __launch_bounds__(SLOT_ROW_THREADS)
       float4 b[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (k0 + j < n_planes) b[j] = *reinterpret_cast<const float4*>(src + (k0 + j) * plane + 4 * q);
+        if (k0 + j < n_planes)
+          b[j] = *reinterpret_cast<const float4*>(src + (k0 + j) * plane + 4 * q);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         if (k0 + j < n_planes) { a.x += b[j].x; a.y += b[j].y; a.z += b[j].z; a.w += b[j].w; }
@@ -516,8 +501,8 @@ cudaError_t topk2_gather_residual_norm(const float* planes, int n_planes, int* i
     if (e != cudaSuccess) return e;
     smem_set = (int)smem;
   }
-  slot_row_kernel<<<M, SLOT_ROW_THREADS, smem, s>>>(planes, n_planes, idx, w, M, S, VP, x, D, nw,
-                                                    ny, eps);
+  slot_row_kernel<<<M, SLOT_ROW_THREADS, smem, s>>>(planes, n_planes, idx, w, M, S, VP, x, D,
+                                                    nw, ny, eps);
   return launched();
 }
 
@@ -532,7 +517,8 @@ cudaError_t fold_rows(const float* A, const float* B, size_t bd, size_t bj, floa
 cudaError_t decode_conv(const float* n, float* ring, const int* pos, const float* w3,
                         const float* w7, const float* w15, float* S, int M, int D,
                         cudaStream_t s) {
-  decode_conv_kernel<<<(M * D + 255) / 256, 256, 0, s>>>(n, ring, pos, w3, w7, w15, S, M, D);
+  if (D % 4) return cudaErrorInvalidValue;
+  decode_conv_kernel<<<(M * D / 4 + 255) / 256, 256, 0, s>>>(n, ring, pos, w3, w7, w15, S, M, D);
   return launched();
 }
 

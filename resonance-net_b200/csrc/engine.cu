@@ -844,7 +844,9 @@ int Engine::decode_step(Decoder* d, const int* d_tokens) {
     float* ring = d->state + (size_t)l * d->floats_per_layer;
     float* h = ring + (size_t)M * 14 * D;
     const size_t so = (size_t)l * S * D;
-    CK(rnet_k::decode_conv(d->n, ring, d->pos, w.c3, w.c7, w.c15, d->S, M, D, s));
+    // layer 0's conv step here; later layers' ran where the previous layer's
+    // down projection was summed (below)
+    if (l == 0) CK(rnet_k::decode_conv(d->n, ring, d->pos, w.c3, w.c7, w.c15, d->S, M, D, s));
     MMS(M, D, D, kmaj(d->S, D), kmaj(w.mix, D), with_norm(epi_accum(d->x, D), w.n2), 0, 1);
     {
       // gate pre-activations -> GRU state update + residual (+ norm 3) where
@@ -880,8 +882,21 @@ int Engine::decode_step(Decoder* d, const int* d_tokens) {
       e.ldf = F;
       MM(M, 2 * F, D, kmaj(d->n, D), kmaj(w.gate, D), e, 0);
     }
-    const float* next_w = l + 1 < L ? W_[l + 1].n1 : fnorm_;
-    MMS(M, D, F, kmaj(d->H, F), kmaj(w.down, F), with_norm(epi_accum(d->x, D), next_w), 0, 1);
+    if (l + 1 < L) {
+      // x += H down^T, n = RMSNorm_1(x) of the next layer, and that layer's
+      // conv step on n, all where the split-K partials are summed
+      const LayerParams& wn = W_[l + 1];
+      Epilogue e = with_norm(epi_accum(d->x, D), wn.n1);
+      e.cw3 = wn.c3;
+      e.cw7 = wn.c7;
+      e.cw15 = wn.c15;
+      e.ring = d->state + (size_t)(l + 1) * d->floats_per_layer;
+      e.pos = d->pos;
+      e.conv_out = d->S;
+      MMS(M, D, F, kmaj(d->H, F), kmaj(w.down, F), e, 0, 1);
+    } else {
+      MMS(M, D, F, kmaj(d->H, F), kmaj(w.down, F), with_norm(epi_accum(d->x, D), fnorm_), 0, 1);
+    }
   }
   MM(M, V, D, kmaj(d->n, D), kmaj(outw_, D), epi_store(d->logits, V), 0);
   CK(rnet_k::sample_rows(d->logits, M, V, d->temperature, d->top_p, d->seed, d->tok, d->pos, 1,

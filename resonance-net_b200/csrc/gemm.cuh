@@ -82,6 +82,15 @@ struct Epilogue {
   // *splits_out their count; 1 means C itself holds the result.
   int* splits_out = nullptr;
   const float** planes_out = nullptr;
+  // decode steps, with ny (EPI_ACCUM / EPI_RESID / EPI_STORE): the next
+  // sublayer's causal-conv step on the normalised row (conv_step.cuh),
+  // its output row into conv_out ([M, N]); ring: [M][14][N], pos: device scalar
+  const float* cw3 = nullptr;
+  const float* cw7 = nullptr;
+  const float* cw15 = nullptr;
+  float* ring = nullptr;
+  const int* pos = nullptr;
+  float* conv_out = nullptr;
 };
 
 // Launch. Both operands fp32 (3xTF32 or bf16-rounded per `precision`) or

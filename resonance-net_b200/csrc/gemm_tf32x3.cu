@@ -36,6 +36,7 @@
 #include <cuda_bf16.h>
 
 #include "common.cuh"
+#include "conv_step.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
 
@@ -1130,7 +1131,20 @@ __global__ void __launch_bounds__(NORM_THREADS)
   }
   ss = block_sum_128(ss, red);
   const float ri = rsqrtf(ss / (float)N + e.eps);
-  norm_row_pass(dst, e.nw, e.ny + r * e.ldc, N, ri);
+  if (!e.conv_out) {
+    norm_row_pass(dst, e.nw, e.ny + r * e.ldc, N, ri);
+    return;
+  }
+  const int pos = *e.pos;
+  float* ring_row = e.ring + r * rnet_dev::CONV_RING * N;
+  for (int c = threadIdx.x * 4; c < N; c += blockDim.x * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(dst + c);
+    const float4 g = *reinterpret_cast<const float4*>(e.nw + c);
+    const float4 y = make_float4(v.x * ri * g.x, v.y * ri * g.y, v.z * ri * g.z, v.w * ri * g.w);
+    *reinterpret_cast<float4*>(e.ny + r * e.ldc + c) = y;
+    *reinterpret_cast<float4*>(e.conv_out + r * N + c) =
+        rnet_dev::conv_step4(y, ring_row, pos, e.cw3, e.cw7, e.cw15, c, N);
+  }
 }
 
 // EPI_PAIR_GRU with the norm: the same update as splitk_pair_kernel, then the
@@ -1224,7 +1238,9 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
     const int width = pair ? epi_in.ldf : N;
     const int pitch = pair ? epi_in.ldf : epi_in.ldc;
     if (!ok_kind || !epi_in.nw || width % 4 || pitch % 4 || epi_in.C16 || b_pair_off ||
-        epi_in.splits_out)
+        epi_in.splits_out ||
+        (epi_in.conv_out && (pair || !epi_in.ring || !epi_in.pos || !epi_in.cw3 ||
+                             !epi_in.cw7 || !epi_in.cw15)))
       return reject("row norm: store / residual / GRU-pair epilogue, width % 4 == 0, weights");
   }
   if (epi_in.splits_out && (epi_in.kind != EPI_STORE || !epi_in.planes_out ||
