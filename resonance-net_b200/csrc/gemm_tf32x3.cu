@@ -52,9 +52,12 @@ constexpr int NUM_SPLIT_WARPS = 8;
 constexpr int NUM_THREADS = 32 * (FIRST_SPLIT_WARP + NUM_SPLIT_WARPS);
 constexpr int SMEM_BUDGET = 200 * 1024;  // pipeline stages (barriers etc. extra)
 constexpr int TILE_LD = 33;              // epilogue transpose tile: 32 x 33 floats per warp
-// per-warp epilogue slot: a 32 x 33 transpose tile, or a 32 x 32 fp32 tile in
-// the SWIZZLE_128B layout a TMA store reads (slots 1024-byte aligned)
-constexpr int EPI_TILE_FLOATS = 1280;
+// per-warp epilogue slot: a 32 x 33 transpose tile, or two 32 x 32 fp32 tiles
+// in the SWIZZLE_128B layout a TMA store reads (slots 1024-byte aligned), used
+// alternately so one tile's copy overlaps the next tile's TMEM load and
+// shared-memory writes (one buffer: the copies ran back to back, 3.3 of a
+// short-K decode GEMM's 8.5 us)
+constexpr int EPI_TILE_FLOATS = 2048;
 static_assert(EPI_TILE_FLOATS >= 32 * TILE_LD && (EPI_TILE_FLOATS * 4) % 1024 == 0, "epi slot");
 
 struct KParams {
@@ -101,8 +104,10 @@ struct Cfg {
   static constexpr int STAGE_BYTES = LO ? 2 * RAW_BYTES : RAW_BYTES;  // raw (= hi) + lo
   static constexpr int EPI_BYTES = NEPI * EPI_TILE_FLOATS * 4;
   // more epilogue warps take their tiles out of the stage budget
-  static constexpr int STAGES_FIT =
+  static constexpr int STAGES_BUDGET =
       (SMEM_BUDGET - (NEPI - NUM_EPI_WARPS) * EPI_TILE_FLOATS * 4) / STAGE_BYTES;
+  static constexpr int STAGES_LIMIT = (227 * 1024 - EPI_BYTES - 1024 - 256) / STAGE_BYTES;
+  static constexpr int STAGES_FIT = STAGES_BUDGET < STAGES_LIMIT ? STAGES_BUDGET : STAGES_LIMIT;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
@@ -112,6 +117,7 @@ struct Cfg {
   static_assert((ELEM == 4 && (BK == 16 || BK == 32)) || (ELEM == 2 && BK == 64), "BK");
   static_assert(CG == 1 || CG == 2, "CG");
   static_assert(STAGES >= 2, "stages");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory above the per-CTA opt-in limit");
   static_assert(B_ROWS % MN_ELEMS == 0, "B rows");
 };
 
@@ -314,6 +320,20 @@ __device__ __forceinline__ void bulk_wait_read_all() {
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+__device__ __forceinline__ void bulk_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
+// The warp's next 32 x 32 TMA staging buffer (alternating halves of its
+// slot): free once at most one bulk group, the other half's, is still
+// reading. The caller's sub-tile ends with bulk_wait_read_all().
+__device__ __forceinline__ float* tma_stage_next(float* slot, int& n, int lane) {
+  float* b = slot + (n & 1) * 1024;
+  ++n;
+  if (lane == 0) bulk_wait_read_1();
+  __syncwarp();
+  return b;
+}
 
 struct Top2State {
   float h0, h1;
@@ -339,17 +359,17 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
     constexpr int HALF_CHUNKS = BN / 64;
     // one 32 x 32 tile through TMA: swizzled into the warp's slot, stored
     // as plane z (the slot is free again once the copy has read it)
+    int nbuf = 0;
     auto tma_plane = [&](const float (&x)[32], int f0, int z) {
-      if (lane == 0) bulk_wait_read_all();
-      __syncwarp();
-      float4* t4 = reinterpret_cast<float4*>(tile);
+      float* buf = tma_stage_next(tile, nbuf, lane);
+      float4* t4 = reinterpret_cast<float4*>(buf);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         t4[lane * 8 + (j ^ (lane & 7))] =
             make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) tma_store_tile3(tmC, tile, f0, row0, z);
+      if (lane == 0) tma_store_tile3(tmC, buf, f0, row0, z);
     };
 #pragma unroll 1
     for (int c = cfirst; c < HALF_CHUNKS; c += cstep) {
@@ -415,16 +435,15 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
   if (p.stage_epi) {
     const int op = e.kind == EPI_STORE ? 0 : (e.kind == EPI_ACCUM ? 1 : 2);
     const bool tma = p.tma_out && ((op == 0 && e.C16 == nullptr) || op == 1);
+    int nbuf = 0;
 #pragma unroll 1
     for (int c = cfirst; c < BN / 32; c += cstep) {
       tmem_ld_32cols(tacc + c * 32, v);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] *= e.alpha;
       if (tma) {
-        // the previous chunk's bulk copy has finished reading the slot
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
-        float4* t4 = reinterpret_cast<float4*>(tile);
+        float* buf = tma_stage_next(tile, nbuf, lane);
+        float4* t4 = reinterpret_cast<float4*>(buf);
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           t4[lane * 8 + (j ^ (lane & 7))] =
@@ -433,9 +452,9 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
         __syncwarp();
         if (lane == 0) {
           if (p.tma_out == 2)  // split-K partial: plane = split index
-            tma_store_tile3(tmC, tile, nt * BN + c * 32, row0, (int)(c_off / p.split_stride));
+            tma_store_tile3(tmC, buf, nt * BN + c * 32, row0, (int)(c_off / p.split_stride));
           else
-            tma_store_tile(tmC, tile, nt * BN + c * 32, row0, op == 1);
+            tma_store_tile(tmC, buf, nt * BN + c * 32, row0, op == 1);
         }
       } else {
         tile_out(tile, v, e.C + c_off, e.ldc, e.R, e.ldr, row0, nt * BN + c * 32, p.M, p.N, op,
