@@ -42,7 +42,7 @@ __global__ void decode_gru_kernel(const float* __restrict__ P, const float* __re
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= M * D) return;
   const int m = i / D, d = i % D;
-  const float z = 1.0f / (1.0f + __expf(-(P[(size_t)m * 2 * D + d] + bz[d])));
+  const float z = sigmoid_fast(P[(size_t)m * 2 * D + d] + bz[d]);
   const float ht = P[(size_t)m * 2 * D + D + d] + bh[d];
   const float hn = (1.f - z) * h[i] + z * ht;
   h[i] = hn;
@@ -215,7 +215,7 @@ __global__ void silu_mul_rows_kernel(const float* __restrict__ gu, float* __rest
     const size_t r = i / F;
     const int f = (int)(i - r * F);
     const float g = gu[r * 2 * F + f];
-    h[i] = g / (1.0f + __expf(-g)) * gu[r * 2 * F + F + f];
+    h[i] = silu_fast(g) * gu[r * 2 * F + F + f];
   }
 }
 

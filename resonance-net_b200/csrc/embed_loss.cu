@@ -149,7 +149,7 @@ __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __rest
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
     const float x = g[i];
-    h[i] = x / (1.0f + __expf(-x)) * u[i];
+    h[i] = silu_fast(x) * u[i];
   }
 }
 
@@ -158,7 +158,7 @@ __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __rest
 //   dG = dH * u * silu'(g),  dU = dH * silu(g),
 // silu'(g) = s + g s (1 - s), s = sigmoid(g) (reference src/swiglu_ffn.cu:23-40).
 __device__ __forceinline__ void swiglu_grad1(float dh, float g, float u, float& dg, float& du) {
-  const float sig = 1.0f / (1.0f + __expf(-g));
+  const float sig = sigmoid_fast(g);
   const float dsilu = sig + g * sig * (1.0f - sig);
   dg = dh * u * dsilu;
   du = dh * (g * sig);

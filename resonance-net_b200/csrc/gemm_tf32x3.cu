@@ -141,7 +141,6 @@ __device__ __forceinline__ void unit_range(const KParams& p, int unit, int& mt, 
   }
 }
 
-__device__ __forceinline__ float silu_fast(float g) { return g / (1.0f + __expf(-g)); }
 
 // ------------------------------------------------------------------ epilogue
 // The accumulator arrives thread-per-row (TMEM lane = tile row, 32 columns
@@ -1068,11 +1067,11 @@ __global__ void __launch_bounds__(256)
     const size_t o = r * e.ldf + c;
     if (e.kind == EPI_PAIR_SILU) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) e.H[o + j] = av[j] / (1.0f + __expf(-av[j])) * bv[j];
+      for (int j = 0; j < 4; ++j) e.H[o + j] = silu_fast(av[j]) * bv[j];
     } else {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float z = 1.0f / (1.0f + __expf(-(av[j] + e.b0[c + j])));
+        const float z = sigmoid_fast(av[j] + e.b0[c + j]);
         const float ht = bv[j] + e.b1[c + j];
         const float hn = (1.f - z) * e.state[o + j] + z * ht;
         e.state[o + j] = hn;
@@ -1231,7 +1230,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
     const size_t o = r * e.ldf + c;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float z = 1.0f / (1.0f + __expf(-(av[j] + e.b0[c + j])));
+      const float z = sigmoid_fast(av[j] + e.b0[c + j]);
       const float ht = bv[j] + e.b1[c + j];
       const float hn = (1.f - z) * e.state[o + j] + z * ht;
       e.state[o + j] = hn;

@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(W * 32)
       const bool live = act && i < n;
       // steps past T (and lanes past D) are identity steps (z = 0: h unchanged);
       // z = 1 / (1 + exp(-(pz + bz))) with the fast divide (a few ulp)
-      const float z = live ? __fdividef(1.0f, 1.0f + __expf(-(sZ[row * CW + lane] + bzd))) : 0.f;
+      const float z = live ? sigmoid_fast(sZ[row * CW + lane] + bzd) : 0.f;
       const float ht = live ? sT[row * CW + lane] + bhd : 0.f;
       sZ[row * CW + lane] = z;
       sT[row * CW + lane] = ht;
