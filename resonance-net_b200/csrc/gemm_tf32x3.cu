@@ -83,6 +83,9 @@ struct KParams {
   // SwiGLU forward: 2 or 3 when G, U (and H) are planes of one 3-D tensor
   // map (tmC: [planes][M][ldf]) that TMA stores; 0 = warp stores
   int swiglu_planes;
+  // SwiGLU forward with a bf16 H copy: 1 when H16 leaves through TMA (tmD,
+  // [M][ldf] bf16, 32 x 32 boxes) instead of the warp's transpose tile
+  int h16_tma;
   Epilogue epi;
   unsigned* err;
 };
@@ -348,7 +351,8 @@ template <int BN, bool PIPE_LD>
 __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc, int row0,
                                                  int nt, bool last_sub, Top2State& st,
                                                  float* tile, size_t c_off, int cfirst = 0,
-                                                 int cstep = 1, const void* tmC = nullptr) {
+                                                 int cstep = 1, const void* tmC = nullptr,
+                                                 const void* tmD = nullptr) {
   const Epilogue& e = p.epi;
   const int lane = threadIdx.x & 31;
   const int row = row0 + lane;
@@ -387,6 +391,23 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
       for (int i = 0; i < 32; ++i) v[i] = silu_fast(g[i]) * v[i];
       if (p.swiglu_planes == 3) {
         tma_plane(v, f0, 2);
+      } else if (p.h16_tma) {
+        // bf16 H: 32 rows of 64 B (no swizzle) in the next staging buffer
+        float* buf = tma_stage_next(tile, nbuf, lane);
+        uint4* t = reinterpret_cast<uint4*>(buf);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * j + 2 * i], v[8 * j + 2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&b2);
+          }
+          t[lane * 4 + j] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tma_store_tile(tmD, buf, f0, row0, false);
       } else {
         if (p.swiglu_planes) {
           if (lane == 0) bulk_wait_read_all();
@@ -592,7 +613,8 @@ template <int BN, int BK, int CG, int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB,
-                       const __grid_constant__ CUtensorMap tmC, const KParams p) {
+                       const __grid_constant__ CUtensorMap tmC,
+                       const __grid_constant__ CUtensorMap tmD, const KParams p) {
   rnet_dev::pdl_trigger();
   constexpr bool BF = MODE == 1;
   // MODE 2: four of the idle split warps (6-9) become a second epilogue set
@@ -877,7 +899,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             p.split_stride ? (size_t)p.split_stride * (size_t)(kb0 / p.kb_per_split) : 0;
         epilogue_subtile<BN, MODE != 2>(p, tacc, row0, nt, nt == nt1 - 1, st,
                              epi_tiles + eslot * EPI_TILE_FLOATS, c_off, eset,
-                             NEPI / NUM_EPI_WARPS, &tmC);
+                             NEPI / NUM_EPI_WARPS, &tmC, &tmD);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -975,7 +997,7 @@ int num_sms() {
 
 template <int BN, int BK, int CG, int MODE>
 static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
-                          const CUtensorMap& tc, const KParams& kp) {
+                          const CUtensorMap& tc, const CUtensorMap& td, const KParams& kp) {
   using C = Cfg<BN, BK, CG, MODE == 2 ? 2 : 4, MODE != 2,
                 MODE == 2 ? 2 * NUM_EPI_WARPS : NUM_EPI_WARPS>;
   static bool configured = false;
@@ -1027,7 +1049,7 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
   const int groups = kp.num_units < max_groups ? kp.num_units : max_groups;
   cfg.gridDim = dim3(groups * CG);
   cudaError_t e =
-      cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, BK, CG, MODE>, ta, tb, tc, kp);
+      cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, BK, CG, MODE>, ta, tb, tc, td, kp);
   if (e != cudaSuccess) {
     g_reason = "kernel launch";
     return e;
@@ -1429,7 +1451,8 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
     return !B.mn_major ? make_map(m, base, (uint64_t)K, b_rows, B.ld, BK, b_box, kswz, st16)
                        : make_map(m, base, b_rows, (uint64_t)K, B.ld, mn_box, BK, mswz, st16);
   };
-  CUtensorMap ta, tb, tc;
+  CUtensorMap ta, tb, tc, td;
+  std::memset(&td, 0, sizeof(td));
   if (!map_a(&ta, A.p)) return reject("tensor map of A rejected");
   if (!map_b(&tb, B.p)) return reject("tensor map of B rejected");
   // plain stores / accumulations leave through TMA when C allows a tensor
@@ -1480,6 +1503,12 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
         kp.swiglu_planes = planes;
     }
   }
+  kp.h16_tma = 0;
+  if (kp.swiglu_planes == 2 && epi.H16 && epi.H == nullptr && epi.ldf % 8 == 0 &&
+      (reinterpret_cast<uintptr_t>(epi.H16) & 15) == 0 &&
+      make_map(&td, reinterpret_cast<const float*>(epi.H16), (uint64_t)N, (uint64_t)M, epi.ldf,
+               32, 32, CU_TENSOR_MAP_SWIZZLE_NONE, true))
+    kp.h16_tma = 1;
   // fp32 tiles: the staged path only pays with TMA stores (split-K partial
   // planes and residual epilogues keep thread-per-row stores, which leave
   // shared memory to the split warps)
@@ -1488,25 +1517,25 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   cudaError_t e;
   if (st16) {
     if (CG == 2)
-      e = BN == 128 ? launch<128, 64, 2, 2>(stream, ta, tb, tc, kp)
-                    : launch<256, 64, 2, 2>(stream, ta, tb, tc, kp);
+      e = BN == 128 ? launch<128, 64, 2, 2>(stream, ta, tb, tc, td, kp)
+                    : launch<256, 64, 2, 2>(stream, ta, tb, tc, td, kp);
     else
-      e = BN == 128 ? launch<128, 64, 1, 2>(stream, ta, tb, tc, kp)
-                    : launch<256, 64, 1, 2>(stream, ta, tb, tc, kp);
+      e = BN == 128 ? launch<128, 64, 1, 2>(stream, ta, tb, tc, td, kp)
+                    : launch<256, 64, 1, 2>(stream, ta, tb, tc, td, kp);
   } else if (bf) {
     if (CG == 2)
-      e = BN == 128 ? launch<128, 16, 2, 1>(stream, ta, tb, tc, kp)
-                    : launch<256, 16, 2, 1>(stream, ta, tb, tc, kp);
+      e = BN == 128 ? launch<128, 16, 2, 1>(stream, ta, tb, tc, td, kp)
+                    : launch<256, 16, 2, 1>(stream, ta, tb, tc, td, kp);
     else
-      e = BN == 128 ? launch<128, 16, 1, 1>(stream, ta, tb, tc, kp)
-                    : launch<256, 16, 1, 1>(stream, ta, tb, tc, kp);
+      e = BN == 128 ? launch<128, 16, 1, 1>(stream, ta, tb, tc, td, kp)
+                    : launch<256, 16, 1, 1>(stream, ta, tb, tc, td, kp);
   } else {
     if (CG == 2)
-      e = BN == 128 ? launch<128, 16, 2, 0>(stream, ta, tb, tc, kp)
-                    : launch<256, 16, 2, 0>(stream, ta, tb, tc, kp);
+      e = BN == 128 ? launch<128, 16, 2, 0>(stream, ta, tb, tc, td, kp)
+                    : launch<256, 16, 2, 0>(stream, ta, tb, tc, td, kp);
     else
-      e = BN == 128 ? launch<128, 16, 1, 0>(stream, ta, tb, tc, kp)
-                    : launch<256, 16, 1, 0>(stream, ta, tb, tc, kp);
+      e = BN == 128 ? launch<128, 16, 1, 0>(stream, ta, tb, tc, td, kp)
+                    : launch<256, 16, 1, 0>(stream, ta, tb, tc, td, kp);
   }
   if (e != cudaSuccess) return e;
   if (pair) {
