@@ -83,9 +83,9 @@ struct KParams {
   // SwiGLU forward: 2 or 3 when G, U (and H) are planes of one 3-D tensor
   // map (tmC: [planes][M][ldf]) that TMA stores; 0 = warp stores
   int swiglu_planes;
-  // SwiGLU forward with a bf16 H copy: 1 when H16 leaves through TMA (tmD,
-  // [M][ldf] bf16, 32 x 32 boxes) instead of the warp's transpose tile
-  int h16_tma;
+  // 1 when the bf16 copy (SwiGLU forward's H16, a store's C16) leaves through
+  // TMA (tmD: bf16 rows, 32 x 32 boxes) instead of the warp's transpose tile
+  int copy16_tma;
   Epilogue epi;
   unsigned* err;
 };
@@ -337,6 +337,24 @@ __device__ __forceinline__ float* tma_stage_next(float* slot, int& n, int lane) 
   return b;
 }
 
+// A 32 x 32 bf16 tile (lane = row, 64 B per row, no swizzle) from fp32
+// values, rounded to nearest even, ready for a TMA store through tmD.
+__device__ __forceinline__ void stage_bf16_tile(float* buf, const float (&v)[32], int lane) {
+  uint4* t = reinterpret_cast<uint4*>(buf);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * j + 2 * i], v[8 * j + 2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&b2);
+    }
+    t[lane * 4 + j] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+}
+
 struct Top2State {
   float h0, h1;
   int i0, i1;
@@ -391,22 +409,10 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
       for (int i = 0; i < 32; ++i) v[i] = silu_fast(g[i]) * v[i];
       if (p.swiglu_planes == 3) {
         tma_plane(v, f0, 2);
-      } else if (p.h16_tma) {
-        // bf16 H: 32 rows of 64 B (no swizzle) in the next staging buffer
+      } else if (p.copy16_tma) {
+        // bf16 H in the next staging buffer
         float* buf = tma_stage_next(tile, nbuf, lane);
-        uint4* t = reinterpret_cast<uint4*>(buf);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t w[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * j + 2 * i], v[8 * j + 2 * i + 1]);
-            w[i] = *reinterpret_cast<const uint32_t*>(&b2);
-          }
-          t[lane * 4 + j] = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
+        stage_bf16_tile(buf, v, lane);
         if (lane == 0) tma_store_tile(tmD, buf, f0, row0, false);
       } else {
         if (p.swiglu_planes) {
@@ -454,8 +460,8 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
   }
   if (p.stage_epi) {
     const int op = e.kind == EPI_STORE ? 0 : (e.kind == EPI_ACCUM ? 1 : 2);
-    const bool tma = p.tma_out && ((op == 0 && e.C16 == nullptr) || op == 1);
-    if (PIPE_LD && tma) {
+    const bool tma = p.tma_out && ((op == 0 && (e.C16 == nullptr || p.copy16_tma)) || op == 1);
+    if (PIPE_LD && tma && e.C16 == nullptr) {
       // the next chunk's TMEM load is in flight while this chunk is staged
       // and its bulk copy issued (fp32 tiles: decode step 0.531 -> 0.520 ms;
       // bf16 storage keeps the plain loop, which spills less: 7.39 -> 7.23 ms)
@@ -517,6 +523,11 @@ __device__ __forceinline__ void epilogue_subtile(const KParams& p, uint32_t tacc
             tma_store_tile3(tmC, buf, nt * BN + c * 32, row0, (int)(c_off / p.split_stride));
           else
             tma_store_tile(tmC, buf, nt * BN + c * 32, row0, op == 1);
+        }
+        if (e.C16 != nullptr && op == 0) {  // the bf16 copy through tmD
+          float* b16 = tma_stage_next(tile, nbuf, lane);
+          stage_bf16_tile(b16, v, lane);
+          if (lane == 0) tma_store_tile(tmD, b16, nt * BN + c * 32, row0, false);
         }
       } else {
         tile_out(tile, v, e.C + c_off, e.ldc, e.R, e.ldr, row0, nt * BN + c * 32, p.M, p.N, op,
@@ -1460,8 +1471,16 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
   // tile through shared memory as coalesced rows
   std::memset(&tc, 0, sizeof(tc));
   kp.tma_out = 0;
+  kp.copy16_tma = 0;
+  // a store's bf16 copy leaves through TMA too when its map can be made
+  if (kp.split_stride == 0 && g_tma_out && epi.kind == EPI_STORE && epi.C16 &&
+      epi.ldc % 8 == 0 && (reinterpret_cast<uintptr_t>(epi.C16) & 15) == 0 &&
+      make_map(&td, reinterpret_cast<const float*>(epi.C16), (uint64_t)N, (uint64_t)M, epi.ldc,
+               32, 32, CU_TENSOR_MAP_SWIZZLE_NONE, true))
+    kp.copy16_tma = 1;
   if (kp.split_stride == 0 && g_tma_out &&
-      ((epi.kind == EPI_STORE && epi.C16 == nullptr) || epi.kind == EPI_ACCUM) &&
+      ((epi.kind == EPI_STORE && (epi.C16 == nullptr || kp.copy16_tma)) ||
+       epi.kind == EPI_ACCUM) &&
       (reinterpret_cast<uintptr_t>(epi.C) & 15) == 0 &&
       epi.ldc % 4 == 0 && epi.ldc >= N &&
       make_map(&tc, epi.C, (uint64_t)N, (uint64_t)M, epi.ldc, 32, 32,
@@ -1503,12 +1522,11 @@ cudaError_t gemm_tf32x3(cudaStream_t stream, int M, int N, int K, const Operand&
         kp.swiglu_planes = planes;
     }
   }
-  kp.h16_tma = 0;
   if (kp.swiglu_planes == 2 && epi.H16 && epi.H == nullptr && epi.ldf % 8 == 0 &&
       (reinterpret_cast<uintptr_t>(epi.H16) & 15) == 0 &&
       make_map(&td, reinterpret_cast<const float*>(epi.H16), (uint64_t)N, (uint64_t)M, epi.ldf,
                32, 32, CU_TENSOR_MAP_SWIZZLE_NONE, true))
-    kp.h16_tma = 1;
+    kp.copy16_tma = 1;
   // fp32 tiles: the staged path only pays with TMA stores (split-K partial
   // planes and residual epilogues keep thread-per-row stores, which leave
   // shared memory to the split warps)
