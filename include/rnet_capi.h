@@ -294,7 +294,9 @@ typedef struct rnet_decoder rnet_decoder;
 int rnet_decoder_create(rnet_model* m, int n_streams, rnet_decoder** out);
 int rnet_decoder_destroy(rnet_decoder* d);
 /* d_tokens [n_streams, seq_len] (device). Runs the chunked-scan forward and
- * keeps the state; the last-position logits / argmax become available. */
+ * keeps the state; the last-position logits / argmax become available. Also
+ * folds the slot keys / values with proj_q / proj_out for the decode steps,
+ * from the weights of this moment: prefill again after changing weights. */
 int rnet_decoder_prefill(rnet_decoder* d, const int* d_tokens, int seq_len);
 /* One token per stream: d_tokens [n_streams] (device) or NULL to feed back
  * the previous argmax. */
