@@ -34,21 +34,6 @@ __global__ void decode_conv_kernel(const float* __restrict__ n, float* __restric
       rnet_dev::conv_step4(x, ring + (size_t)m * RING * D, *pos_ptr, w3, w7, w15, d, D);
 }
 
-// h = (1 - z) h + z h~, z = sigmoid(pz + bz), h~ = ph + bh; x += h.
-__global__ void decode_gru_kernel(const float* __restrict__ P, const float* __restrict__ bz,
-                                  const float* __restrict__ bh, float* __restrict__ h,
-                                  float* __restrict__ x, int M, int D) {
-  rnet_dev::pdl_trigger();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= M * D) return;
-  const int m = i / D, d = i % D;
-  const float z = sigmoid_fast(P[(size_t)m * 2 * D + d] + bz[d]);
-  const float ht = P[(size_t)m * 2 * D + D + d] + bh[d];
-  const float hn = (1.f - z) * h[i] + z * ht;
-  h[i] = hn;
-  x[i] += hn;
-}
-
 // After a prefill of T steps: h_state[m] = h[m, T-1]; ring[t % 14] = n1[m, t]
 // for t in [T-14, T-1] (zero for t < 0).
 __global__ void extract_state_kernel(const float* __restrict__ n1, const float* __restrict__ h,
@@ -205,20 +190,6 @@ __global__ void advance_pos_kernel(int* pos_ptr) {
   if (threadIdx.x == 0) atomicAdd(pos_ptr, 1);
 }
 
-// h[r, f] = silu(gu[r, f]) * gu[r, F + f]  (gate | up rows of width 2F)
-__global__ void silu_mul_rows_kernel(const float* __restrict__ gu, float* __restrict__ h, int M,
-                                     int F) {
-  rnet_dev::pdl_trigger();
-  const size_t n = (size_t)M * F;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const size_t r = i / F;
-    const int f = (int)(i - r * F);
-    const float g = gu[r * 2 * F + f];
-    h[i] = silu_fast(g) * gu[r * 2 * F + F + f];
-  }
-}
-
 // Top-2 of each score row by the reference's sequential rule (walk the slots
 // in order; a score strictly above the smaller held score replaces the first
 // such minimum), then softmax over the pair (src/slot_memory.cu:40-51).
@@ -297,43 +268,6 @@ __device__ __forceinline__ void top2_scan_warp(Load ld, int S, int lane, float& 
       h1 = __shfl_sync(0xffffffffu, h1, src);
       i0 = __shfl_sync(0xffffffffu, i0, src);
       i1 = __shfl_sync(0xffffffffu, i1, src);
-    }
-  }
-}
-
-// VT / r (optional): the warp also gathers r[row] = w0 VT[i0] + w1 VT[i1]
-// (the slot_gather of the selected pair, same arithmetic), saving a launch.
-__global__ void topk2_rows_kernel(const float* __restrict__ scores, int* __restrict__ idx,
-                                  float* __restrict__ w, int M, int S,
-                                  const float* __restrict__ VT, float* __restrict__ r, int D) {
-  rnet_dev::pdl_trigger();
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= M) return;
-  const float* sr = scores + (size_t)row * S;
-  float h0, h1;
-  int i0, i1;
-  top2_scan_warp([&](int j) { return sr[j]; }, S, lane, h0, h1, i0, i1);
-  const float mx = fmaxf(h0, h1);
-  const float e0 = __expf(h0 - mx), e1 = __expf(h1 - mx);
-  const float sum = e0 + e1;
-  const float w0 = e0 / sum, w1 = e1 / sum;
-  if (lane == 0) {
-    idx[2 * (size_t)row] = i0;
-    idx[2 * (size_t)row + 1] = i1;
-    w[2 * (size_t)row] = w0;
-    w[2 * (size_t)row + 1] = w1;
-  }
-  if (r) {
-    const int id[2] = {i0, i1};
-    const float ww[2] = {w0, w1};
-    for (int c = lane * 4; c < D; c += 128) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int j = 0; j < 2; ++j) {
-        const float4 v = *reinterpret_cast<const float4*>(VT + (size_t)id[j] * D + c);
-        acc.x += ww[j] * v.x; acc.y += ww[j] * v.y; acc.z += ww[j] * v.z; acc.w += ww[j] * v.w;
-      }
-      *reinterpret_cast<float4*>(r + (size_t)row * D + c) = acc;
     }
   }
 }
@@ -470,23 +404,6 @@ __global__ void __launch_bounds__(256) fold_kernel(const float* __restrict__ A,
 
 }  // namespace
 
-cudaError_t silu_mul_rows(const float* gu, float* h, int M, int F, cudaStream_t s) {
-  if (M <= 0 || F <= 0) return cudaSuccess;
-  const size_t n = (size_t)M * F;
-  size_t grid = (n + 255) / 256;
-  if (grid > 148 * 16) grid = 148 * 16;
-  silu_mul_rows_kernel<<<(unsigned)grid, 256, 0, s>>>(gu, h, M, F);
-  return launched();
-}
-
-cudaError_t topk2_rows(const float* scores, int* idx, float* w, int M, int S, cudaStream_t s,
-                       const float* VT, float* r, int D) {
-  if (M <= 0) return cudaSuccess;
-  if (r && (D % 4 || !VT)) return cudaErrorInvalidValue;
-  topk2_rows_kernel<<<(M + 7) / 8, 256, 0, s>>>(scores, idx, w, M, S, VT, r, D);
-  return launched();
-}
-
 cudaError_t topk2_gather_residual_norm(const float* planes, int n_planes, int* idx, float* w,
                                        int M, int S, const float* VP, float* x, int D,
                                        const float* nw, float* ny, float eps, cudaStream_t s) {
@@ -519,12 +436,6 @@ cudaError_t decode_conv(const float* n, float* ring, const int* pos, const float
                         cudaStream_t s) {
   if (D % 4) return cudaErrorInvalidValue;
   decode_conv_kernel<<<(M * D / 4 + 255) / 256, 256, 0, s>>>(n, ring, pos, w3, w7, w15, S, M, D);
-  return launched();
-}
-
-cudaError_t decode_gru(const float* P, const float* bz, const float* bh, float* h, float* x,
-                       int M, int D, cudaStream_t s) {
-  decode_gru_kernel<<<(M * D + 255) / 256, 256, 0, s>>>(P, bz, bh, h, x, M, D);
   return launched();
 }
 

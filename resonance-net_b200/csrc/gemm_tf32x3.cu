@@ -1075,8 +1075,8 @@ static cudaError_t launch(cudaStream_t stream, const CUtensorMap& ta, const CUte
 // results do not depend on scheduling) and applies the epilogue.
 // Paired-column rules over S partial planes [M, 2h] (S = 1: a stored C):
 // a = sum of column f, b = sum of column h + f, summed in split order.
-// Same formulas as the decode step's separate kernels (silu_mul_rows,
-// decode_gru), so the results do not depend on the fusion.
+// Same formulas (sigmoid_fast / silu_fast) as the training forward's SwiGLU
+// epilogue and MinGRU scan.
 __global__ void __launch_bounds__(256)
     splitk_pair_kernel(const float* __restrict__ ws, int S, int M, int h, Epilogue e) {
   rnet_dev::pdl_trigger();

@@ -121,13 +121,6 @@ cudaError_t swiglu_bwd_pointwise(float* dgu, int ld, const float* G, const float
                                  cudaStream_t s, __nv_bfloat16* dgu16 = nullptr);
 
 // ---- recurrent decode (decode.cu) -----------------------------------------
-// h[r, f] = silu(gu[r, f]) * gu[r, F + f] over rows of width 2F.
-cudaError_t silu_mul_rows(const float* gu, float* h, int M, int F, cudaStream_t s);
-// Top-2 slots of each score row ([M, S]) by the reference's sequential rule,
-// softmax weights over the pair; same results as the GEMM's top-2 epilogue.
-// VT / r (optional): also gather r = sum_j w_j VT[idx_j] (as slot_gather).
-cudaError_t topk2_rows(const float* scores, int* idx, float* w, int M, int S, cudaStream_t s,
-                       const float* VT = nullptr, float* r = nullptr, int D = 0);
 // The decode step's slot sublayer after the score GEMM, in one launch:
 // top-2 over the scores (the sum of n_planes split-K partial planes [M, S],
 // M * S floats apart, in plane order; 1 = plain scores), then
@@ -146,8 +139,6 @@ cudaError_t fold_rows(const float* A, const float* B, size_t bd, size_t bj, floa
 cudaError_t decode_conv(const float* n, float* ring, const int* pos, const float* w3,
                         const float* w7, const float* w15, float* S, int M, int D,
                         cudaStream_t s);
-cudaError_t decode_gru(const float* P, const float* bz, const float* bh, float* h, float* x,
-                       int M, int D, cudaStream_t s);
 cudaError_t decode_extract_state(const float* n1, const float* h, float* ring, float* hs, int M,
                                  int T, int D, cudaStream_t s);
 cudaError_t last_rows(const float* x, float* out, int M, int T, int D, cudaStream_t s);
