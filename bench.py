@@ -358,9 +358,9 @@ def run_ours(args, rank, world, local):
             if v["ms"] > 0 and v["bytes"] > 0 and k != "gemm":
                 kernels[k]["GBps"] = round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1)
                 kernels[k]["hbm_frac"] = round(kernels[k]["GBps"] / peaks["hbm"], 3)
-            # the same time against the survey's algorithmic bytes per [N, D]
-            # element (the kernels' own extra outputs, e.g. the scan's saved
-            # e and second residual copy, not counted as work)
+            # the same time against the algorithmic bytes per [N, D] element (reads
+            # of the inputs and writes of the outputs the math needs; the kernels' own
+            # extra outputs, e.g. the scan's saved e and second residual copy, excluded)
             if k in ALG_BYTES_PER_ELEM and v["ms"] > 0:
                 alg = ALG_BYTES_PER_ELEM[k] * B * T * C["d_model"] * v["launches"]
                 kernels[k]["alg_GBps"] = round(alg / (v["ms"] * 1e-3) / 1e9, 1)
