@@ -69,6 +69,9 @@ Engine::Engine(const rnet_model_config& c) : cfg_(c) {}
 Engine::~Engine() {
   if (device_ >= 0) cudaSetDevice(device_);
   save_wait();
+  if (train_exec_) cudaGraphExecDestroy(train_exec_);
+  cudaFree(g_in_);
+  cudaFree(g_tgt_);
   cudaFree(snap_);
   if (snap_host_) cudaFreeHost(snap_host_);
   if (snap_ready_) cudaEventDestroy(snap_ready_);
@@ -113,6 +116,7 @@ int Engine::init(int device, bool reference_init) {
   CK(cudaSetDevice(device));
   CK(cudaStreamCreate(&stream_));  // blocking w.r.t. the legacy stream, like the reference
   CK(cudaStreamCreateWithFlags(&wstream_, cudaStreamNonBlocking));
+  if (const char* v = getenv("RNET_TRAIN_GRAPH")) train_graphs_ = v[0] != '0';
   CK(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
   CK(cudaEventCreateWithFlags(&ev_join_, cudaEventDisableTiming));
 
@@ -716,6 +720,99 @@ int Engine::step(float lr, float clip) {
 }
 
 int Engine::train_step(const int* d_in, const int* d_tgt, int B, int T, float lr, float clip,
+                       float* d_loss_sum) {
+  const int N = B * T;
+  if (!train_graphs_ || dist || prof_on_ || (warmup_ > 0 && step_count_ < warmup_) || N <= 0 ||
+      N > 64 * (cfg_.seq_len > 0 ? cfg_.seq_len : 256))
+    return train_step_eager(d_in, d_tgt, B, T, lr, clip, d_loss_sum);
+  int rc = ensure_capacity(N, true);  // may reallocate: never inside a capture
+  if (rc) return rc;
+  if (N > g_cap_) {
+    if (train_exec_) cudaGraphExecDestroy(train_exec_);
+    train_exec_ = nullptr;
+    warm_valid_ = false;
+    CK(cudaStreamSynchronize(stream_));
+    cudaFree(g_in_);
+    cudaFree(g_tgt_);
+    g_in_ = g_tgt_ = nullptr;
+    CK(cudaMalloc(&g_in_, N * sizeof(int)));
+    CK(cudaMalloc(&g_tgt_, N * sizeof(int)));
+    g_cap_ = N;
+  }
+  TrainKey key;
+  key.B = B;
+  key.T = T;
+  key.lr = lr;
+  key.clip = clip;
+  key.arena = arena_;
+  key.params16 = params16_;
+  key.velocity = velocity_;
+  key.momentum = momentum_;
+  key.weight_decay = weight_decay_;
+  key.precision = precision;
+  key.recompute = recompute_;
+  key.conv_quirk = conv_quirk;
+  CK(cudaMemcpyAsync(g_in_, d_in, N * sizeof(int), cudaMemcpyDeviceToDevice, stream_));
+  CK(cudaMemcpyAsync(g_tgt_, d_tgt, N * sizeof(int), cudaMemcpyDeviceToDevice, stream_));
+  if (!(train_exec_ && key == train_key_)) {
+    if (!(warm_valid_ && key == warm_key_)) {
+      // first step with this key: eager (kernel attributes, tensor maps and
+      // caches are set up outside any capture)
+      warm_key_ = key;
+      warm_valid_ = true;
+      rc = train_step_eager(g_in_, g_tgt_, B, T, lr, clip, loss_dev_);
+      if (rc) return rc;
+      if (d_loss_sum)
+        CK(cudaMemcpyAsync(d_loss_sum, loss_dev_, sizeof(float), cudaMemcpyDeviceToDevice,
+                           stream_));
+      return RNET_OK;
+    }
+    if (train_exec_) cudaGraphExecDestroy(train_exec_);
+    train_exec_ = nullptr;
+    const long long count0 = step_count_;
+    CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    rc = train_step_eager(g_in_, g_tgt_, B, T, lr, clip, loss_dev_);
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(stream_, &g);
+    cudaGraphExec_t exec = nullptr;
+    size_t nodes = 0;
+    bool captured = rc == RNET_OK && ce == cudaSuccess && g &&
+                    cudaGraphGetNodes(g, nullptr, &nodes) == cudaSuccess;
+    size_t kernels = 0;  // launches counted: kernel nodes only (not the memset)
+    if (captured && nodes) {
+      std::vector<cudaGraphNode_t> list(nodes);
+      captured = cudaGraphGetNodes(g, list.data(), &nodes) == cudaSuccess;
+      for (size_t i = 0; captured && i < nodes; ++i) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(list[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel)
+          ++kernels;
+      }
+    }
+    captured = captured && cudaGraphInstantiate(&exec, g, 0) == cudaSuccess;
+    if (g) cudaGraphDestroy(g);
+    if (!captured) {
+      // run eagerly from now on (the capture ran nothing)
+      cudaGetLastError();
+      train_graphs_ = false;
+      step_count_ = count0;
+      return train_step_eager(d_in, d_tgt, B, T, lr, clip, d_loss_sum);
+    }
+    train_exec_ = exec;
+    train_nodes_ = kernels;
+    train_key_ = key;
+    // the capture advanced the host-side step count; the launch below is
+    // that step
+  } else {
+    ++step_count_;
+  }
+  CK(cudaGraphLaunch(train_exec_, stream_));
+  rnet_status::count_launch((unsigned)train_nodes_);
+  if (d_loss_sum)
+    CK(cudaMemcpyAsync(d_loss_sum, loss_dev_, sizeof(float), cudaMemcpyDeviceToDevice, stream_));
+  return RNET_OK;
+}
+
+int Engine::train_step_eager(const int* d_in, const int* d_tgt, int B, int T, float lr, float clip,
                        float* d_loss_sum) {
   const int N = B * T, V = cfg_.vocab_size;
   if (N > 64 * (cfg_.seq_len > 0 ? cfg_.seq_len : 256))

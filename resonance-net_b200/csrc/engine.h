@@ -128,8 +128,16 @@ class Engine {
   int step(float lr, float clip);
   // zero_grad + forward + CE (dlogits scaled by 1/N) + backward + step.
   // d_loss_sum: device float receiving sum of token losses (may be null).
+  // Single-GPU steps run from a captured CUDA graph once the same (B, T, lr,
+  // clip, configuration) repeats: the inputs are copied into engine buffers
+  // first and the loss sum out afterwards, so the graph holds no caller
+  // pointer. Data-parallel, profiled and warmup steps run eagerly, and so
+  // does everything with RNET_TRAIN_GRAPH=0.
   int train_step(const int* d_in, const int* d_tgt, int B, int T, float lr, float clip,
                  float* d_loss_sum);
+  // the step's launches in order (what the graph captures)
+  int train_step_eager(const int* d_in, const int* d_tgt, int B, int T, float lr, float clip,
+                       float* d_loss_sum);
 
   // Optimizer extensions (off by default: the reference's plain SGD with
   // clipping, src/resonance_net.cpp:551-663): momentum, weight decay added
@@ -233,6 +241,31 @@ class Engine {
   float momentum_ = 0.0f, weight_decay_ = 0.0f;
   int warmup_ = 0;
   long long step_count_ = 0;
+  // captured train step (see train_step)
+  struct TrainKey {
+    int B = 0, T = 0;
+    float lr = 0.f, clip = 0.f;
+    const void* arena = nullptr;
+    const void* params16 = nullptr;
+    const void* velocity = nullptr;
+    float momentum = 0.f, weight_decay = 0.f;
+    int precision = 0;
+    bool recompute = false, conv_quirk = false;
+    bool operator==(const TrainKey& o) const {
+      return B == o.B && T == o.T && lr == o.lr && clip == o.clip && arena == o.arena &&
+             params16 == o.params16 && velocity == o.velocity && momentum == o.momentum &&
+             weight_decay == o.weight_decay && precision == o.precision &&
+             recompute == o.recompute && conv_quirk == o.conv_quirk;
+    }
+  };
+  bool train_graphs_ = true;
+  cudaGraphExec_t train_exec_ = nullptr;
+  size_t train_nodes_ = 0;
+  TrainKey train_key_, warm_key_;
+  bool warm_valid_ = false;
+  int* g_in_ = nullptr;  // the graph's token inputs / targets
+  int* g_tgt_ = nullptr;
+  int g_cap_ = 0;
   float* velocity_ = nullptr;
   // asynchronous save
   float* snap_ = nullptr;   // device snapshot of params_
