@@ -246,7 +246,12 @@ int rnet_model_zero_grad(rnet_model* m);
 int rnet_model_step(rnet_model* m, float lr, float grad_clip);
 /* zero_grad + forward + cross-entropy (dlogits scaled by 1/(batch*seq_len))
  * + backward + (all-reduce) + clipped SGD, all on the model stream.
- * d_loss_sum (device, may be NULL) receives the summed token loss. */
+ * d_loss_sum (device, may be NULL) receives the summed token loss. Without a
+ * data-parallel group, repeated calls with the same batch, seq_len, lr,
+ * grad_clip and model configuration replay a CUDA graph of the step captured
+ * on the second such call (RNET_TRAIN_GRAPH=0 in the environment at model
+ * creation keeps every step eager); the tokens are copied first, so the
+ * buffers may differ from call to call. */
 int rnet_model_train_step(rnet_model* m, const int* d_inputs, const int* d_targets, int batch,
                           int seq_len, float lr, float grad_clip, float* d_loss_sum);
 /* Same with host token buffers; copies in, steps, copies the loss sum out and
